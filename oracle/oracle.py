@@ -1,0 +1,222 @@
+"""CPU oracle for the G2V path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py`` import this module, and
+only as the checker (or as the timed CPU baseline).  The product library never calls it.
+
+It wraps ``g2v_oracle.c`` (built into ``oracle/_build/libg2v_oracle.so`` by :func:`build`) with numpy
+arrays.  The C file lists, per function, which part of the reference it restates:
+``src/cuda_gaussian_voxelizer.cu`` for the grid shape, the boxes and the CSR maps, and
+``test/test_reference.py:57-79`` (float64 brute force) for the values and, by analytic differentiation,
+the gradients.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+BUILD_DIR = os.path.join(HERE, "_build")
+LIB_PATH = os.path.join(BUILD_DIR, "libg2v_oracle.so")
+SRC = os.path.join(HERE, "g2v_oracle.c")
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile the oracle with gcc (no fp contraction, OpenMP) into oracle/_build/."""
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    if not force and os.path.exists(LIB_PATH) and os.path.getmtime(LIB_PATH) >= os.path.getmtime(SRC):
+        return LIB_PATH
+    tmp = LIB_PATH + f".tmp{os.getpid()}"
+    subprocess.check_call(["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off",
+                           "-fno-fast-math", SRC, "-o", tmp, "-lm"])
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(SRC):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.c_void_p
+        i64, i32 = ctypes.c_int64, ctypes.c_int
+        L.g2v_oracle_grid_shape.argtypes = [P, P, P, P]
+        L.g2v_oracle_grid_shape.restype = i32
+        L.g2v_oracle_boxes.argtypes = [i64, P, P, P, P, P, P, P, P, P, P, P, P, P]
+        L.g2v_oracle_boxes.restype = None
+        L.g2v_oracle_g2t_offsets.argtypes = [i64, P, P]
+        L.g2v_oracle_g2t_offsets.restype = i64
+        L.g2v_oracle_g2t_fill.argtypes = [i64, P, P, P, P, P]
+        L.g2v_oracle_g2t_fill.restype = None
+        L.g2v_oracle_t2g.argtypes = [i64, i64, P, P, P, P]
+        L.g2v_oracle_t2g.restype = None
+        L.g2v_oracle_forward.argtypes = [i64, i32, P, P, P, P, P, P, P, P, P, i32, i32, P, P, i32]
+        L.g2v_oracle_forward.restype = None
+        L.g2v_oracle_backward.argtypes = [i64, i32, P, P, P, P, P, P, P, P, P, i32, i32, P, P, P, P, P, P, P,
+                                          P, i32]
+        L.g2v_oracle_backward.restype = None
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def grid_shape(voxel_size, voxel_range):
+    """(dims, tiles) with the reference's float32 arithmetic; raises ValueError on an invalid grid."""
+    size, rng = _f32(voxel_size), _f32(voxel_range)
+    dims = np.zeros(3, np.int32)
+    tiles = np.zeros(3, np.int32)
+    if lib().g2v_oracle_grid_shape(_p(size), _p(rng), _p(dims), _p(tiles)) != 0:
+        raise ValueError(f"invalid voxel grid: size={voxel_size} range={voxel_range}")
+    return tuple(int(v) for v in dims), tuple(int(v) for v in tiles)
+
+
+@dataclass
+class Boxes:
+    dims: tuple
+    tiles: tuple
+    lb: np.ndarray
+    ub: np.ndarray
+    num_voxels: np.ndarray
+    tile_lo: np.ndarray
+    tile_hi: np.ndarray
+    num_tiles: np.ndarray
+    cov_inv: np.ndarray
+    g2t_offsets: np.ndarray      # int64 (N+1)
+    g2t_tile_ids: np.ndarray     # int32 (M)
+    tile_offsets: np.ndarray     # int64 (num_tiles_total+1)
+    t2g_gaussians: np.ndarray    # int32 (M)
+
+
+def boxes(means, cov, voxel_size, voxel_range) -> Boxes:
+    """Boxes, G2T and T2G maps of the reference (float32 box arithmetic, IEEE sqrt/div)."""
+    means, cov = _f32(means).reshape(-1, 3), _f32(cov).reshape(-1, 9)
+    size, rng = _f32(voxel_size), _f32(voxel_range)
+    dims, tiles = grid_shape(size, rng)
+    n = means.shape[0]
+    d = np.asarray(dims, np.int32)
+    t = np.asarray(tiles, np.int32)
+    lb = np.zeros((n, 3), np.int32)
+    ub = np.zeros((n, 3), np.int32)
+    nv = np.zeros(n, np.int32)
+    tlo = np.zeros((n, 3), np.int32)
+    thi = np.zeros((n, 3), np.int32)
+    nt = np.zeros(n, np.int32)
+    ci = np.zeros((n, 9), np.float32)
+    L = lib()
+    L.g2v_oracle_boxes(n, _p(means), _p(cov), _p(size), _p(rng), _p(d), _p(t), _p(lb), _p(ub), _p(nv), _p(tlo),
+                       _p(thi), _p(nt), _p(ci))
+    off = np.zeros(n + 1, np.int64)
+    m = L.g2v_oracle_g2t_offsets(n, _p(nt), _p(off))
+    ids = np.zeros(max(m, 1), np.int32)
+    L.g2v_oracle_g2t_fill(n, _p(tlo), _p(thi), _p(off), _p(t), _p(ids))
+    ntt = int(t[0]) * int(t[1]) * int(t[2])
+    toff = np.zeros(ntt + 1, np.int64)
+    t2g = np.zeros(max(m, 1), np.int32)
+    L.g2v_oracle_t2g(n, ntt, _p(off), _p(ids), _p(toff), _p(t2g))
+    return Boxes(dims, tiles, lb, ub, nv, tlo, thi, nt, ci, off, ids[:m], toff, t2g[:m])
+
+
+def forward(means, opacity, cov, features, lb, ub, voxel_size, voxel_range, dims, x_range=None, nthreads=0):
+    """float64 brute-force density (X,Y,Z) and grid_feats (X,Y,Z,C) given the boxes lb/ub.
+
+    ``voxel_size``/``voxel_range`` are taken as float64 (the reference test builds them from Python
+    floats).  With ``x_range=(x0, x1)`` only that voxel slab is computed (the rest stays zero).
+    """
+    means, opacity, cov = _f32(means).reshape(-1, 3), _f32(opacity).reshape(-1), _f32(cov).reshape(-1, 9)
+    n = means.shape[0]
+    feats = None if features is None else _f32(features).reshape(n, -1)
+    c = 0 if feats is None else feats.shape[1]
+    X, Y, Z = dims
+    vlo = np.asarray(voxel_range[:3], np.float64)
+    vs = np.asarray(voxel_size, np.float64)
+    dm = np.asarray(dims, np.int32)
+    x0, x1 = (0, X) if x_range is None else x_range
+    dens = np.zeros((X, Y, Z), np.float64)
+    gf = np.zeros((X, Y, Z, c), np.float64) if c > 0 else None
+    lib().g2v_oracle_forward(n, c, _p(means), _p(opacity), _p(cov), _p(feats), _p(_i32(lb)), _p(_i32(ub)),
+                             _p(vlo), _p(vs), _p(dm), x0, x1, _p(dens), _p(gf), nthreads)
+    if gf is None:
+        gf = np.zeros((X, Y, Z, 0), np.float64)
+    return dens, gf
+
+
+def backward(means, opacity, cov, features, lb, ub, voxel_size, voxel_range, dims, grad_density, grad_feats,
+             density, grid_feats, x_range=None, nthreads=0):
+    """float64 analytic gradients (means (N,3), cov (N,9), opacity (N,), features (N,C))."""
+    means, opacity, cov = _f32(means).reshape(-1, 3), _f32(opacity).reshape(-1), _f32(cov).reshape(-1, 9)
+    n = means.shape[0]
+    feats = None if features is None else _f32(features).reshape(n, -1)
+    c = 0 if feats is None else feats.shape[1]
+    X, Y, Z = dims
+    vlo = np.asarray(voxel_range[:3], np.float64)
+    vs = np.asarray(voxel_size, np.float64)
+    dm = np.asarray(dims, np.int32)
+    x0, x1 = (0, X) if x_range is None else x_range
+    gD = _f32(grad_density).reshape(-1)
+    gF = _f32(grad_feats).reshape(-1) if c > 0 else None
+    D = np.ascontiguousarray(np.asarray(density, np.float64)).reshape(-1)
+    F = np.ascontiguousarray(np.asarray(grid_feats, np.float64)).reshape(-1) if c > 0 else None
+    g_means = np.zeros((n, 3), np.float64)
+    g_cov = np.zeros((n, 9), np.float64)
+    g_op = np.zeros(n, np.float64)
+    g_feat = np.zeros((n, c), np.float64)
+    lib().g2v_oracle_backward(n, c, _p(means), _p(opacity), _p(cov), _p(feats), _p(_i32(lb)), _p(_i32(ub)),
+                              _p(vlo), _p(vs), _p(dm), x0, x1, _p(gD), _p(gF), _p(D), _p(F), _p(g_means),
+                              _p(g_cov), _p(g_op), _p(g_feat), nthreads)
+    return g_means, g_cov, g_op, g_feat
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def rel_err(a, b) -> float:
+    """Relative L2 error, as test/test_reference.py:82-83 defines it."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+def generate_inputs(num_gaussians, feat_dim, voxel_range, num_outside=0, seed=0, var_max=2.5, expand=0.0):
+    """Seeded CPU inputs with the reference's distributions (test/test_reference.py:30-45).
+
+    means ~ U(range) (optionally widened by ``expand`` x extent on each side), opacity ~ U(0,1),
+    cov = R diag(U(0.5, var_max)) R^T with R from QR of randn(3,3), features ~ randn.  ``num_outside``
+    extra Gaussians are centred beyond x_max by U(0, 1.5).  Uses torch's CPU generator so that the
+    same seed gives the same inputs everywhere.
+    """
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    lo = torch.tensor(voxel_range[:3], dtype=torch.float32)
+    hi = torch.tensor(voxel_range[3:], dtype=torch.float32)
+    if expand:
+        ext = hi - lo
+        lo, hi = lo - expand * ext, hi + expand * ext
+    means = torch.rand(num_gaussians, 3, generator=g) * (hi - lo) + lo
+    if num_outside:
+        lo0 = torch.tensor(voxel_range[:3], dtype=torch.float32)
+        hi0 = torch.tensor(voxel_range[3:], dtype=torch.float32)
+        out = torch.rand(num_outside, 3, generator=g) * (hi0 - lo0) + lo0
+        out[:, 0] = hi0[0] + torch.rand(num_outside, generator=g) * 1.5
+        means = torch.cat([means, out])
+    n = means.shape[0]
+    opacity = torch.rand(n, generator=g)
+    R, _ = torch.linalg.qr(torch.randn(n, 3, 3, generator=g))
+    var = torch.rand(n, 3, generator=g) * (var_max - 0.5) + 0.5
+    cov = (R @ torch.diag_embed(var) @ R.mT).reshape(n, 9)
+    feats = torch.randn(n, feat_dim, generator=g) if feat_dim is not None else None
+    return means.contiguous(), opacity.contiguous(), cov.contiguous(), (
+        feats.contiguous() if feats is not None else None)
