@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""G2V fwd+bwd benchmark (BASELINE.json metric: ms/step at 18k Gaussians x 1024-D on 200x200x16).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3] [--impl ours|reference]
+
+One step = forward of PyCudaGaussianVoxelizer + backward with randn upstream gradients for density
+and grid_feats, i.e. the gradient of sum(density*gD) + sum(grid_feats*gF) w.r.t. means3D, opacity,
+covariances and features.  Inputs are synthetic with the reference's distributions (seeded CPU
+generation, test/test_reference.py:30-45).  Every input of a step is larger than L2 (grid_feats and its
+gradient are 2.6 GB each at cfg3), so no L2 flush is needed between steps.
+
+With N > 1 (torchrun, one rank per GPU) every rank runs its own scene (batched scenes, data-parallel,
+no collective in the step); the reported time is the max over ranks ("scaling": "weak").
+``--impl reference`` times the CPU restatement of the reference's algorithm (oracle/, float64, all host
+threads) on a bounded x-slab sample of the same workload and, when the reference build exists in
+oracle/_ref, also times that CUDA build on the GPU ("reference_cuda").
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "shelfgaussian-cudagaussianvoxelizer_b200")
+for _p in (REPO, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+RANGE = [-40.0, -40.0, -1.0, 40.0, 40.0, 5.4]
+CONFIGS = {
+    "cfg1": dict(n=512, c=32, size=0.4, range=[-8.0, -8.0, -1.0, 8.0, 8.0, 5.4], var_max=2.5, expand=0.0),
+    "cfg2": dict(n=9000, c=768, size=0.4, range=RANGE, var_max=2.5, expand=0.0),
+    "cfg3": dict(n=18000, c=1024, size=0.4, range=RANGE, var_max=2.5, expand=0.0),
+    "cfg4": dict(n=18000, c=1024, size=0.4, range=RANGE, var_max=2.5, expand=0.05),
+    "cfg5": dict(n=100000, c=256, size=0.2, range=RANGE, var_max=8.0, expand=0.0),
+}
+METRIC = "G2V fwd+bwd ms/step (18k Gaussians, 1024-D, 200×200×16) and % HBM roofline"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="g2v_clocks_", suffix=".csv")
+        try:
+            self.fh = open(self.path, "w")
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+            if gpu_id is not None:
+                cmd += ["-i", str(gpu_id)]
+            self.proc = subprocess.Popen(cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_id_for(dev_index):
+    import torch
+    try:
+        u = str(torch.cuda.get_device_properties(dev_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[dev_index]
+        return dev_index
+
+
+# ------------------------------------------------------------------------------------------------
+def make_inputs(cfg, seed):
+    from oracle import oracle
+    size = [cfg["size"]] * 3
+    m, o, c, f = oracle.generate_inputs(cfg["n"], cfg["c"], cfg["range"], seed=seed, var_max=cfg["var_max"],
+                                        expand=cfg["expand"])
+    return size, cfg["range"], m, o, c, f
+
+
+def algorithmic_bytes(kernel, n, c, V, M, MB, ntiles):
+    """Algorithmic HBM bytes of one launch over the whole grid (per-unit figures of the design doc)."""
+    per_gauss = n * (12 + 4 + 36 + 24)  # mean, opacity, cov_inv, lb/ub
+    if kernel == "splat_tile_kernel":
+        return 4 * V * c + 4 * V + 4 * n * c + per_gauss + 4 * M + 4 * (ntiles + 1)
+    if kernel == "spass_kernel":
+        return 4 * V * c + 4 * n * c + 8 * V + 40 * M + per_gauss + 4 * M + 4 * (ntiles + 1)
+    if kernel == "fpass_kernel":
+        return 4 * V * c + 4 * V + 4 * MB * c + per_gauss
+    if kernel == "reduce_feats_kernel":
+        return 4 * MB * c + 4 * n * c
+    return None
+
+
+def step_bytes(n, c, V, M):
+    """Algorithmic bytes of one fwd+bwd step (SURVEY formula, 8.11 GB at cfg3)."""
+    fwd = n * 52 + 4 * n * c + 4 * V + 4 * V * c + n * 64 + 4 * (n + 1) + 4 * M
+    bwd = 8 * V + 8 * V * c + 4 * n * c + n * 76 + 4 * (n + 1) + 4 * M + n * 52 + 4 * n * c
+    return fwd + bwd
+
+
+def run_ours(args, rank, world, dev):
+    import numpy as np  # noqa: F401
+    import torch
+    import torch.distributed as dist
+    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer, _C, _lib
+
+    cfg = CONFIGS[args.config]
+    size, rng, m_h, o_h, c_h, f_h = make_inputs(cfg, seed=args.seed + rank)
+    (X, Y, Z), tiles = _C.grid_shape(size, rng)
+    V = X * Y * Z
+    n, c = cfg["n"], cfg["c"]
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gD = torch.randn((X, Y, Z), device=dev, generator=g)
+    gF = torch.randn((X, Y, Z, c), device=dev, generator=g)
+    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
+    vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+
+    def step():
+        density, grid_feats, _ = vox(*leaves)
+        return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_id_for(dev.index))
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # per-kernel device time (CUDA events on the launch stream, inside the library) over K steps
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    launches_per_step = sum(v[1] for v in prof.values()) / args.steps
+
+    # sizes for the roofline
+    out = _C.gaussian_voxelizer_forward(*[t.detach() for t in leaves[:3]], size, rng, leaves[3].detach(),
+                                        timing=False)
+    M = int(out[7].numel())
+    MB = _C.backward_plan(out[2], out[3], (X, Y, Z), c)
+    del out
+    ntiles = tiles[0] * tiles[1] * tiles[2]
+    peak, peak_kind = load_peaks()
+    top = max(prof.items(), key=lambda kv: kv[1][0])
+    kname, (kms, kcount) = top
+    kbytes = algorithmic_bytes(kname, n, c, V, M, MB, ntiles)
+    avg_ms = kms / kcount
+    achieved = kbytes / (avg_ms * 1e-3) / 1e9 if kbytes else None
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as fh:
+            traffic = json.load(fh).get(args.config, {}).get(kname)
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": avg_ms,
+                "kernel_share": {k: round(v[0] / sum(x[0] for x in prof.values()), 4) for k, v in prof.items()}}
+    sb = step_bytes(n, c, V, M)
+
+    # end-to-end through the public API with pinned host inputs (H2D inside the timed region)
+    host = [t.pin_memory() for t in (m_h, o_h, c_h, f_h)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    vox_e2e = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng)  # default: stats timing on
+
+    def e2e_step():
+        ls = [t.to(dev, non_blocking=True).requires_grad_() for t in host]
+        density, grid_feats, stats = vox_e2e(*ls)
+        loss = (density * gD).sum() + (grid_feats * gF).sum()
+        loss.backward()
+        return loss.detach().to("cpu").item()
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, args.seed, threads=os.cpu_count() or 1, steps=1)
+
+    line = {
+        "metric": METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference distributions)",
+        "config": {"workload": f"{args.config}: N={n} Gaussians, C={c} fp32 features, {X}x{Y}x{Z} voxels, "
+                               f"fwd+bwd with randn upstream grads", "global_batch": world,
+                   "scenes_per_rank": 1, "l2": "inputs larger than L2 (grid_feats 4*V*C bytes)",
+                   "pairs_M": M, "block_pairs": MB, "parallelism": f"dp{world} (independent scenes)"},
+        "roofline": roofline,
+        "step_roofline": {"algorithmic_bytes": sb, "achieved_gbs": sb / (ms * 1e-3) / 1e9,
+                          "frac": sb / (ms * 1e-3) / 1e9 / peak},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": clocks,
+    }
+    return line
+
+
+def cpu_baseline(cfg, seed, threads, steps=1, slab_vox=16):
+    """The oracle (float64 C restatement of the reference algorithm) on an x-slab of the grid: the
+    forward and backward of the voxels in `slab_vox` x-columns at the centre of the grid; ms/step
+    scaled to the full grid by X / slab_vox."""
+    import numpy as np
+    from oracle import oracle
+    size, rng, m, o, c, f = make_inputs(cfg, seed)
+    m, o, c, f = m.numpy(), o.numpy(), c.numpy(), f.numpy()
+    bx = oracle.boxes(m, c, size, rng)
+    X, Y, Z = bx.dims
+    x0 = (X // 2 // 4) * 4 - slab_vox // 2
+    x0 = max(0, x0 - x0 % 4)
+    x1 = min(X, x0 + slab_vox)
+    C = f.shape[1]
+    rs = np.random.default_rng(7)
+    gD = np.zeros((X, Y, Z), np.float32)
+    gF = np.zeros((X, Y, Z, C), np.float32)
+    gD[x0:x1] = rs.standard_normal((x1 - x0, Y, Z), dtype=np.float32)
+    gF[x0:x1] = rs.standard_normal((x1 - x0, Y, Z, C), dtype=np.float32)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        D, F = oracle.forward(m, o, c, f, bx.lb, bx.ub, size, rng, (X, Y, Z), x_range=(x0, x1), nthreads=threads)
+        oracle.backward(m, o, c, f, bx.lb, bx.ub, size, rng, (X, Y, Z), gD, gF, D, F, x_range=(x0, x1),
+                        nthreads=threads)
+        times.append(time.perf_counter() - t0)
+        del D, F
+    t = min(times)
+    return {"value": round(t * 1e3 * X / (x1 - x0), 1), "unit": "ms", "cores": threads, "kind": "port",
+            "sample": f"x-slab of {x1 - x0} of {X} voxel columns (forward + backward of those voxels), "
+                      f"float64, scaled x{X / (x1 - x0):.1f} to the full grid; {t:.2f} s per sample"}
+
+
+def reference_cuda(cfg, seed, dev, steps=2):
+    """Time the reference's own CUDA build (oracle/_ref, compiled from its sources) on this GPU."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import build_ref
+    ext = build_ref.load()
+    if ext is None:
+        return {"unavailable": "oracle/_ref has no reference build"}
+    import torch
+    size, rng, m, o, c, f = make_inputs(cfg, seed)
+    m, o, c, f = [t.to(dev).contiguous() for t in (m, o, c, f)]
+    vs = torch.tensor(size, dtype=torch.float32, device=dev)
+    vr = torch.tensor(rng, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    out = ext.gaussian_voxelizer_forward(m, o, c, vs, vr, f)
+    X, Y, Z = out[0].shape
+    gD = torch.randn((X, Y, Z), device=dev, generator=g)
+    gF = torch.randn((X, Y, Z, f.shape[1]), device=dev, generator=g)
+    del out
+
+    def step():
+        d, ci, lb, ub, nv, gf, off, ids, fs = ext.gaussian_voxelizer_forward(m, o, c, vs, vr, f)
+        r = ext.gaussian_voxelizer_backward(gD, gF, m, o, ci, vs, vr, lb, ub, nv, off, ids, d, gf, f)
+        return fs, r[4]
+
+    step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    st = [step() for _ in range(steps)]
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": round(ms, 3), "unit": "ms", "steps": steps, "device": torch.cuda.get_device_name(dev),
+            "fwd_sec": [round(a, 5) for a, _ in st], "bwd_sec": [round(b, 5) for _, b in st],
+            "source": "reference src/cuda_gaussian_voxelizer.cu built for sm_100a by oracle/build_ref.py"}
+
+
+def run_reference(args, rank, world, dev):
+    cfg = CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(cfg, args.seed, threads=threads, steps=1)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    value = statistics.median(vals)
+    cpu = dict(r)
+    cpu["value"] = value
+    line = {"metric": METRIC, "value": value, "unit": "ms", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded, reference distributions)",
+            "config": {"workload": f"{args.config}: N={cfg['n']}, C={cfg['c']}, CPU x-slab sample",
+                       "global_batch": 1},
+            "cpu_baseline": cpu, "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0}}
+    if dev is not None and not args.no_reference_cuda:
+        try:
+            line["reference_cuda"] = reference_cuda(cfg, args.seed, dev)
+        except Exception as exc:  # report, do not fail the CPU arm
+            line["reference_cuda"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="cfg3", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-cuda", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import torch
+        dev = torch.device("cuda", local) if torch.cuda.is_available() else None
+        print(json.dumps(run_reference(args, rank, world, dev)), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    try:
+        line = run_ours(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

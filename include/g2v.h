@@ -1,0 +1,163 @@
+/*
+ * g2v.h -- C ABI of libg2v.so, the B200 (sm_100a) Gaussian-to-voxel (G2V) splatting library.
+ *
+ * The library replaces the reference's CUDA path behind `CudaGaussianVoxelizer._C`
+ * (src/bindings.cpp:8-64 of lunarlab-gatech/ShelfGaussian-CudaGaussianVoxelizer).  Every argument is a
+ * plain pointer or size; device pointers are CUDA device memory on the current device, `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  The library never allocates device memory: every call
+ * that needs scratch takes a caller-provided `workspace` whose size comes from the matching
+ * *_workspace_size query.  No call exits the process; errors come back as a g2v_status and
+ * g2v_last_error() holds a message for the calling thread.
+ *
+ * Layouts (row-major, float32 unless noted):
+ *   means3d (N,3), opacity (N), covariances (N,9) (flattened 3x3), features (N,C)
+ *   cov_inv (N,9), valid_voxel_lb / valid_voxel_ub (N,3) int32, num_voxels (N) int32
+ *   g2t_offsets (N+1) int32, g2t_tile_ids (M) int32        -- the Gaussian->Tile CSR
+ *   density (X,Y,Z), grid_feats (X,Y,Z,C)
+ * Tiles are 4x4x4 voxels; the tile id of tile (tx,ty,tz) is (tx*Ty+ty)*Tz+tz.
+ */
+#ifndef G2V_H
+#define G2V_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define G2V_API __attribute__((visibility("default")))
+#else
+#define G2V_API
+#endif
+
+#define G2V_ABI_VERSION 1
+#define G2V_TILE 4
+
+typedef enum g2v_status {
+    G2V_SUCCESS = 0,
+    G2V_ERROR_INVALID_VALUE = 1,        /* bad pointer, shape or voxel grid */
+    G2V_ERROR_WORKSPACE_TOO_SMALL = 2,  /* workspace_bytes below the queried size */
+    G2V_ERROR_SIZE_LIMIT = 3,           /* a count exceeds the int32 range of the CSR maps */
+    G2V_ERROR_CUDA = 4,                 /* a CUDA runtime call or kernel launch failed */
+    G2V_ERROR_NOT_SUPPORTED = 5         /* e.g. no sm_100 device */
+} g2v_status;
+
+/* Version of this ABI (G2V_ABI_VERSION). */
+G2V_API int g2v_abi_version(void);
+
+/* Short name of a status code. */
+G2V_API const char* g2v_status_string(int status);
+
+/* Message of the last failing call made by this thread ("" if none). */
+G2V_API const char* g2v_last_error(void);
+
+/*
+ * Voxel grid and tile grid from the voxel size (3) and range [x0,y0,z0,x1,y1,z1] (6), computed with
+ * float32 host arithmetic: dims[a] = (int)((range[a+3]-range[a]) / size[a]), tiles[a] = ceil(dims[a]/4).
+ * Replaces src/cuda_gaussian_voxelizer.cu:1512-1519 (which reads the values with 9 .item() syncs).
+ * Fails with G2V_ERROR_INVALID_VALUE when a dimension is < 1.
+ */
+G2V_API int g2v_grid_shape(const float voxel_size[3], const float voxel_range[6], int dims[3], int tiles[3]);
+
+/* Workspace of g2v_forward_prepare for N Gaussians. */
+G2V_API int g2v_forward_prepare_workspace_size(int64_t num_gaussians, size_t* bytes);
+
+/*
+ * Forward, stage 1: per-Gaussian 3-sigma voxel box, tile count and inverse covariance, then the
+ * exclusive prefix sum of the tile counts (g2t_offsets, N+1 entries).  Writes cov_inv, valid_voxel_lb,
+ * valid_voxel_ub, num_voxels and g2t_offsets, then reads M = g2t_offsets[N] back to *num_pairs
+ * (host) -- the one stream synchronisation of the forward.
+ * Replaces src/cuda_gaussian_voxelizer.cu:1484-1631 (ComputeGaussianVoxelPairTile cu:348-536, the CUB
+ * scan cu:1608-1615 and the total_tiles_touched readback cu:1628-1631).
+ */
+G2V_API int g2v_forward_prepare(const float* means3d, const float* covariances, int64_t num_gaussians,
+                        const float voxel_size[3], const float voxel_range[6], float* cov_inv,
+                        int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
+                        int32_t* g2t_offsets, void* workspace, size_t workspace_bytes, void* stream,
+                        int64_t* num_pairs);
+
+/* Workspace of g2v_forward_splat. */
+G2V_API int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3],
+                                     int64_t channels, size_t* bytes);
+
+/*
+ * Forward, stage 2: fills the Gaussian->Tile tile ids (g2t_tile_ids, M entries, x-major over each
+ * Gaussian's tile box), builds the Tile->Gaussian CSR (Gaussian ids ascending inside a tile) and
+ * splats every tile: density D_v = sum_g w_gv and grid_feats F_v = sum_g w_gv f_g / max(D_v, 1e-6),
+ * w_gv = opacity_g * exp(-1/2 d^T cov_inv_g d) over the voxels of the Gaussian's box.  Every voxel of
+ * the tiles with tile x in [tile_x_begin, tile_x_end) is written (zeros where no Gaussian reaches);
+ * pass 0 and tiles[0] for the whole grid.  features == NULL selects the density-only path
+ * (grid_feats unused, channels ignored).  With features != NULL and channels == 0 the density is
+ * left at zero, as the reference does (its density sum sits inside the channel loop, cu:857-926).
+ * Replaces src/cuda_gaussian_voxelizer.cu:1633-1913 (FillG2TKernel, CUB SortPairs / RunLengthEncode /
+ * scan, zero_, ComputeGaussian2VoxelTileWithFeats or ComputeGaussian2VoxelTile, clamp_min + div_).
+ */
+G2V_API int g2v_forward_splat(const float* means3d, const float* opacity, const float* features, int64_t num_gaussians,
+                      int64_t channels, const float voxel_size[3], const float voxel_range[6],
+                      const float* cov_inv, const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub,
+                      const int32_t* g2t_offsets, int64_t num_pairs, int32_t* g2t_tile_ids, float* density,
+                      float* grid_feats, int tile_x_begin, int tile_x_end, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/*
+ * Backward planning: counts the (Gaussian, tile block) pairs that the feature-gradient pass needs and
+ * reads the count back to *num_block_pairs (one stream synchronisation).  Needed only to size the
+ * backward workspace; the Python layer obtains it once per forward.
+ * No direct reference counterpart (the reference backward allocates inside cu:1964-1967).
+ */
+G2V_API int g2v_backward_plan(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, int64_t num_gaussians,
+                      const int dims[3], int64_t channels, void* workspace, size_t workspace_bytes,
+                      void* stream, int64_t* num_block_pairs);
+
+/* Workspace of g2v_backward_plan (N-sized). */
+G2V_API int g2v_backward_plan_workspace_size(int64_t num_gaussians, size_t* bytes);
+
+/* Workspace of g2v_backward. */
+G2V_API int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs, int64_t num_block_pairs,
+                                const int dims[3], int64_t channels, size_t* bytes);
+
+/*
+ * Backward of L(density, grid_feats) given dL/ddensity (X,Y,Z) and dL/dgrid_feats (X,Y,Z,C):
+ * writes grad_means3d (N,3), grad_covariances (N,9, symmetric, off-diagonal not halved),
+ * grad_opacity (N) and, when features != NULL, grad_features (N,C).  Every output element is written.
+ * Only the voxels of tiles with tile x in [tile_x_begin, tile_x_end) contribute (0 / tiles[0] for the
+ * whole grid): on an x-slab the outputs are that slab's partial gradients.
+ * grid_feats is accepted for interface parity and not read: sum_c dL/dF_vc F_vc is formed from the
+ * per-pair dot products the kernel computes anyway.
+ * Replaces src/cuda_gaussian_voxelizer.cu:1920-2057 (the at::bmm at cu:1996 and
+ * ComputeGaussian2VoxelGradientTileWithFeats / ComputeGaussian2VoxelGradientTile).
+ */
+G2V_API int g2v_backward(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                 const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
+                 int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                 const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                 const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs, const float* density,
+                 const float* grid_feats, float* grad_means3d, float* grad_covariances, float* grad_opacity,
+                 float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/*
+ * Debug / parity hook: the Tile->Gaussian CSR built by g2v_forward_splat for the whole grid, copied
+ * out of the splat workspace after the call: tile_offsets (num_tiles+1, int32) and t2g_gaussians
+ * (M, int32).  No reference counterpart (the reference keeps this map internal, cu:1675-1772).
+ */
+G2V_API int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs,
+                       const int dims[3], int32_t* tile_offsets, int32_t* t2g_gaussians, void* stream);
+
+/*
+ * Profiling hook (no reference counterpart): when enabled, every kernel launch of the library is
+ * bracketed by CUDA events on its launch stream.  g2v_profile_enable(1) clears the records and starts
+ * recording, g2v_profile_enable(0) stops.  g2v_profile_read(i, ...) waits for the recorded events,
+ * aggregates them by kernel name and returns entry i (name, total milliseconds, launches);
+ * it returns G2V_ERROR_INVALID_VALUE past the last entry.
+ */
+G2V_API int g2v_profile_enable(int enabled);
+G2V_API int g2v_profile_read(int index, char* name, size_t name_len, double* total_ms, int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G2V_H */

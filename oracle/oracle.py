@@ -129,6 +129,28 @@ def boxes(means, cov, voxel_size, voxel_range) -> Boxes:
     return Boxes(dims, tiles, lb, ub, nv, tlo, thi, nt, ci, off, ids[:m], toff, t2g[:m])
 
 
+def csr_from_boxes(lb, ub, dims):
+    """G2T / T2G maps of given voxel boxes (tile box = voxel box / 4, empty when ub < lb)."""
+    lb, ub = _i32(lb).reshape(-1, 3), _i32(ub).reshape(-1, 3)
+    n = lb.shape[0]
+    tiles = np.asarray([(d + 3) // 4 for d in dims], np.int32)
+    empty = (ub < lb).any(axis=1)
+    tlo = np.where(empty[:, None], 0, lb // 4).astype(np.int32)
+    thi = np.where(empty[:, None], -1, ub // 4).astype(np.int32)
+    nt = np.where(empty, 0, np.prod(thi - tlo + 1, axis=1)).astype(np.int32)
+    L = lib()
+    off = np.zeros(n + 1, np.int64)
+    m = L.g2v_oracle_g2t_offsets(n, _p(nt), _p(off))
+    ids = np.zeros(max(m, 1), np.int32)
+    L.g2v_oracle_g2t_fill(n, _p(np.ascontiguousarray(tlo)), _p(np.ascontiguousarray(thi)), _p(off), _p(tiles),
+                          _p(ids))
+    ntt = int(tiles.prod())
+    toff = np.zeros(ntt + 1, np.int64)
+    t2g = np.zeros(max(m, 1), np.int32)
+    L.g2v_oracle_t2g(n, ntt, _p(off), _p(ids), _p(toff), _p(t2g))
+    return off, ids[:m], toff, t2g[:m]
+
+
 def forward(means, opacity, cov, features, lb, ub, voxel_size, voxel_range, dims, x_range=None, nthreads=0):
     """float64 brute-force density (X,Y,Z) and grid_feats (X,Y,Z,C) given the boxes lb/ub.
 

@@ -1,0 +1,242 @@
+"""Drop-in replacement of the reference's ``CudaGaussianVoxelizer._C`` voxelizer functions.
+
+Same names, argument names, argument meaning and return tuples as the reference's pybind module
+(src/bindings.cpp:8-64), implemented over the C ABI of libg2v.so.  Outputs are allocated from the
+torch caching allocator on ``means3D.device``; the library itself never allocates: every call passes
+it a workspace tensor.  Failures raise ``RuntimeError`` (never exit the process).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["gaussian_voxelizer_forward", "gaussian_voxelizer_backward", "grid_shape", "t2g_maps"]
+
+_geom_cache: dict = {}
+
+
+def _host_values(t, n: int, name: str):
+    """Host floats of voxel_size / voxel_range; tensors are read once and cached by storage + version."""
+    if isinstance(t, torch.Tensor):
+        if t.numel() != n:
+            raise RuntimeError(f"{name} must have {n} elements, got {t.numel()}")
+        key = (name, t.device, t.data_ptr(), t._version, t.dtype)
+        v = _geom_cache.get(key)
+        if v is None:
+            v = tuple(float(x) for x in t.detach().to("cpu", torch.float32).tolist())
+            if len(_geom_cache) > 64:
+                _geom_cache.clear()
+            _geom_cache[key] = v
+        return v
+    v = tuple(float(x) for x in t)
+    if len(v) != n:
+        raise RuntimeError(f"{name} must have {n} elements, got {len(v)}")
+    return v
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None and t.numel() > 0 else ctypes.c_void_p(0)
+
+
+def _need(t, name, dtype=torch.float32, dim=None, device=None):
+    if not isinstance(t, torch.Tensor):
+        raise RuntimeError(f"{name} must be a tensor")
+    if t.dtype != dtype:
+        raise RuntimeError(f"expected scalar type {dtype} for {name} but found {t.dtype}")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if device is not None and t.device != device:
+        raise RuntimeError(f"{name} is on {t.device}, expected {device}")
+    if dim is not None and t.dim() != dim:
+        raise RuntimeError(f"{name} must have {dim} dimensions, got {t.dim()}")
+
+
+def _need_contig(t, name, dtype, device):
+    _need(t, name, dtype, None, device)
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def grid_shape(voxel_size, voxel_range):
+    """((X, Y, Z), (Tx, Ty, Tz)) with the reference's float32 rule (cu:1512-1519)."""
+    return _lib.grid_shape(_host_values(voxel_size, 3, "voxel_size"), _host_values(voxel_range, 6, "voxel_range"))
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False):
+    lib = _lib.load()
+    size_h = _host_values(voxel_size, 3, "voxel_size")
+    range_h = _host_values(voxel_range, 6, "voxel_range")
+    _need(means3D, "means3D", dim=2)
+    dev = means3D.device
+    _need(opacity, "opacity", dim=1, device=dev)
+    _need(covariances, "covariances", dim=2, device=dev)
+    n = means3D.shape[0]
+    if means3D.shape[1] != 3 or covariances.shape != (n, 9) or opacity.shape[0] != n:
+        raise RuntimeError(f"expected means3D (N,3), opacity (N,), covariances (N,9); got {tuple(means3D.shape)}, "
+                           f"{tuple(opacity.shape)}, {tuple(covariances.shape)}")
+    if features is not None:
+        _need(features, "features", dim=2, device=dev)
+        if features.shape[0] != n:
+            raise RuntimeError(f"features must have {n} rows, got {features.shape[0]}")
+        features = features.contiguous()
+    c = 0 if features is None else int(features.shape[1])
+    means3D, opacity, covariances = means3D.contiguous(), opacity.contiguous(), covariances.contiguous()
+    (X, Y, Z), _ = _lib.grid_shape(size_h, range_h)
+    i32 = dict(dtype=torch.int32, device=dev)
+    f32 = dict(dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        sptr = ctypes.c_void_p(stream.cuda_stream)
+        cov_inv = torch.empty((n, 9), **f32)
+        lb = torch.empty((n, 3), **i32)
+        ub = torch.empty((n, 3), **i32)
+        nvox = torch.empty((n,), **i32)
+        g2t_offsets = torch.empty((n + 1,), **i32)
+        nbytes = ctypes.c_size_t()
+        _lib.check(lib.g2v_forward_prepare_workspace_size(n, ctypes.byref(nbytes)), "g2v_forward_prepare_workspace_size")
+        ws1 = _workspace(nbytes.value, dev)
+        if timing:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+        m = ctypes.c_int64()
+        _lib.check(lib.g2v_forward_prepare(_ptr(means3D), _ptr(covariances), n, _lib.f3(size_h), _lib.f6(range_h),
+                                           _ptr(cov_inv), _ptr(lb), _ptr(ub), _ptr(nvox), _ptr(g2t_offsets),
+                                           _ptr(ws1), ws1.numel(), sptr, ctypes.byref(m)), "g2v_forward_prepare")
+        m = int(m.value)
+        g2t_tile_ids = torch.empty((m,), **i32)
+        density = torch.empty((X, Y, Z), **f32)
+        grid_feats = torch.empty((X, Y, Z, c), **f32)
+        _lib.check(lib.g2v_forward_splat_workspace_size(n, m, _lib.i3((X, Y, Z)), c, ctypes.byref(nbytes)),
+                   "g2v_forward_splat_workspace_size")
+        ws2 = _workspace(nbytes.value, dev)
+        _lib.check(lib.g2v_forward_splat(_ptr(means3D), _ptr(opacity),
+                                         ctypes.c_void_p(features.data_ptr()) if features is not None else None,
+                                         n, c, _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub),
+                                         _ptr(g2t_offsets), m, _ptr(g2t_tile_ids), _ptr(density), _ptr(grid_feats),
+                                         0, 0, _ptr(ws2), ws2.numel(), sptr), "g2v_forward_splat")
+        sec = 0.0
+        if timing:
+            ev1.record(stream)
+            ev1.synchronize()
+            sec = ev0.elapsed_time(ev1) / 1000.0
+        out = (density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, sec)
+        if keep_t2g:
+            tiles = _lib.grid_shape(size_h, range_h)[1]
+            nt = tiles[0] * tiles[1] * tiles[2]
+            toff = torch.empty((nt + 1,), **i32)
+            t2g = torch.empty((max(m, 1),), **i32)
+            _lib.check(lib.g2v_debug_copy_t2g(_ptr(ws2), n, m, _lib.i3((X, Y, Z)), _ptr(toff), _ptr(t2g), sptr),
+                       "g2v_debug_copy_t2g")
+            return out, (toff, t2g[:m])
+        return out
+
+
+def gaussian_voxelizer_forward(means3D, opacity, covariances, voxel_size, voxel_range, features=None, *,
+                               timing: bool = True):
+    """Forward of the G2V splat (reference src/bindings.cpp:8-28, cu:1484-1918).
+
+    Returns ``(density (X,Y,Z), cov_inv (N,9), valid_voxel_lb (N,3), valid_voxel_ub (N,3),
+    num_voxels_per_gaussian (N,), grid_feats (X,Y,Z,C), g2t_offsets (N+1,), g2t_tile_ids (M,), fwd_sec)``.
+    ``fwd_sec`` is the device time of the call (CUDA events; 0.0 with ``timing=False``, which also
+    drops the end-of-call synchronisation).
+    """
+    return _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing)
+
+
+def t2g_maps(means3D, opacity, covariances, voxel_size, voxel_range, features=None):
+    """Forward outputs plus the Tile->Gaussian CSR built by the splat: (outputs, (tile_offsets, t2g_gaussians))."""
+    return _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, False, keep_t2g=True)
+
+
+def backward_plan(valid_voxel_lb, valid_voxel_ub, dims, channels) -> int:
+    """Number of (Gaussian, tile block) pairs of the feature-gradient pass (one synchronisation)."""
+    lib = _lib.load()
+    dev = valid_voxel_lb.device
+    n = valid_voxel_lb.shape[0]
+    nbytes = ctypes.c_size_t()
+    _lib.check(lib.g2v_backward_plan_workspace_size(n, ctypes.byref(nbytes)), "g2v_backward_plan_workspace_size")
+    with torch.cuda.device(dev):
+        ws = _workspace(nbytes.value, dev)
+        mb = ctypes.c_int64()
+        sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(lib.g2v_backward_plan(_ptr(valid_voxel_lb), _ptr(valid_voxel_ub), n, _lib.i3(dims), int(channels),
+                                         _ptr(ws), ws.numel(), sptr, ctypes.byref(mb)), "g2v_backward_plan")
+    return int(mb.value)
+
+
+def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity, cov_inv, voxel_size, voxel_range,
+                                valid_voxel_lb, valid_voxel_ub, num_voxels_per_gaussian, g2t_offsets, g2t_tile_ids,
+                                density, grid_feats, features=None, *, timing: bool = True,
+                                num_block_pairs: int | None = None, tile_x_range=None):
+    """Backward of the G2V splat (reference src/bindings.cpp:30-64, cu:1920-2057).
+
+    Returns ``(grad_means3D (N,3), grad_cov (N,9), grad_opacity (N,), grad_feats (N,C), bwd_sec)``;
+    ``grad_feats`` is (N,0) when ``features`` is None.  Inputs must be contiguous CUDA tensors of the
+    reference's dtypes (RuntimeError otherwise, like the reference's TORCH_CHECKs, cu:1941-1954).
+    ``tile_x_range=(b, e)`` restricts the gradient to the voxels of tiles with x in [b, e).
+    """
+    lib = _lib.load()
+    dev = means3D.device
+    size_h = _host_values(voxel_size, 3, "voxel_size")
+    range_h = _host_values(voxel_range, 6, "voxel_range")
+    for t, name, dt in ((grad_output, "grad_output", torch.float32), (means3D, "means3D", torch.float32),
+                        (opacity, "opacity", torch.float32), (cov_inv, "cov_inv", torch.float32),
+                        (valid_voxel_lb, "valid_voxel_lb", torch.int32), (valid_voxel_ub, "valid_voxel_ub", torch.int32),
+                        (num_voxels_per_gaussian, "num_voxels_per_gaussian", torch.int32),
+                        (g2t_offsets, "g2t_offsets", torch.int32), (g2t_tile_ids, "g2t_tile_ids", torch.int32),
+                        (density, "density", torch.float32), (grid_feats, "grid_feats", torch.float32)):
+        _need_contig(t, name, dt, dev)
+    n = means3D.shape[0]
+    if g2t_offsets.numel() != n + 1:
+        raise RuntimeError("g2t_offsets must have N+1 entries")
+    c = 0
+    if features is not None:
+        _need_contig(features, "features", torch.float32, dev)
+        c = int(features.shape[1])
+        _need_contig(grad_feats_output, "grad_feats_output", torch.float32, dev)
+    dims = tuple(int(s) for s in grad_output.shape)
+    if len(dims) != 3 or tuple(density.shape) != dims:
+        raise RuntimeError("grad_output and density must be (X,Y,Z)")
+    if c > 0 and tuple(grad_feats_output.shape) != dims + (c,):
+        raise RuntimeError(f"grad_feats_output must be {dims + (c,)}")
+    m = g2t_tile_ids.numel()
+    f32 = dict(dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        sptr = ctypes.c_void_p(stream.cuda_stream)
+        if num_block_pairs is None:
+            num_block_pairs = backward_plan(valid_voxel_lb, valid_voxel_ub, dims, c) if c > 0 else 0
+        nbytes = ctypes.c_size_t()
+        _lib.check(lib.g2v_backward_workspace_size(n, m, int(num_block_pairs), _lib.i3(dims), c, ctypes.byref(nbytes)),
+                   "g2v_backward_workspace_size")
+        ws = _workspace(nbytes.value, dev)
+        grad_means = torch.empty((n, 3), **f32)
+        grad_cov = torch.empty((n, 9), **f32)
+        grad_op = torch.empty((n,), **f32)
+        grad_feats = torch.empty((n, c), **f32)
+        tb, te = (0, 0) if tile_x_range is None else (int(tile_x_range[0]), int(tile_x_range[1]))
+        if timing:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+        fptr = ctypes.c_void_p(features.data_ptr()) if features is not None else None
+        _lib.check(lib.g2v_backward(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None, _ptr(means3D),
+                                    _ptr(opacity), _ptr(cov_inv), fptr, n, c, _lib.f3(size_h), _lib.f6(range_h),
+                                    _lib.i3(dims), _ptr(valid_voxel_lb), _ptr(valid_voxel_ub), _ptr(g2t_offsets),
+                                    _ptr(g2t_tile_ids), m, int(num_block_pairs), _ptr(density), _ptr(grid_feats),
+                                    _ptr(grad_means), _ptr(grad_cov), _ptr(grad_op), _ptr(grad_feats), tb, te,
+                                    _ptr(ws), ws.numel(), sptr), "g2v_backward")
+        sec = 0.0
+        if timing:
+            ev1.record(stream)
+            ev1.synchronize()
+            sec = ev0.elapsed_time(ev1) / 1000.0
+    return grad_means, grad_cov, grad_op, grad_feats, sec

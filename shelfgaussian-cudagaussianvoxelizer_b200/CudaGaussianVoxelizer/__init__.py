@@ -1,0 +1,78 @@
+"""B200 Gaussian-to-voxel splatting, drop-in for the reference ``CudaGaussianVoxelizer`` package.
+
+    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer
+    voxelizer = PyCudaGaussianVoxelizer(voxel_size=[0.4] * 3, voxel_range=[-40, -40, -1, 40, 40, 5.4])
+    density, grid_feats, stats = voxelizer(means3D, opacity, covariances, features)
+
+Same module, autograd function, argument meaning, outputs and ``stats`` semantics as the reference's
+``CudaGaussianVoxelizer/__init__.py:10-47, 69-82``; the compute runs in libg2v.so (hand-written sm_100a
+kernels behind a C ABI, include/g2v.h).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _C, _lib
+from ._C import gaussian_voxelizer_backward, gaussian_voxelizer_forward
+
+_lib.load()  # fail loudly at import when the native library is missing
+
+__all__ = ["PyCudaGaussianVoxelizer", "_CudaGaussianVoxelizeFunction", "gaussian_voxelizer_forward",
+           "gaussian_voxelizer_backward", "_C"]
+
+
+class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
+    """Autograd function of the splat (reference CudaGaussianVoxelizer/__init__.py:10-47)."""
+
+    @staticmethod
+    def forward(ctx, means3D, opacity, covariances, voxel_size, voxel_range, features, timing=True):
+        (density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids,
+         fwd_sec) = gaussian_voxelizer_forward(means3D, opacity, covariances, voxel_size, voxel_range, features,
+                                               timing=timing)
+        stats = torch.zeros(2, dtype=torch.float32, device="cpu")
+        stats[0] = fwd_sec
+        ctx.save_for_backward(means3D, opacity, voxel_size, voxel_range, cov_inv, lb, ub, nvox, g2t_offsets,
+                              g2t_tile_ids, density, grid_feats, features, stats)
+        ctx.timing = timing
+        ctx.mark_non_differentiable(stats)
+        return density, grid_feats, stats
+
+    @staticmethod
+    def backward(ctx, grad_density_output, grad_feats_output, grad_stats):
+        (means3D, opacity, voxel_size, voxel_range, cov_inv, lb, ub, nvox, g2t_offsets, g2t_tile_ids, density,
+         grid_feats, features, stats) = ctx.saved_tensors
+        gout = grad_density_output.to(torch.float32).contiguous()
+        if features is not None and features.shape[1] > 0:
+            gfeat = grad_feats_output.to(torch.float32).contiguous()
+        else:
+            gfeat = grad_feats_output
+        grad_means, grad_cov, grad_op, grad_feats, bwd_sec = gaussian_voxelizer_backward(
+            gout, gfeat, means3D, opacity, cov_inv, voxel_size, voxel_range, lb, ub, nvox, g2t_offsets,
+            g2t_tile_ids, density, grid_feats, features, timing=ctx.timing)
+        stats[1] = bwd_sec
+        return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None)
+
+
+class PyCudaGaussianVoxelizer(nn.Module):
+    """Splat 3D Gaussians (and optional per-Gaussian features) into a dense voxel grid.
+
+    forward(means3D (N,3), opacity (N,), covariances (N,9), features (N,C) or None)
+        -> (density (X,Y,Z), grid_feats (X,Y,Z,C), stats (2,) CPU float32)
+    ``stats[0]`` is the forward device time in seconds, ``stats[1]`` the backward's (filled by
+    ``.backward()``).  ``timing=False`` skips the two end-of-call synchronisations that fill them
+    (stats stay 0).  Reference: CudaGaussianVoxelizer/__init__.py:69-82.
+    """
+
+    def __init__(self, voxel_size=[0.4, 0.4, 0.4], voxel_range=[-40, -40, -1, 40, 40, 5.4], timing: bool = True):
+        super().__init__()
+        self.voxel_size = torch.tensor(voxel_size, dtype=torch.float32, device="cuda")
+        self.voxel_range = torch.tensor(voxel_range, dtype=torch.float32, device="cuda")
+        self.timing = timing
+        # host copies: the C ABI takes the geometry by value, so no device read-back is needed
+        _C._host_values(self.voxel_size, 3, "voxel_size")
+        _C._host_values(self.voxel_range, 6, "voxel_range")
+
+    def forward(self, means3D, opacity, covariances, features=None):
+        return _CudaGaussianVoxelizeFunction.apply(means3D, opacity, covariances, self.voxel_size, self.voxel_range,
+                                                   features, self.timing)

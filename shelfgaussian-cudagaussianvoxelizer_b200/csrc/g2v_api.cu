@@ -1,0 +1,479 @@
+// g2v_api.cu -- the extern "C" entry points of libg2v.so (declared in include/g2v.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "g2v.h"
+#include "g2v_internal.cuh"
+
+namespace g2v {
+
+static thread_local char g_msg[512] = "";
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+    return G2V_ERROR_CUDA;
+}
+
+// implemented in the other translation units
+int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
+                     const int ncells_dim[3], int cell_x_begin, int cell_x_end, const int32_t* g2t_offsets,
+                     int32_t* g2t_tile_ids, int64_t g2t_cap, int32_t* per_gaussian, int32_t* counts, int32_t* cell_offsets,
+                     int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s);
+int count_gaussian_cells(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
+                         int32_t* per_gaussian, int32_t* dummy_counts, cudaStream_t s);
+int launch_splat_simt(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
+                      const int32_t* ub, const float* features, int C, const int32_t* tile_offsets,
+                      const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
+                      float* grid_feats, cudaStream_t s);
+int launch_spass(const float* grad_density, const float* grad_feats, const float* means, const float* opacity,
+                 const float* cov_inv, const int32_t* lb, const int32_t* ub, const float* features, int C,
+                 const float* density, const int32_t* g2t_offsets, const int32_t* tile_offsets,
+                 const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* partial10,
+                 int64_t pair_cap, cudaStream_t s);
+int launch_fpass(const float* grad_feats, const float* means, const float* opacity, const float* cov_inv,
+                 const int32_t* lb, const int32_t* ub, int C, const float* density, const int32_t* block_offsets,
+                 const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin, int nbx, int nby, int nbz,
+                 const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF, int64_t block_pair_cap,
+                 cudaStream_t s);
+int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
+                    const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
+                    float* grad_opacity, cudaStream_t s);
+int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const int32_t* lb, const int32_t* ub,
+                        int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
+                        cudaStream_t s);
+
+namespace {
+
+int make_grid(const float size[3], const float range[6], Grid& G) {
+    if (!size || !range) {
+        set_error("voxel_size / voxel_range must not be NULL");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    for (int a = 0; a < 3; ++a) {
+        // float32 host arithmetic, as src/cuda_gaussian_voxelizer.cu:1512-1514
+        const float q = (range[3 + a] - range[a]) / size[a];
+        if (!(q >= 1.0f) || !(q < 1073741824.0f)) {
+            set_error("invalid voxel grid along axis %d: (%g - %g) / %g", a, (double)range[3 + a], (double)range[a],
+                      (double)size[a]);
+            return G2V_ERROR_INVALID_VALUE;
+        }
+        G.r0[a] = range[a];
+        G.r1[a] = range[3 + a];
+        G.h[a] = size[a];
+        G.dims[a] = static_cast<int>(q);
+        G.tiles[a] = (G.dims[a] + kTile - 1) / kTile;
+    }
+    const int64_t ntiles = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
+    const int64_t nvox = (int64_t)G.dims[0] * G.dims[1] * G.dims[2];
+    if (ntiles > INT32_MAX / 2 || nvox > ((int64_t)1 << 40)) {
+        set_error("voxel grid %dx%dx%d is too large", G.dims[0], G.dims[1], G.dims[2]);
+        return G2V_ERROR_SIZE_LIMIT;
+    }
+    return 0;
+}
+
+int check_slab(const Grid& G, int& tx_begin, int& tx_end) {
+    if (tx_begin == 0 && tx_end == 0) tx_end = G.tiles[0];
+    if (tx_begin < 0 || tx_end > G.tiles[0] || tx_begin > tx_end) {
+        set_error("tile x range [%d, %d) is outside [0, %d)", tx_begin, tx_end, G.tiles[0]);
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return 0;
+}
+
+// Blocks of tiles used by the feature-gradient pass.
+void block_shape(const Grid& G, int B[3], int nb[3]) {
+    B[0] = 2;
+    B[1] = 2;
+    B[2] = G.tiles[2] < 4 ? G.tiles[2] : 4;
+    for (int a = 0; a < 3; ++a) nb[a] = (G.tiles[a] + B[a] - 1) / B[a];
+}
+
+struct PrepareWs {
+    int32_t* ntiles;
+    void* scan;
+    int64_t* total;
+};
+size_t carve_prepare(void* p, int64_t n, PrepareWs& w) {
+    Carver c(p);
+    w.ntiles = c.take<int32_t>((size_t)(n > 0 ? n : 1));
+    w.scan = c.take<char>(scan_workspace_bytes(n));
+    w.total = c.take<int64_t>(1);
+    return c.bytes();
+}
+
+// The Tile->Gaussian part comes first so that its offsets depend only on (tiles, M).
+struct T2GWs {
+    int32_t* tile_offsets;
+    int32_t* lists;
+    int32_t* unsorted;
+    int32_t* counts;
+    void* scan;
+    int64_t* total;
+};
+void carve_t2g(Carver& c, int64_t ntiles, int64_t m, T2GWs& w) {
+    w.tile_offsets = c.take<int32_t>((size_t)ntiles + 1);
+    w.lists = c.take<int32_t>((size_t)(m > 0 ? m : 1));
+    w.unsorted = c.take<int32_t>((size_t)(m > 0 ? m : 1));
+    w.counts = c.take<int32_t>((size_t)(ntiles > 0 ? ntiles : 1));
+    w.scan = c.take<char>(scan_workspace_bytes(ntiles));
+    w.total = c.take<int64_t>(1);
+}
+
+struct BackwardWs {
+    T2GWs t2g;
+    int32_t* g2b_counts;
+    int32_t* g2b_offsets;
+    int32_t* block_offsets;
+    int32_t* block_lists;
+    int32_t* block_unsorted;
+    int32_t* block_counts;
+    void* block_scan;
+    void* g_scan;
+    float* partial10;
+    float* partialF;
+};
+size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, int64_t C, BackwardWs& w) {
+    Carver c(p);
+    const int64_t ntiles = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
+    carve_t2g(c, ntiles, m, w.t2g);
+    int B[3], nb[3];
+    block_shape(G, B, nb);
+    const int64_t nblocks = (int64_t)nb[0] * nb[1] * nb[2];
+    const bool feats = C > 0;
+    w.g2b_counts = c.take<int32_t>((size_t)(feats ? (n > 0 ? n : 1) : 1));
+    w.g2b_offsets = c.take<int32_t>((size_t)(feats ? n + 1 : 1));
+    w.block_offsets = c.take<int32_t>((size_t)(feats ? nblocks + 1 : 1));
+    w.block_lists = c.take<int32_t>((size_t)(feats && mb > 0 ? mb : 1));
+    w.block_unsorted = c.take<int32_t>((size_t)(feats && mb > 0 ? mb : 1));
+    w.block_counts = c.take<int32_t>((size_t)(feats ? nblocks : 1));
+    w.block_scan = c.take<char>(scan_workspace_bytes(feats ? nblocks : 1));
+    w.g_scan = c.take<char>(scan_workspace_bytes(feats ? n : 1));
+    w.partial10 = c.take<float>((size_t)(m > 0 ? m : 1) * 10);
+    w.partialF = c.take<float>((size_t)(feats && mb > 0 ? mb : 1) * (size_t)(feats ? C : 1));
+    return c.bytes();
+}
+
+struct PlanWs {
+    int32_t* counts;
+    int32_t* offsets;
+    int32_t* dummy;
+    void* scan;
+    int64_t* total;
+};
+size_t carve_plan(void* p, int64_t n, PlanWs& w) {
+    Carver c(p);
+    w.counts = c.take<int32_t>((size_t)(n > 0 ? n : 1));
+    w.offsets = c.take<int32_t>((size_t)n + 1);
+    w.dummy = c.take<int32_t>(1);
+    w.scan = c.take<char>(scan_workspace_bytes(n));
+    w.total = c.take<int64_t>(1);
+    return c.bytes();
+}
+
+int need_ws(size_t need, size_t have, const void* ws) {
+    if (have < need || (need > 0 && ws == nullptr)) {
+        set_error("workspace of %zu bytes is smaller than the %zu bytes required", have, need);
+        return G2V_ERROR_WORKSPACE_TOO_SMALL;
+    }
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+        set_error("workspace must be 256-byte aligned");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return 0;
+}
+
+}  // namespace
+}  // namespace g2v
+
+using namespace g2v;
+
+extern "C" {
+
+int g2v_abi_version(void) { return G2V_ABI_VERSION; }
+
+const char* g2v_status_string(int status) {
+    switch (status) {
+        case G2V_SUCCESS: return "G2V_SUCCESS";
+        case G2V_ERROR_INVALID_VALUE: return "G2V_ERROR_INVALID_VALUE";
+        case G2V_ERROR_WORKSPACE_TOO_SMALL: return "G2V_ERROR_WORKSPACE_TOO_SMALL";
+        case G2V_ERROR_SIZE_LIMIT: return "G2V_ERROR_SIZE_LIMIT";
+        case G2V_ERROR_CUDA: return "G2V_ERROR_CUDA";
+        case G2V_ERROR_NOT_SUPPORTED: return "G2V_ERROR_NOT_SUPPORTED";
+        default: return "G2V_UNKNOWN_STATUS";
+    }
+}
+
+const char* g2v_last_error(void) { return g_msg; }
+
+int g2v_grid_shape(const float voxel_size[3], const float voxel_range[6], int dims[3], int tiles[3]) {
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    for (int a = 0; a < 3; ++a) {
+        if (dims) dims[a] = G.dims[a];
+        if (tiles) tiles[a] = G.tiles[a];
+    }
+    return G2V_SUCCESS;
+}
+
+int g2v_forward_prepare_workspace_size(int64_t num_gaussians, size_t* bytes) {
+    if (!bytes || num_gaussians < 0) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    PrepareWs w;
+    *bytes = carve_prepare(nullptr, num_gaussians, w);
+    return G2V_SUCCESS;
+}
+
+int g2v_forward_prepare(const float* means3d, const float* covariances, int64_t num_gaussians,
+                        const float voxel_size[3], const float voxel_range[6], float* cov_inv,
+                        int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
+                        int32_t* g2t_offsets, void* workspace, size_t workspace_bytes, void* stream,
+                        int64_t* num_pairs) {
+    g_msg[0] = 0;
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if (num_gaussians < 0 || num_gaussians > INT32_MAX - 1 || !g2t_offsets || !num_pairs ||
+        (num_gaussians > 0 && (!means3d || !covariances || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
+                               !num_voxels))) {
+        set_error("g2v_forward_prepare: invalid pointer or Gaussian count");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    PrepareWs w;
+    const size_t need = carve_prepare(nullptr, num_gaussians, w);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    carve_prepare(workspace, num_gaussians, w);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((rc = launch_prepare_boxes(means3d, covariances, num_gaussians, G, cov_inv, valid_voxel_lb, valid_voxel_ub,
+                                   num_voxels, w.ntiles, s)))
+        return rc;
+    if ((rc = launch_exclusive_scan(w.ntiles, num_gaussians, g2t_offsets, w.total, w.scan, s))) return rc;
+    int64_t m = 0;
+    G2V_CUDA(cudaMemcpyAsync(&m, w.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    G2V_CUDA(cudaStreamSynchronize(s));
+    if (m > INT32_MAX) {
+        set_error("%lld (Gaussian, tile) pairs exceed the int32 range of the Gaussian->Tile map", (long long)m);
+        return G2V_ERROR_SIZE_LIMIT;
+    }
+    *num_pairs = m;
+    return G2V_SUCCESS;
+}
+
+int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3],
+                                     int64_t channels, size_t* bytes) {
+    if (!bytes || !dims || num_gaussians < 0 || num_pairs < 0 || channels < 0) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    const int64_t ntiles = (int64_t)((dims[0] + 3) / 4) * ((dims[1] + 3) / 4) * ((dims[2] + 3) / 4);
+    Carver c(nullptr);
+    T2GWs w;
+    carve_t2g(c, ntiles, num_pairs, w);
+    *bytes = c.bytes();
+    return G2V_SUCCESS;
+}
+
+int g2v_forward_splat(const float* means3d, const float* opacity, const float* features, int64_t num_gaussians,
+                      int64_t channels, const float voxel_size[3], const float voxel_range[6],
+                      const float* cov_inv, const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub,
+                      const int32_t* g2t_offsets, int64_t num_pairs, int32_t* g2t_tile_ids, float* density,
+                      float* grid_feats, int tile_x_begin, int tile_x_end, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    g_msg[0] = 0;
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if ((rc = check_slab(G, tile_x_begin, tile_x_end))) return rc;
+    const int C = features ? (int)channels : 0;
+    if (num_gaussians < 0 || num_pairs < 0 || channels < 0 || channels > INT32_MAX / 2 || !density ||
+        !g2t_offsets || (num_pairs > 0 && !g2t_tile_ids) || (features && channels > 0 && !grid_feats) ||
+        (num_gaussians > 0 && (!means3d || !opacity || !cov_inv || !valid_voxel_lb || !valid_voxel_ub))) {
+        set_error("g2v_forward_splat: invalid pointer or size");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    size_t need = 0;
+    g2v_forward_splat_workspace_size(num_gaussians, num_pairs, G.dims, channels, &need);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    Carver c(workspace);
+    T2GWs w;
+    const int64_t ntiles_all = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
+    carve_t2g(c, ntiles_all, num_pairs, w);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int one[3] = {1, 1, 1};
+    if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
+                               tile_x_end, g2t_offsets, g2t_tile_ids, num_pairs, nullptr, w.counts, w.tile_offsets, w.unsorted,
+                               w.lists, w.scan, w.total, s)))
+        return rc;
+    const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
+    const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
+    return launch_splat_simt(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, C, w.tile_offsets,
+                             w.lists, first_tile, nt, G, density, grid_feats, s);
+}
+
+int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs, const int dims[3],
+                       int32_t* tile_offsets, int32_t* t2g_gaussians, void* stream) {
+    (void)num_gaussians;
+    if (!splat_workspace || !dims || !tile_offsets || (num_pairs > 0 && !t2g_gaussians)) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    const int64_t ntiles = (int64_t)((dims[0] + 3) / 4) * ((dims[1] + 3) / 4) * ((dims[2] + 3) / 4);
+    Carver c(const_cast<void*>(splat_workspace));
+    T2GWs w;
+    carve_t2g(c, ntiles, num_pairs, w);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    G2V_CUDA(cudaMemcpyAsync(tile_offsets, w.tile_offsets, sizeof(int32_t) * (size_t)(ntiles + 1),
+                             cudaMemcpyDeviceToDevice, s));
+    if (num_pairs > 0)
+        G2V_CUDA(cudaMemcpyAsync(t2g_gaussians, w.lists, sizeof(int32_t) * (size_t)num_pairs,
+                                 cudaMemcpyDeviceToDevice, s));
+    return G2V_SUCCESS;
+}
+
+int g2v_backward_plan_workspace_size(int64_t num_gaussians, size_t* bytes) {
+    if (!bytes || num_gaussians < 0) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    PlanWs w;
+    *bytes = carve_plan(nullptr, num_gaussians, w);
+    return G2V_SUCCESS;
+}
+
+int g2v_backward_plan(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, int64_t num_gaussians,
+                      const int dims[3], int64_t channels, void* workspace, size_t workspace_bytes, void* stream,
+                      int64_t* num_block_pairs) {
+    g_msg[0] = 0;
+    if (!dims || !num_block_pairs || num_gaussians < 0 || channels < 0 ||
+        (num_gaussians > 0 && (!valid_voxel_lb || !valid_voxel_ub))) {
+        set_error("g2v_backward_plan: invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    if (channels == 0 || num_gaussians == 0) {
+        *num_block_pairs = 0;
+        return G2V_SUCCESS;
+    }
+    Grid G{};
+    for (int a = 0; a < 3; ++a) {
+        G.dims[a] = dims[a];
+        G.tiles[a] = (dims[a] + 3) / 4;
+    }
+    PlanWs w;
+    int rc;
+    const size_t need = carve_plan(nullptr, num_gaussians, w);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    carve_plan(workspace, num_gaussians, w);
+    int B[3], nb[3];
+    block_shape(G, B, nb);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((rc = count_gaussian_cells(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, B, w.counts, w.dummy, s)))
+        return rc;
+    if ((rc = launch_exclusive_scan(w.counts, num_gaussians, w.offsets, w.total, w.scan, s))) return rc;
+    int64_t mb = 0;
+    G2V_CUDA(cudaMemcpyAsync(&mb, w.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    G2V_CUDA(cudaStreamSynchronize(s));
+    if (mb > INT32_MAX) {
+        set_error("%lld (Gaussian, block) pairs exceed the int32 range", (long long)mb);
+        return G2V_ERROR_SIZE_LIMIT;
+    }
+    *num_block_pairs = mb;
+    return G2V_SUCCESS;
+}
+
+int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs, int64_t num_block_pairs,
+                                const int dims[3], int64_t channels, size_t* bytes) {
+    if (!bytes || !dims || num_gaussians < 0 || num_pairs < 0 || num_block_pairs < 0 || channels < 0) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    Grid G{};
+    for (int a = 0; a < 3; ++a) {
+        G.dims[a] = dims[a];
+        G.tiles[a] = (dims[a] + 3) / 4;
+    }
+    BackwardWs w;
+    *bytes = carve_backward(nullptr, num_gaussians, num_pairs, num_block_pairs, G, channels, w);
+    return G2V_SUCCESS;
+}
+
+int g2v_backward(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                 const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
+                 int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                 const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                 const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs, const float* density,
+                 const float* grid_feats, float* grad_means3d, float* grad_covariances, float* grad_opacity,
+                 float* grad_features, int tile_x_begin, int tile_x_end, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+    (void)grid_feats;
+    g_msg[0] = 0;
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if (!dims || dims[0] != G.dims[0] || dims[1] != G.dims[1] || dims[2] != G.dims[2]) {
+        set_error("g2v_backward: dims do not match the voxel grid %dx%dx%d", G.dims[0], G.dims[1], G.dims[2]);
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    if ((rc = check_slab(G, tile_x_begin, tile_x_end))) return rc;
+    const int C = features ? (int)channels : 0;
+    if (num_gaussians < 0 || num_pairs < 0 || channels < 0 || channels > INT32_MAX / 2 || num_block_pairs < 0 ||
+        !grad_density || !density || !g2t_offsets || (num_pairs > 0 && !g2t_tile_ids) ||
+        (C > 0 && !grad_grid_feats) || (C > 0 && num_gaussians > 0 && !grad_features) ||
+        (num_gaussians > 0 && (!means3d || !opacity || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
+                               !grad_means3d || !grad_covariances || !grad_opacity))) {
+        set_error("g2v_backward: invalid pointer or size");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    BackwardWs w;
+    const size_t need = carve_backward(nullptr, num_gaussians, num_pairs, num_block_pairs, G, C, w);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    carve_backward(workspace, num_gaussians, num_pairs, num_block_pairs, G, C, w);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int one[3] = {1, 1, 1};
+    if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
+                               tile_x_end, g2t_offsets, nullptr, 0, nullptr, w.t2g.counts, w.t2g.tile_offsets,
+                               w.t2g.unsorted, w.t2g.lists, w.t2g.scan, w.t2g.total, s)))
+        return rc;
+    const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
+    const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
+    if ((rc = launch_spass(grad_density, grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub,
+                           features, C, density, g2t_offsets, w.t2g.tile_offsets, w.t2g.lists, first_tile, nt, G,
+                           w.partial10, num_pairs, s)))
+        return rc;
+    if ((rc = launch_reduce10(w.partial10, g2t_offsets, g2t_tile_ids, num_gaussians, G, tile_x_begin, tile_x_end,
+                              grad_means3d, grad_covariances, grad_opacity, s)))
+        return rc;
+    if (C > 0 && num_gaussians > 0) {
+        int B[3], nb[3];
+        block_shape(G, B, nb);
+        const int bx_begin = tile_x_begin / B[0];
+        const int bx_end = (tile_x_end + B[0] - 1) / B[0];
+        int64_t* total = w.t2g.total;
+        // per-Gaussian block counts, then the offsets of the partial rows
+        if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, B, nb, bx_begin, bx_end,
+                                   nullptr, nullptr, 0, w.g2b_counts, w.block_counts, w.block_offsets,
+                                   w.block_unsorted, w.block_lists, w.block_scan, total, s)))
+            return rc;
+        if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s))) return rc;
+        if ((rc = launch_fpass(grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, C, density,
+                               w.block_offsets, w.block_lists, w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1],
+                               nb[2], B, tile_x_begin, tile_x_end, G, w.partialF, num_block_pairs, s)))
+            return rc;
+        if ((rc = launch_reduce_feats(w.partialF, w.g2b_offsets, valid_voxel_lb, valid_voxel_ub, num_gaussians, C, B,
+                                      bx_begin, bx_end, grad_features, s)))
+            return rc;
+    }
+    return G2V_SUCCESS;
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+// g2v_internal.cuh -- shared constants, device helpers and host plumbing of libg2v.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstddef>
+
+namespace g2v {
+
+constexpr int kTile = 4;                          // tile edge in voxels (reference include/utils.cuh:50-52)
+constexpr int kVoxPerTile = kTile * kTile * kTile;  // 64
+constexpr float kEps = 1e-6f;                     // density clamp of the normalisation (utils.cuh:80)
+
+// ---------------------------------------------------------------------------------------------
+// Grid geometry passed by value to kernels.
+struct Grid {
+    float r0[3];     // range origin
+    float r1[3];     // range end
+    float h[3];      // voxel size
+    int dims[3];     // X, Y, Z voxels
+    int tiles[3];    // Tx, Ty, Tz tiles
+};
+
+// Voxel centre along one axis: origin + (i + 1/2) * h (reference cu:825-828).
+__device__ __forceinline__ float voxel_centre(const Grid& G, int a, int i) {
+    return G.r0[a] + (static_cast<float>(i) + 0.5f) * G.h[a];
+}
+
+// Local voxel index inside a tile, x-major: lv = (lx*4 + ly)*4 + lz (reference DecodeTileVoxel cu:1226).
+__device__ __forceinline__ void local_voxel(int lv, int& lx, int& ly, int& lz) {
+    lx = lv >> 4;
+    ly = (lv >> 2) & 3;
+    lz = lv & 3;
+}
+
+__device__ __forceinline__ void decode_tile(int tile, const Grid& G, int& tx, int& ty, int& tz) {
+    const int tyz = G.tiles[1] * G.tiles[2];
+    tx = tile / tyz;
+    const int r = tile - tx * tyz;
+    ty = r / G.tiles[2];
+    tz = r - ty * G.tiles[2];
+}
+
+// Tile box of a Gaussian from its voxel box; empty (returns false) when the voxel box is empty.
+__device__ __forceinline__ bool tile_box(const int32_t* lb, const int32_t* ub, int64_t g, int lo[3], int hi[3]) {
+    bool ok = true;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+        const int l = lb[g * 3 + a], u = ub[g * 3 + a];
+        ok = ok && (u >= l);
+        lo[a] = l / kTile;
+        hi[a] = u / kTile;
+    }
+    return ok;
+}
+
+// exp(-1/2 d^T P d) with d = centre - mean and q = P d; returns the exponential, writes q.
+__device__ __forceinline__ float eval_gaussian(const float* c, float dx, float dy, float dz, float& qx, float& qy,
+                                               float& qz) {
+    qx = c[0] * dx + c[1] * dy + c[2] * dz;
+    qy = c[3] * dx + c[4] * dy + c[5] * dz;
+    qz = c[6] * dx + c[7] * dy + c[8] * dz;
+    const float maha = dx * qx + dy * qy + dz * qz;
+    return __expf(-0.5f * maha);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side: workspace carving (256-byte aligned sub-buffers of one caller-provided block).
+struct Carver {
+    char* base;
+    size_t off = 0;
+    explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+    template <typename T>
+    T* take(size_t count) {
+        off = (off + 255) & ~size_t(255);
+        T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+        off += count * sizeof(T);
+        return p;
+    }
+    size_t bytes() const { return (off + 255) & ~size_t(255); }
+};
+
+// Error reporting (defined in g2v_api.cu).
+void set_error(const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define G2V_LAUNCH_CHECK(what)                                  \
+    do {                                                        \
+        cudaError_t _e = cudaGetLastError();                    \
+        if (_e != cudaSuccess) return ::g2v::cuda_fail(_e, what); \
+    } while (0)
+
+#define G2V_CUDA(call)                                          \
+    do {                                                        \
+        cudaError_t _e = (call);                                \
+        if (_e != cudaSuccess) return ::g2v::cuda_fail(_e, #call); \
+    } while (0)
+
+// ---------------------------------------------------------------------------------------------
+// Launchers implemented in the .cu files (all return a g2v_status code).
+int launch_prepare_boxes(const float* means, const float* cov, int64_t n, const Grid& G, float* cov_inv,
+                         int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s);
+
+size_t scan_workspace_bytes(int64_t n);
+// Exclusive prefix sum of n int32 counts into out[0..n] (out[n] = total).  Fails with
+// G2V_ERROR_SIZE_LIMIT when the total does not fit int32.  `total` (device, int64) receives the sum.
+int launch_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_t* total, void* ws,
+                          cudaStream_t s);
+
+}  // namespace g2v
+
+// ---------------------------------------------------------------------------------------------
+// Optional per-kernel timing (g2v_profile_enable): CUDA events recorded on the launch stream around
+// every kernel launch, aggregated by kernel name when read back.  Off by default.
+namespace g2v {
+extern volatile int g_profiling;
+int prof_start(const char* name, cudaStream_t s);
+void prof_stop(int slot, cudaStream_t s);
+}  // namespace g2v
+
+#define G2V_TIMED(name, stream, ...)                                           \
+    do {                                                                       \
+        const int _slot = ::g2v::g_profiling ? ::g2v::prof_start(name, stream) : -1; \
+        __VA_ARGS__;                                                           \
+        if (_slot >= 0) ::g2v::prof_stop(_slot, stream);                       \
+    } while (0)
