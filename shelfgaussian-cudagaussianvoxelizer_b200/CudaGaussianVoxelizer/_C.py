@@ -8,6 +8,7 @@ it a workspace tensor.  Failures raise ``RuntimeError`` (never exit the process)
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import torch
 
@@ -15,26 +16,38 @@ from . import _lib
 
 __all__ = ["gaussian_voxelizer_forward", "gaussian_voxelizer_backward", "grid_shape", "t2g_maps"]
 
+# id(tensor) -> (weakref to the tensor, its _version, host values).  The weak reference makes sure a
+# hit is the same live tensor object (an address or id can be reused after a tensor is freed).
 _geom_cache: dict = {}
 
 
 def _host_values(t, n: int, name: str):
-    """Host floats of voxel_size / voxel_range; tensors are read once and cached by storage + version."""
+    """Host floats of voxel_size / voxel_range; a tensor is read back once per (object, version)."""
     if isinstance(t, torch.Tensor):
         if t.numel() != n:
             raise RuntimeError(f"{name} must have {n} elements, got {t.numel()}")
-        key = (name, t.device, t.data_ptr(), t._version, t.dtype)
-        v = _geom_cache.get(key)
-        if v is None:
-            v = tuple(float(x) for x in t.detach().to("cpu", torch.float32).tolist())
-            if len(_geom_cache) > 64:
-                _geom_cache.clear()
-            _geom_cache[key] = v
+        hit = _geom_cache.get(id(t))
+        if hit is not None and hit[0]() is t and hit[1] == t._version:
+            return hit[2]
+        v = tuple(float(x) for x in t.detach().to("cpu", torch.float32).tolist())
+        if len(_geom_cache) > 256:
+            for k in [k for k, e in _geom_cache.items() if e[0]() is None]:
+                del _geom_cache[k]
+        _geom_cache[id(t)] = (weakref.ref(t), t._version, v)
         return v
     v = tuple(float(x) for x in t)
     if len(v) != n:
         raise RuntimeError(f"{name} must have {n} elements, got {len(v)}")
     return v
+
+
+def _features_ptr(features, fallback):
+    """Pointer for the C ABI's features argument.  NULL selects the density-only path, so a given but
+    empty tensor (whose data_ptr() is 0) is passed as a non-NULL address the library never reads."""
+    if features is None:
+        return None
+    p = features.data_ptr()
+    return ctypes.c_void_p(p if p else fallback.data_ptr())
 
 
 def _ptr(t):
@@ -117,8 +130,7 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
         _lib.check(lib.g2v_forward_splat_workspace_size(n, m, _lib.i3((X, Y, Z)), c, ctypes.byref(nbytes)),
                    "g2v_forward_splat_workspace_size")
         ws2 = _workspace(nbytes.value, dev)
-        _lib.check(lib.g2v_forward_splat(_ptr(means3D), _ptr(opacity),
-                                         ctypes.c_void_p(features.data_ptr()) if features is not None else None,
+        _lib.check(lib.g2v_forward_splat(_ptr(means3D), _ptr(opacity), _features_ptr(features, density),
                                          n, c, _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub),
                                          _ptr(g2t_offsets), m, _ptr(g2t_tile_ids), _ptr(density), _ptr(grid_feats),
                                          0, 0, _ptr(ws2), ws2.numel(), sptr), "g2v_forward_splat")
@@ -227,7 +239,7 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record(stream)
-        fptr = ctypes.c_void_p(features.data_ptr()) if features is not None else None
+        fptr = _features_ptr(features, grad_op if grad_op.numel() else density)
         _lib.check(lib.g2v_backward(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None, _ptr(means3D),
                                     _ptr(opacity), _ptr(cov_inv), fptr, n, c, _lib.f3(size_h), _lib.f6(range_h),
                                     _lib.i3(dims), _ptr(valid_voxel_lb), _ptr(valid_voxel_ub), _ptr(g2t_offsets),

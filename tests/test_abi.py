@@ -104,3 +104,20 @@ def test_python_api_rejects_cpu_tensors():
     with pytest.raises(RuntimeError, match="scalar type"):
         _C.gaussian_voxelizer_forward(m.double(), torch.zeros(4), torch.zeros(4, 9), [0.4] * 3,
                                       [-4, -4, -1, 4, 4, 2.2])
+
+
+def test_geometry_cache_never_serves_a_freed_tensor():
+    """Host copies of voxel_size/voxel_range are cached per live tensor object; a new tensor that reuses
+    the address (or id) of a freed one must be read again."""
+    import gc
+    import torch
+    from CudaGaussianVoxelizer import _C
+    for i in range(50):
+        t = torch.tensor([0.4, 0.4, 0.1 * (i + 1)])
+        assert _C._host_values(t, 3, "voxel_size")[2] == pytest.approx(0.1 * (i + 1), rel=1e-6)
+        del t
+        gc.collect()
+    t = torch.tensor([1.0, 2.0, 3.0])
+    assert _C._host_values(t, 3, "voxel_size") == (1.0, 2.0, 3.0)
+    t.mul_(2)  # in-place change bumps the version
+    assert _C._host_values(t, 3, "voxel_size") == (2.0, 4.0, 6.0)
