@@ -78,6 +78,22 @@ G2V_API int g2v_forward_prepare(const float* means3d, const float* covariances, 
                         int32_t* g2t_offsets, void* workspace, size_t workspace_bytes, void* stream,
                         int64_t* num_pairs);
 
+/*
+ * Forward, stage 1, for callers that cannot allocate device memory (no counterpart in the reference).
+ * Same inputs, outputs and single stream synchronisation as g2v_forward_prepare, but no workspace: some
+ * callers cannot provide one -- e.g. a serving process that reserves all device memory at start-up and
+ * must not call cudaMalloc afterwards, or a plugin whose host application owns every device allocation.
+ * The scratch is a fixed array of about 1 MiB in the library's own device memory, so inputs are limited
+ * to G2V_STATIC_MAX_GAUSSIANS Gaussians (larger inputs fail with G2V_ERROR_SIZE_LIMIT).  The first call
+ * on a device looks up that array's address (call it once before any stream capture); all calls share
+ * the array, so calls that overlap on the GPU race.
+ */
+#define G2V_STATIC_MAX_GAUSSIANS 262144
+G2V_API int g2v_forward_prepare_static(const float* means3d, const float* covariances, int64_t num_gaussians,
+                                       const float voxel_size[3], const float voxel_range[6], float* cov_inv,
+                                       int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
+                                       int32_t* g2t_offsets, void* stream, int64_t* num_pairs);
+
 /* Workspace of g2v_forward_splat. */
 G2V_API int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3],
                                      int64_t channels, size_t* bytes);

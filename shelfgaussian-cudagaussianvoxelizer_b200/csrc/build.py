@@ -31,6 +31,7 @@ SOURCES = {
     "g2v_splat.cu": [],
     "g2v_grad.cu": [],
     "g2v_profile.cu": [],
+    "g2v_static.cu": [],
 }
 HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(INCLUDE, "g2v.h")]
 
