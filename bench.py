@@ -40,6 +40,8 @@ CONFIGS = {
     "cfg3": dict(n=18000, c=1024, size=0.4, range=RANGE, var_max=2.5, expand=0.0),
     "cfg4": dict(n=18000, c=1024, size=0.4, range=RANGE, var_max=2.5, expand=0.05),
     "cfg5": dict(n=100000, c=256, size=0.2, range=RANGE, var_max=8.0, expand=0.0),
+    # test_reference.py's forward shape; small enough for multi-pass ncu captures (grid_feats 328 MB > L2)
+    "small128": dict(n=18000, c=128, size=0.4, range=RANGE, var_max=2.5, expand=0.0),
 }
 METRIC = "G2V fwd+bwd ms/step (18k Gaussians, 1024-D, 200×200×16) and % HBM roofline"
 
