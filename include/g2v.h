@@ -163,6 +163,15 @@ G2V_API int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussian
                        const int dims[3], int32_t* tile_offsets, int32_t* t2g_gaussians, void* stream);
 
 /*
+ * Device error word (no reference counterpart): the tensor-core kernels never spin without a bound;
+ * a wait that gives up sets a bit in a per-device word instead of hanging.  g2v_forward_prepare and
+ * g2v_backward_plan read the word at the synchronisation they already do and fail with
+ * G2V_ERROR_CUDA if it is set.  This call reads it explicitly (synchronising `stream`), returns it in
+ * *word and clears it.
+ */
+G2V_API int g2v_device_error(void* stream, int* word);
+
+/*
  * Profiling hook (no reference counterpart): when enabled, every kernel launch of the library is
  * bracketed by CUDA events on its launch stream.  g2v_profile_enable(1) clears the records and starts
  * recording, g2v_profile_enable(0) stops.  g2v_profile_read(i, ...) waits for the recorded events,

@@ -32,8 +32,10 @@ SOURCES = {
     "g2v_grad.cu": [],
     "g2v_profile.cu": [],
     "g2v_static.cu": [],
+    "g2v_splat_tc.cu": [],
 }
-HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(INCLUDE, "g2v.h")]
+HEADERS_TC = ["g2v_tc.cuh"]
+HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(HERE, "g2v_tc.cuh"), os.path.join(INCLUDE, "g2v.h")]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

@@ -1,7 +1,9 @@
 // g2v_api.cu -- the extern "C" entry points of libg2v.so (declared in include/g2v.h).
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "g2v.h"
 #include "g2v_internal.cuh"
@@ -33,6 +35,11 @@ int launch_splat_simt(const float* means, const float* opacity, const float* cov
                       const int32_t* ub, const float* features, int C, const int32_t* tile_offsets,
                       const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
                       float* grid_feats, cudaStream_t s);
+int launch_splat_tc(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
+                    const int32_t* ub, const float* features, int64_t n, int C, const int32_t* tile_offsets,
+                    const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
+                    float* grid_feats, void* split, int* err, cudaStream_t s);
+size_t splat_tc_split_bytes(int64_t n, int64_t C);
 int launch_spass(const float* grad_density, const float* grad_feats, const float* means, const float* opacity,
                  const float* cov_inv, const int32_t* lb, const int32_t* ub, const float* features, int C,
                  const float* density, const int32_t* g2t_offsets, const int32_t* tile_offsets,
@@ -50,7 +57,57 @@ int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const
                         int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
                         cudaStream_t s);
 
+// Device error word: kernels with bounded waits set bits here when a wait gives up.  It is read (and
+// cleared) at the synchronisation points the API already has (g2v_forward_prepare, g2v_backward_plan)
+// and by g2v_device_error().
+__device__ int g_device_error_word = 0;
+
 namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_err_mu;
+int* g_err_ptr[kMaxDevices] = {nullptr};
+
+int device_error_ptr(int** out) {
+    int dev = 0;
+    G2V_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("device ordinal %d out of range", dev);
+        return G2V_ERROR_NOT_SUPPORTED;
+    }
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    if (!g_err_ptr[dev]) {
+        void* p = nullptr;
+        G2V_CUDA(cudaGetSymbolAddress(&p, g_device_error_word));
+        g_err_ptr[dev] = static_cast<int*>(p);
+    }
+    *out = g_err_ptr[dev];
+    return 0;
+}
+
+// Reads the error word with the caller's stream (the caller synchronises), queued before the sync.
+int queue_error_read(cudaStream_t s, int* host_word) {
+    int* p = nullptr;
+    int rc = device_error_ptr(&p);
+    if (rc) return rc;
+    G2V_CUDA(cudaMemcpyAsync(host_word, p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    return 0;
+}
+
+int report_device_error(int word, cudaStream_t s) {
+    if (word == 0) return 0;
+    int* p = nullptr;
+    if (device_error_ptr(&p) == 0) cudaMemsetAsync(p, 0, sizeof(int), s);
+    set_error("a kernel's bounded wait gave up (device error word 0x%x); results of the preceding calls are "
+              "invalid", word);
+    return G2V_ERROR_CUDA;
+}
+
+// Kernel variant: the tensor-core path unless G2V_VARIANT=simt.
+bool use_tensor_cores() {
+    const char* v = getenv("G2V_VARIANT");
+    return !(v && strcmp(v, "simt") == 0);
+}
 
 int make_grid(const float size[3], const float range[6], Grid& G) {
     if (!size || !range) {
@@ -260,8 +317,11 @@ int g2v_forward_prepare(const float* means3d, const float* covariances, int64_t 
         return rc;
     if ((rc = launch_exclusive_scan(w.ntiles, num_gaussians, g2t_offsets, w.total, w.scan, s))) return rc;
     int64_t m = 0;
+    int word = 0;
     G2V_CUDA(cudaMemcpyAsync(&m, w.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    if ((rc = queue_error_read(s, &word))) return rc;
     G2V_CUDA(cudaStreamSynchronize(s));
+    if ((rc = report_device_error(word, s))) return rc;
     if (m > INT32_MAX) {
         set_error("%lld (Gaussian, tile) pairs exceed the int32 range of the Gaussian->Tile map", (long long)m);
         return G2V_ERROR_SIZE_LIMIT;
@@ -280,6 +340,7 @@ int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, c
     Carver c(nullptr);
     T2GWs w;
     carve_t2g(c, ntiles, num_pairs, w);
+    c.take<char>(splat_tc_split_bytes(num_gaussians, channels));
     *bytes = c.bytes();
     return G2V_SUCCESS;
 }
@@ -317,6 +378,13 @@ int g2v_forward_splat(const float* means3d, const float* opacity, const float* f
         return rc;
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
+    if (features != nullptr && C > 0 && use_tensor_cores()) {
+        void* split = c.take<char>(splat_tc_split_bytes(num_gaussians, C));
+        int* err = nullptr;
+        if ((rc = device_error_ptr(&err))) return rc;
+        return launch_splat_tc(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, num_gaussians, C,
+                               w.tile_offsets, w.lists, first_tile, nt, G, density, grid_feats, split, err, s);
+    }
     return launch_splat_simt(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, C, w.tile_offsets,
                              w.lists, first_tile, nt, G, density, grid_feats, s);
 }
@@ -338,6 +406,22 @@ int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64
     if (num_pairs > 0)
         G2V_CUDA(cudaMemcpyAsync(t2g_gaussians, w.lists, sizeof(int32_t) * (size_t)num_pairs,
                                  cudaMemcpyDeviceToDevice, s));
+    return G2V_SUCCESS;
+}
+
+int g2v_device_error(void* stream, int* word) {
+    if (!word) {
+        set_error("word must not be NULL");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int rc = queue_error_read(s, word);
+    if (rc) return rc;
+    G2V_CUDA(cudaStreamSynchronize(s));
+    if (*word) {
+        int* p = nullptr;
+        if (device_error_ptr(&p) == 0) G2V_CUDA(cudaMemsetAsync(p, 0, sizeof(int), s));
+    }
     return G2V_SUCCESS;
 }
 
@@ -381,8 +465,11 @@ int g2v_backward_plan(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_
         return rc;
     if ((rc = launch_exclusive_scan(w.counts, num_gaussians, w.offsets, w.total, w.scan, s))) return rc;
     int64_t mb = 0;
+    int word = 0;
     G2V_CUDA(cudaMemcpyAsync(&mb, w.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    if ((rc = queue_error_read(s, &word))) return rc;
     G2V_CUDA(cudaStreamSynchronize(s));
+    if ((rc = report_device_error(word, s))) return rc;
     if (mb > INT32_MAX) {
         set_error("%lld (Gaussian, block) pairs exceed the int32 range", (long long)mb);
         return G2V_ERROR_SIZE_LIMIT;

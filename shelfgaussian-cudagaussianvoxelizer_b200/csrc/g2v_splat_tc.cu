@@ -1,0 +1,356 @@
+// g2v_splat_tc.cu -- forward splat on the 5th-generation tensor cores (tcgen05, kind::f16).
+//
+// Per tile (64 voxels) and group of 512 channels, the feature sum is the contraction
+//     S[c][v] = sum_k F[g_k][c] * w[v][k]       (C x K) . (K x 64)
+// computed as D^T in TMEM: M = 128 channels per MMA (4 M-blocks, 256 TMEM columns), N = 64 voxels,
+// K = 16 Gaussians per step.  fp32-level accuracy comes from splitting both operands into a half
+// pair, x = hi + lo (~22 bits), and accumulating hi*hi + hi*lo + lo*hi in fp32 (the dropped lo*lo
+// term is ~2^-22 relative).  Range: features are scaled per channel by a power of two so that a
+// channel's max |f| lies in [2^14, 2^15); weights by a per-tile power of two from the tile's max
+// |opacity| (w <= |opacity|).  The epilogue undoes both exactly and divides by max(D_v, 1e-6).
+//
+// Operands in shared memory:
+//   A = F^T slice (128 channels x 16 Gaussians) MN-major, 128-byte swizzle: 64-channel x 8-Gaussian
+//       atoms of 1 KB (LBO = 1 KB between the two channel halves, SBO = 2 KB between Gaussian octets),
+//       gathered row by row from the split features with cp.async (16 B = 8 channels).
+//   B = w slice (64 voxels x 16 Gaussians) K-major, no swizzle: 8x8 core matrices of 128 B
+//       (LBO = 128 B between Gaussian octets, SBO = 256 B between voxel octets), written by the
+//       threads that evaluate the weights.
+// Roles (256 threads): threads 0-127 evaluate weights (voxel = t % 64, Gaussian octet = t / 64) and
+// accumulate the density; threads 128-255 issue the feature gathers one step ahead; thread 0 issues
+// the 12 MMAs of a step and commits them to the stage's mbarrier.  Three stages; every wait is bounded.
+#include "g2v_internal.cuh"
+#include "g2v_tc.cuh"
+
+namespace g2v {
+
+namespace {
+constexpr int kThreads = 256;
+constexpr int kKStep = 16;
+constexpr int kMB = 4;                   // M-blocks of 128 channels per CTA
+constexpr int kChGroup = kMB * 128;      // channels per CTA
+constexpr int kStages = 3;
+constexpr int kABytes = kMB * 4096;      // one operand half (hi or lo), one stage
+constexpr int kWBytes = 2048;
+constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
+constexpr uint32_t kTmemCols = kMB * 64;
+constexpr uint32_t kIdesc = tc::idesc_f16_f32(128, 64, /*a MN-major*/ 1, /*b K-major*/ 0);
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + 1024;
+
+struct TcMisc {
+    uint64_t mbar[kStages];
+    uint32_t tmem_base;
+    int fail;
+    float dpart[2][kVoxPerTile];
+    float red[kThreads / 32];
+};
+
+__device__ __forceinline__ int pow2_exponent(float m) {
+    // floor(log2(m)) for a finite m > 0
+    int e;
+    frexpf(m, &e);
+    return e - 1;
+}
+
+// Per-channel max |f| (as float bits; non-negative floats order like integers).
+__global__ void __launch_bounds__(256) feature_colmax_kernel(const float* __restrict__ f, int64_t n, int C,
+                                                             int rows_per_block, unsigned* __restrict__ colmax) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+    const int64_t r1 = min(n, r0 + rows_per_block);
+    float m = 0.0f;
+    for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, fabsf(f[r * C + c]));
+    atomicMax(&colmax[c], __float_as_uint(m));
+}
+
+// features (N, C) fp32 -> hi / lo halves (N, Cp) scaled by 2^k_c, and unscale[c] = 2^-k_c.
+__global__ void __launch_bounds__(256) feature_split_kernel(const float* __restrict__ f, int64_t n, int C, int Cp,
+                                                            const unsigned* __restrict__ colmax,
+                                                            __half* __restrict__ hi, __half* __restrict__ lo,
+                                                            float* __restrict__ unscale) {
+    const int64_t chunks = (int64_t)Cp / 8;
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n * chunks) return;
+    const int64_t r = i / chunks;
+    const int c8 = (int)(i - r * chunks) * 8;
+    __align__(16) __half h[8], l[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int c = c8 + j;
+        float x = 0.0f;
+        int k = 0;
+        if (c < C) {
+            x = f[r * C + c];
+            const float m = __uint_as_float(colmax[c]);
+            k = (m > 0.0f) ? max(-100, min(100, 14 - pow2_exponent(m))) : 0;
+        }
+        tc::split_half(ldexpf(x, k), h[j], l[j]);
+        if (r == 0) unscale[c] = ldexpf(1.0f, -k);
+    }
+    *reinterpret_cast<uint4*>(hi + r * Cp + c8) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(lo + r * Cp + c8) = *reinterpret_cast<const uint4*>(l);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) m = fmaxf(m, red[w]);
+    __syncthreads();
+    return m;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
+    const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C,
+    int Cp, const float* __restrict__ means, const float* __restrict__ opacity, const float* __restrict__ cov_inv,
+    const int32_t* __restrict__ lb, const int32_t* __restrict__ ub, const int32_t* __restrict__ tile_offsets,
+    const int32_t* __restrict__ tile_lists, int first_tile, int ngroups, Grid G, float* __restrict__ density,
+    float* __restrict__ grid_feats, int* __restrict__ err) {
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = tc::smem_u32(smem_raw);
+    unsigned char* base = smem_raw + ((1024 - (raw & 1023)) & 1023);
+    TcMisc& ms = *reinterpret_cast<TcMisc*>(base + kStages * kStageBytes);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tl = blockIdx.x / ngroups, grp = blockIdx.x - tl * ngroups;
+    int tx, ty, tz;
+    decode_tile(first_tile + tl, G, tx, ty, tz);
+    const int x0 = tx * kTile, y0 = ty * kTile, z0 = tz * kTile;
+    const int s = tile_offsets[tl], K = tile_offsets[tl + 1] - s;
+    const int32_t* list = tile_lists + s;
+    const int c0 = grp * kChGroup;
+    const int nx = min(kTile, G.dims[0] - x0), ny = min(kTile, G.dims[1] - y0), nz = min(kTile, G.dims[2] - z0);
+    const int64_t row0 = ((int64_t)x0 * G.dims[1] + y0) * G.dims[2] + z0;
+    const int64_t sx = (int64_t)G.dims[1] * G.dims[2], sy = G.dims[2];
+
+    if (K == 0) {  // no Gaussian reaches the tile: zeros
+        for (int i = tid; i < kVoxPerTile * kChGroup; i += kThreads) {
+            const int v = i / kChGroup, c = c0 + (i - v * kChGroup);
+            int lx, ly, lz;
+            local_voxel(v, lx, ly, lz);
+            if (c < C && lx < nx && ly < ny && lz < nz) grid_feats[(row0 + lx * sx + ly * sy + lz) * C + c] = 0.0f;
+        }
+        if (grp == 0 && tid < kVoxPerTile) {
+            int lx, ly, lz;
+            local_voxel(tid, lx, ly, lz);
+            if (lx < nx && ly < ny && lz < nz) density[row0 + lx * sx + ly * sy + lz] = 0.0f;
+        }
+        return;
+    }
+
+    // per-tile weight scale: |w| <= |opacity|
+    float om = 0.0f;
+    for (int k = tid; k < K; k += kThreads) om = fmaxf(om, fabsf(opacity[list[k]]));
+    om = block_max(om, ms.red);
+    const int kt = (om > 0.0f) ? max(-100, min(100, 14 - pow2_exponent(om))) : 0;
+    const float wscale = ldexpf(1.0f, kt);
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) tc::mbar_init(&ms.mbar[i], 1);
+        tc::mbar_fence_init();
+        ms.fail = 0;
+    }
+    if (warp == 0) tc::tmem_alloc(&ms.tmem_base, kTmemCols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = ms.tmem_base;
+
+    const int nsteps = (K + kKStep - 1) / kKStep;
+    const bool producer = tid >= 128;
+    const int ptid = tid - 128;
+
+    auto a_stage = [&](int st, int hl) -> unsigned char* { return base + st * kStageBytes + hl * kABytes; };
+    auto w_stage = [&](int st, int hl) -> unsigned char* {
+        return base + st * kStageBytes + 2 * kABytes + hl * kWBytes;
+    };
+    // gather the split features of step `step` into stage `st` (producer threads)
+    auto issue_a = [&](int step, int st) {
+        const int k0 = step * kKStep;
+        for (int idx = ptid; idx < 2 * kKStep * (kChGroup / 8); idx += 128) {
+            const int hl = idx >> 10;           // 1024 16-byte chunks per half
+            const int rem = idx & 1023;
+            const int k = rem >> 6;             // Gaussian within the step
+            const int ch16 = rem & 63;          // 8-channel chunk within the group
+            const int mb = ch16 >> 4, a = (ch16 >> 3) & 1, j = ch16 & 7;
+            const int r = k & 7, g8 = k >> 3;
+            const uint32_t dst = tc::smem_u32(a_stage(st, hl)) + mb * 4096 + a * 1024 + g8 * 2048 + r * 128 +
+                                 ((j ^ r) << 4);
+            const int kk = k0 + k;
+            const int c = c0 + ch16 * 8;
+            const __half* F = hl ? Flo : Fhi;
+            const bool ok = kk < K && c < Cp;
+            const __half* src = ok ? F + (int64_t)list[kk] * Cp + c : F;
+            tc::cp_async16(dst, src, ok ? 16u : 0u);
+        }
+    };
+
+    // weight-thread constants
+    const int v = tid & 63, h8 = (tid >> 6) & 1;
+    int lx, ly, lz;
+    local_voxel(v, lx, ly, lz);
+    const int vx = x0 + lx, vy = y0 + ly, vz = z0 + lz;
+    const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz = voxel_centre(G, 2, vz);
+    float dsum = 0.0f;
+    bool ok = true;
+
+    if (producer) {
+        issue_a(0, 0);
+        tc::cp_async_commit();
+    }
+    for (int i = 0; i < nsteps; ++i) {
+        const int st = i % kStages;
+        if (producer) {
+            if (i + 1 < nsteps) {
+                const int st1 = (i + 1) % kStages;
+                if (i + 1 >= kStages) ok = ok && tc::mbar_wait(&ms.mbar[st1], ((i + 1) / kStages - 1) & 1, err);
+                issue_a(i + 1, st1);
+            }
+            tc::cp_async_commit();
+            tc::cp_async_wait<1>();
+        } else {
+            if (i >= kStages) ok = ok && tc::mbar_wait(&ms.mbar[st], (i / kStages - 1) & 1, err);
+            __align__(16) __half wh[8], wl[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int kk = i * kKStep + h8 * 8 + j;
+                float w = 0.0f;
+                if (kk < K) {
+                    const int64_t g = list[kk];
+                    if (vx >= lb[g * 3] && vx <= ub[g * 3] && vy >= lb[g * 3 + 1] && vy <= ub[g * 3 + 1] &&
+                        vz >= lb[g * 3 + 2] && vz <= ub[g * 3 + 2]) {
+                        float c9[9];
+#pragma unroll
+                        for (int q = 0; q < 9; ++q) c9[q] = cov_inv[g * 9 + q];
+                        float qx, qy, qz;
+                        const float e = eval_gaussian(c9, cx - means[g * 3], cy - means[g * 3 + 1],
+                                                      cz - means[g * 3 + 2], qx, qy, qz);
+                        w = opacity[g] * e;
+                    }
+                }
+                dsum += w;
+                tc::split_half(w * wscale, wh[j], wl[j]);
+            }
+            const int off = (v >> 3) * 256 + h8 * 128 + (v & 7) * 16;
+            *reinterpret_cast<uint4*>(w_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(wh);
+            *reinterpret_cast<uint4*>(w_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(wl);
+        }
+        tc::fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc::tc_fence_after();
+            if (ok && !ms.fail) {
+                const uint64_t bh = tc::smem_desc(tc::smem_u32(w_stage(st, 0)), 128, 256, tc::kLayoutNone);
+                const uint64_t bl = tc::smem_desc(tc::smem_u32(w_stage(st, 1)), 128, 256, tc::kLayoutNone);
+#pragma unroll
+                for (int mb = 0; mb < kMB; ++mb) {
+                    const uint64_t ah =
+                        tc::smem_desc(tc::smem_u32(a_stage(st, 0)) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                    const uint64_t al =
+                        tc::smem_desc(tc::smem_u32(a_stage(st, 1)) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                    const uint32_t d = tmem + mb * 64;
+                    tc::mma_f16_ss(d, ah, bh, kIdesc, i > 0);
+                    tc::mma_f16_ss(d, ah, bl, kIdesc, true);
+                    tc::mma_f16_ss(d, al, bh, kIdesc, true);
+                }
+            }
+            tc::mma_commit(tc::smem_u32(&ms.mbar[st]));
+        }
+    }
+    // all MMAs of this CTA are complete once the last commit has arrived
+    {
+        const int last = nsteps - 1;
+        ok = tc::mbar_wait(&ms.mbar[last % kStages], (last / kStages) & 1, err) && ok;
+    }
+    if (!ok) ms.fail = 1;  // benign race: every writer stores 1
+    if (!producer) ms.dpart[h8][v] = dsum;
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+
+    // epilogue: warp w reads TMEM lanes 32*(w%4).. (channels) of M-blocks (w/4) and (w/4)+2
+    const bool good = !ms.fail;
+    const int q = warp & 3, hh = warp >> 2;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int mb = hh + 2 * t;
+        const int c = c0 + mb * 128 + q * 32 + lane;
+        const float us = (c < C) ? unscale[c] / wscale : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float vals[16];
+            if (good) {
+                tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + mb * 64 + j * 16, vals);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) vals[e] = 0.0f;
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int vv = j * 16 + e;
+                const int ex = vv >> 4, ey = (vv >> 2) & 3, ez = vv & 3;
+                if (c < C && ex < nx && ey < ny && ez < nz) {
+                    const float D = ms.dpart[0][vv] + ms.dpart[1][vv];
+                    grid_feats[(row0 + ex * sx + ey * sy + ez) * C + c] = vals[e] * us / fmaxf(D, kEps);
+                }
+            }
+        }
+    }
+    if (grp == 0 && tid < kVoxPerTile && lx < nx && ly < ny && lz < nz)
+        density[row0 + lx * sx + ly * sy + lz] = ms.dpart[0][tid] + ms.dpart[1][tid];
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+}  // namespace
+
+size_t splat_tc_split_bytes(int64_t n, int64_t C) {
+    const int64_t Cp = (C + 7) / 8 * 8;
+    return 2 * ((size_t)n * Cp * sizeof(__half) + 256) + 2 * ((size_t)Cp * 4 + 256);
+}
+
+// Splits the features (per-channel power-of-two scale) into `split` (splat_tc_split_bytes) and runs the
+// tensor-core splat over the tiles [first_tile, first_tile + num_tiles).
+int launch_splat_tc(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
+                    const int32_t* ub, const float* features, int64_t n, int C, const int32_t* tile_offsets,
+                    const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
+                    float* grid_feats, void* split, int* err, cudaStream_t s) {
+    if (num_tiles <= 0) return 0;
+    const int Cp = (C + 7) / 8 * 8;
+    Carver cv(split);
+    __half* hi = cv.take<__half>((size_t)n * Cp);
+    __half* lo = cv.take<__half>((size_t)n * Cp);
+    unsigned* colmax = cv.take<unsigned>((size_t)Cp);
+    float* unscale = cv.take<float>((size_t)Cp);
+    if (n > 0) {
+        G2V_CUDA(cudaMemsetAsync(colmax, 0, sizeof(unsigned) * Cp, s));
+        const int rows = 256;
+        dim3 g1((C + 255) / 256, (unsigned)((n + rows - 1) / rows));
+        G2V_TIMED("feature_colmax_kernel", s, feature_colmax_kernel<<<g1, 256, 0, s>>>(features, n, C, rows, colmax));
+        G2V_LAUNCH_CHECK("feature_colmax_kernel");
+        const int64_t total = n * (Cp / 8);
+        G2V_TIMED("feature_split_kernel", s,
+                  feature_split_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(features, n, C, Cp, colmax, hi,
+                                                                                    lo, unscale));
+        G2V_LAUNCH_CHECK("feature_split_kernel");
+    }
+    const int ngroups = (C + kChGroup - 1) / kChGroup;
+    G2V_CUDA(cudaFuncSetAttribute(splat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    const int64_t grid = (int64_t)num_tiles * ngroups;
+    G2V_TIMED("splat_tc_kernel", s,
+              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(hi, lo, unscale, C, Cp, means, opacity,
+                                                                            cov_inv, lb, ub, tile_offsets, tile_lists,
+                                                                            first_tile, ngroups, G, density,
+                                                                            grid_feats, err));
+    G2V_LAUNCH_CHECK("splat_tc_kernel");
+    return 0;
+}
+
+}  // namespace g2v

@@ -1,0 +1,69 @@
+"""Both splat variants (tcgen05 split-f16 and FP32-FMA) against the oracle and against each other."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_close, dev
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _forward(variant, means, opacity, cov, feats, size, rng):
+    from CudaGaussianVoxelizer import _C
+    old = os.environ.get("G2V_VARIANT")
+    os.environ["G2V_VARIANT"] = variant
+    try:
+        out = _C.gaussian_voxelizer_forward(*dev(means, opacity, cov), size, rng, dev(feats)[0])
+        torch.cuda.synchronize()
+    finally:
+        if old is None:
+            del os.environ["G2V_VARIANT"]
+        else:
+            os.environ["G2V_VARIANT"] = old
+    return [t.cpu().numpy() if isinstance(t, torch.Tensor) else t for t in out]
+
+
+@pytest.mark.parametrize("n,c,seed,size,half", [(300, 24, 1, 0.4, 6.0), (2000, 512, 2, 0.4, 10.0),
+                                                (1500, 1000, 3, 0.4, 10.0), (4000, 1100, 4, 0.4, 12.0)])
+def test_tensor_core_splat_matches_oracle_and_fp32_variant(n, c, seed, size, half):
+    rng = [-half, -half, -1.0, half, half, 5.4]
+    m, o, cv, f = oracle.generate_inputs(n, c, rng, seed=seed, num_outside=n // 20)
+    m, o, cv, f = m.numpy(), o.numpy(), cv.numpy(), f.numpy()
+    tc = _forward("tc", m, o, cv, f, [size] * 3, rng)
+    fp = _forward("simt", m, o, cv, f, [size] * 3, rng)
+    for i in (1, 2, 3, 4, 6, 7):  # maps and inverse are variant-independent
+        np.testing.assert_array_equal(tc[i], fp[i])
+    assert_close("density tc vs simt", tc[0], fp[0], rtol=1e-6)
+    assert_close("grid_feats tc vs simt", tc[5], fp[5])
+    dims = oracle.grid_shape([size] * 3, rng)[0]
+    dref, fref = oracle.forward(m, o, cv, f, tc[2], tc[3], [size] * 3, rng, dims)
+    assert_close("density", tc[0], dref)
+    assert_close("grid_feats", tc[5], fref)
+
+
+def test_tensor_core_splat_handles_feature_scales():
+    """Channels spanning 1e-30 .. 1e30 and opacities up to 50: the power-of-two scaling keeps the split exact."""
+    rng = [-6.0, -6.0, -1.0, 6.0, 6.0, 5.4]
+    m, o, cv, f = oracle.generate_inputs(400, 40, rng, seed=9)
+    scales = np.logspace(-30, 30, 40).astype(np.float32)
+    f = (f.numpy() * scales[None, :]).astype(np.float32)
+    o = (o.numpy() * 50.0).astype(np.float32)
+    m, cv = m.numpy(), cv.numpy()
+    tc = _forward("tc", m, o, cv, f, [0.4] * 3, rng)
+    dims = oracle.grid_shape([0.4] * 3, rng)[0]
+    dref, fref = oracle.forward(m, o, cv, f, tc[2], tc[3], [0.4] * 3, rng, dims)
+    assert_close("density", tc[0], dref)
+    for ch in (0, 13, 39):  # per channel, relative to that channel's own scale
+        assert_close(f"grid_feats[..., {ch}]", tc[5][..., ch], fref[..., ch])
+
+
+def test_device_error_word_is_clear():
+    import ctypes
+    from CudaGaussianVoxelizer import _lib
+    w = ctypes.c_int(-1)
+    _lib.check(_lib.load().g2v_device_error(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(w)),
+               "g2v_device_error")
+    assert w.value == 0
