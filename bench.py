@@ -42,6 +42,9 @@ CONFIGS = {
     "cfg5": dict(n=100000, c=256, size=0.2, range=RANGE, var_max=8.0, expand=0.0),
     # test_reference.py's forward shape; small enough for multi-pass ncu captures (grid_feats 328 MB > L2)
     "small128": dict(n=18000, c=128, size=0.4, range=RANGE, var_max=2.5, expand=0.0),
+    # cfg3's Gaussian density and channels on a quarter of the area (100x100x16): same tile lists,
+    # grid_feats 655 MB (> L2), small enough for multi-pass ncu captures
+    "cfg3q": dict(n=4500, c=1024, size=0.4, range=[-20.0, -20.0, -1.0, 20.0, 20.0, 5.4], var_max=2.5, expand=0.0),
 }
 METRIC = "G2V fwd+bwd ms/step (18k Gaussians, 1024-D, 200×200×16) and % HBM roofline"
 
@@ -351,6 +354,25 @@ def reference_cuda(cfg, seed, dev, steps=2):
             "source": "reference src/cuda_gaussian_voxelizer.cu built for sm_100a by oracle/build_ref.py"}
 
 
+def run_forward_only(args, dev):
+    """Profiling mode: only forward passes (for ncu captures of the splat kernels)."""
+    import torch
+    from CudaGaussianVoxelizer import _C
+    cfg = CONFIGS[args.config]
+    size, rng, m, o, c, f = make_inputs(cfg, seed=args.seed)
+    m, o, c, f = [t.to(dev) for t in (m, o, c, f)]
+    for _ in range(args.warmup):
+        _C.gaussian_voxelizer_forward(m, o, c, size, rng, f, timing=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        _C.gaussian_voxelizer_forward(m, o, c, size, rng, f, timing=False)
+    e1.record()
+    torch.cuda.synchronize()
+    return {"mode": "forward-only", "config": args.config, "ms_per_forward": e0.elapsed_time(e1) / args.steps}
+
+
 def run_reference(args, rank, world, dev):
     cfg = CONFIGS[args.config]
     threads = os.cpu_count() or 1
@@ -387,6 +409,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-cuda", action="store_true")
+    ap.add_argument("--forward-only", action="store_true", help="profiling mode: forward passes only")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -406,6 +429,9 @@ def main():
     from datetime import timedelta
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.forward_only:
+        print(json.dumps(run_forward_only(args, dev)), flush=True)
+        return
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     try:

@@ -35,15 +35,30 @@ constexpr int kWBytes = 2048;
 constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
 constexpr uint32_t kTmemCols = kMB * 64;
 constexpr uint32_t kIdesc = tc::idesc_f16_f32(128, 64, /*a MN-major*/ 1, /*b K-major*/ 0);
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + 1024;
+
+// Parameters of one Gaussian as five 16-byte words: (mean, opacity), P[0..3], P[4..7], (P[8], lb.xyz),
+// (ub.xyz, pad).  The producer threads stage the 16 Gaussians of a step one step ahead.
+struct __align__(16) GParams {
+    float4 w[5];
+};
+struct StepParams {
+    GParams g[kKStep];
+};
 
 struct TcMisc {
     uint64_t mbar[kStages];
     uint32_t tmem_base;
     int fail;
     float dpart[2][kVoxPerTile];
+    float vscale[kVoxPerTile];  // 1 / (max(D_v, eps) * weight scale)
     float red[kThreads / 32];
+    StepParams prm[kStages];
 };
+// Two CTAs per SM: 3 stages (108 KB) + TcMisc (4.3 KB) per CTA.  The 128-byte swizzle atoms need the
+// dynamic shared memory to start on a 1024-byte boundary; the kernel checks that at run time.
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(TcMisc);
+// 228 KB per SM, 1 KB of it reserved per resident CTA: two CTAs need <= 113 KB of dynamic smem each
+static_assert(kSmemBytes <= (228 * 1024) / 2 - 1024, "splat_tc_kernel no longer fits two CTAs per SM");
 
 __device__ __forceinline__ int pow2_exponent(float m) {
     // floor(log2(m)) for a finite m > 0
@@ -110,10 +125,13 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     const int32_t* __restrict__ lb, const int32_t* __restrict__ ub, const int32_t* __restrict__ tile_offsets,
     const int32_t* __restrict__ tile_lists, int first_tile, int ngroups, Grid G, float* __restrict__ density,
     float* __restrict__ grid_feats, int* __restrict__ err) {
-    extern __shared__ unsigned char smem_raw[];
-    const uint32_t raw = tc::smem_u32(smem_raw);
-    unsigned char* base = smem_raw + ((1024 - (raw & 1023)) & 1023);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = smem_raw;
     TcMisc& ms = *reinterpret_cast<TcMisc*>(base + kStages * kStageBytes);
+    if ((tc::smem_u32(smem_raw) & 1023u) != 0) {  // never expected; fail loudly instead of mis-swizzling
+        if (threadIdx.x == 0) atomicOr(err, 2);
+        return;
+    }
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tl = blockIdx.x / ngroups, grp = blockIdx.x - tl * ngroups;
@@ -189,6 +207,26 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
         }
     };
 
+    // stage the parameters of step `step` into prm[st] (producer threads; one field per thread)
+    auto stage_params = [&](int step, int st) {
+        float* P = reinterpret_cast<float*>(ms.prm[st].g);
+        const int k0 = step * kKStep;
+        for (int idx = ptid; idx < kKStep * 20; idx += 128) {
+            const int k = idx / 20, f = idx - k * 20;
+            const int kk = k0 + k;
+            const bool valid = kk < K;
+            const int64_t g = valid ? list[kk] : 0;
+            float val;
+            if (f < 3) val = means[g * 3 + f];
+            else if (f == 3) val = opacity[g];
+            else if (f < 13) val = cov_inv[g * 9 + (f - 4)];
+            else if (f < 16) val = __int_as_float(valid ? lb[g * 3 + (f - 13)] : 1);   // padding: empty box
+            else if (f < 19) val = __int_as_float(valid ? ub[g * 3 + (f - 16)] : 0);
+            else val = 0.0f;
+            P[k * 20 + f] = val;
+        }
+    };
+
     // weight-thread constants
     const int v = tid & 63, h8 = (tid >> 6) & 1;
     int lx, ly, lz;
@@ -201,7 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     if (producer) {
         issue_a(0, 0);
         tc::cp_async_commit();
+        stage_params(0, 0);
     }
+    __syncthreads();
     for (int i = 0; i < nsteps; ++i) {
         const int st = i % kStages;
         if (producer) {
@@ -209,28 +249,26 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
                 const int st1 = (i + 1) % kStages;
                 if (i + 1 >= kStages) ok = ok && tc::mbar_wait(&ms.mbar[st1], ((i + 1) / kStages - 1) & 1, err);
                 issue_a(i + 1, st1);
+                // prm[st1] was last read by the weight threads two barriers ago
+                stage_params(i + 1, st1);
             }
             tc::cp_async_commit();
             tc::cp_async_wait<1>();
         } else {
             if (i >= kStages) ok = ok && tc::mbar_wait(&ms.mbar[st], (i / kStages - 1) & 1, err);
             __align__(16) __half wh[8], wl[8];
+            const GParams* GP = ms.prm[st].g + h8 * 8;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int kk = i * kKStep + h8 * 8 + j;
+                const float4 a = GP[j].w[0], b = GP[j].w[1], c = GP[j].w[2], d = GP[j].w[3], e4 = GP[j].w[4];
                 float w = 0.0f;
-                if (kk < K) {
-                    const int64_t g = list[kk];
-                    if (vx >= lb[g * 3] && vx <= ub[g * 3] && vy >= lb[g * 3 + 1] && vy <= ub[g * 3 + 1] &&
-                        vz >= lb[g * 3 + 2] && vz <= ub[g * 3 + 2]) {
-                        float c9[9];
-#pragma unroll
-                        for (int q = 0; q < 9; ++q) c9[q] = cov_inv[g * 9 + q];
-                        float qx, qy, qz;
-                        const float e = eval_gaussian(c9, cx - means[g * 3], cy - means[g * 3 + 1],
-                                                      cz - means[g * 3 + 2], qx, qy, qz);
-                        w = opacity[g] * e;
-                    }
+                // padding Gaussians (beyond K) carry an empty box
+                if (vx >= __float_as_int(d.y) && vx <= __float_as_int(e4.x) && vy >= __float_as_int(d.z) &&
+                    vy <= __float_as_int(e4.y) && vz >= __float_as_int(d.w) && vz <= __float_as_int(e4.z)) {
+                    const float c9[9] = {b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x};
+                    float qx, qy, qz;
+                    const float e = eval_gaussian(c9, cx - a.x, cy - a.y, cz - a.z, qx, qy, qz);
+                    w = a.w * e;
                 }
                 dsum += w;
                 tc::split_half(w * wscale, wh[j], wl[j]);
@@ -271,15 +309,27 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
+    if (tid < kVoxPerTile) {
+        const float D = ms.dpart[0][tid] + ms.dpart[1][tid];
+        ms.vscale[tid] = 1.0f / (fmaxf(D, kEps) * wscale);
+        if (grp == 0 && lx < nx && ly < ny && lz < nz) density[row0 + lx * sx + ly * sy + lz] = D;
+    }
+    __syncthreads();
 
-    // epilogue: warp w reads TMEM lanes 32*(w%4).. (channels) of M-blocks (w/4) and (w/4)+2
+    // epilogue: warp w reads TMEM lanes 32*(w%4).. (channels) of M-blocks (w/4) and (w/4)+2; lane = channel,
+    // the 16 columns of one load are the voxels (lx, 0..3, 0..3) of x-slice lx = j
     const bool good = !ms.fail;
+    const bool full = nx == kTile && ny == kTile && nz == kTile;
     const int q = warp & 3, hh = warp >> 2;
+    int64_t off[16];  // element offsets of the 16 voxels (ly, lz) of an x-slice, relative to the slice
+#pragma unroll
+    for (int e = 0; e < 16; ++e) off[e] = ((int64_t)(e >> 2) * sy + (e & 3)) * C;
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         const int mb = hh + 2 * t;
         const int c = c0 + mb * 128 + q * 32 + lane;
-        const float us = (c < C) ? unscale[c] / wscale : 0.0f;
+        const bool cok = c < C;
+        const float us = cok ? unscale[c] : 0.0f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             float vals[16];
@@ -289,19 +339,26 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
 #pragma unroll
                 for (int e = 0; e < 16; ++e) vals[e] = 0.0f;
             }
+            float* slice = grid_feats + (row0 + j * sx) * C + c;
+            const float4* vs4 = reinterpret_cast<const float4*>(&ms.vscale[j * 16]);
+            if (full) {
+                if (cok) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const int vv = j * 16 + e;
-                const int ex = vv >> 4, ey = (vv >> 2) & 3, ez = vv & 3;
-                if (c < C && ex < nx && ey < ny && ez < nz) {
-                    const float D = ms.dpart[0][vv] + ms.dpart[1][vv];
-                    grid_feats[(row0 + ex * sx + ey * sy + ez) * C + c] = vals[e] * us / fmaxf(D, kEps);
+                    for (int e4 = 0; e4 < 4; ++e4) {
+                        const float4 r = vs4[e4];
+                        slice[off[4 * e4 + 0]] = vals[4 * e4 + 0] * (us * r.x);
+                        slice[off[4 * e4 + 1]] = vals[4 * e4 + 1] * (us * r.y);
+                        slice[off[4 * e4 + 2]] = vals[4 * e4 + 2] * (us * r.z);
+                        slice[off[4 * e4 + 3]] = vals[4 * e4 + 3] * (us * r.w);
+                    }
                 }
+            } else if (cok && j < nx) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    if ((e >> 2) < ny && (e & 3) < nz) slice[off[e]] = vals[e] * (us * ms.vscale[j * 16 + e]);
             }
         }
     }
-    if (grp == 0 && tid < kVoxPerTile && lx < nx && ly < ny && lz < nz)
-        density[row0 + lx * sx + ly * sy + lz] = ms.dpart[0][tid] + ms.dpart[1][tid];
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 0) {
