@@ -21,6 +21,7 @@
 // the 12 MMAs of a step and commits them to the stage's mbarrier.  Three stages; every wait is bounded.
 #include "g2v_internal.cuh"
 #include "g2v_tc.cuh"
+#include "g2v_tmap.cuh"
 
 namespace g2v {
 
@@ -46,11 +47,14 @@ struct StepParams {
 };
 
 struct TcMisc {
-    uint64_t mbar[kStages];
+    uint64_t full_a[kStages];   // TMA bytes of the stage's A operand landed
+    uint64_t full_p[kStages];   // the stage's Gaussian parameters landed (32 producer lanes)
+    uint64_t full_w[kStages];   // the stage's weights written (4 weight warps)
+    uint64_t empty[kStages];    // the MMAs reading the stage completed
+    uint64_t mma_done;
     uint32_t tmem_base;
     int fail;
-    float dpart[2][kVoxPerTile];
-    float vscale[kVoxPerTile];  // 1 / (max(D_v, eps) * weight scale)
+    float vscale[kVoxPerTile];     // 1 / (max(D_v, eps) * weight scale)
     float red[kThreads / 32];
     StepParams prm[kStages];
 };
@@ -119,12 +123,17 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return m;
 }
 
+// Roles: warp 0 stages step i+1 (TMA gathers of the split features into the swizzled A layout, 4-byte
+// cp.async of the Gaussian parameters); warp 1 (one thread) issues the 12 MMAs of a step once its A and
+// w are ready and commits them to the stage's "empty" barrier; warps 2-5 evaluate the weights of a
+// step.  No CTA-wide barrier in the main loop: stages hand over through mbarriers.
 __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
-    const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C,
-    int Cp, const float* __restrict__ means, const float* __restrict__ opacity, const float* __restrict__ cov_inv,
-    const int32_t* __restrict__ lb, const int32_t* __restrict__ ub, const int32_t* __restrict__ tile_offsets,
-    const int32_t* __restrict__ tile_lists, int first_tile, int ngroups, Grid G, float* __restrict__ density,
-    float* __restrict__ grid_feats, int* __restrict__ err) {
+    const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
+    const float* __restrict__ unscale, int C, int64_t n, const float* __restrict__ means,
+    const float* __restrict__ opacity, const float* __restrict__ cov_inv, const int32_t* __restrict__ lb,
+    const int32_t* __restrict__ ub, const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ tile_lists,
+    int first_tile, int ngroups, Grid G, float* __restrict__ density, float* __restrict__ grid_feats,
+    int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
     TcMisc& ms = *reinterpret_cast<TcMisc*>(base + kStages * kStageBytes);
@@ -168,7 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     const float wscale = ldexpf(1.0f, kt);
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) tc::mbar_init(&ms.mbar[i], 1);
+        for (int i = 0; i < kStages; ++i) {
+            tc::mbar_init(&ms.full_a[i], 1);
+            tc::mbar_init(&ms.full_p[i], 32);
+            tc::mbar_init(&ms.full_w[i], 4);
+            tc::mbar_init(&ms.empty[i], 1);
+        }
+        tc::mbar_init(&ms.mma_done, 1);
         tc::mbar_fence_init();
         ms.fail = 0;
     }
@@ -177,141 +192,166 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = ms.tmem_base;
-
     const int nsteps = (K + kKStep - 1) / kKStep;
-    const bool producer = tid >= 128;
-    const int ptid = tid - 128;
+    bool ok = true;
+    float dsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // weight threads: density partials of their z-line
+    int dline = 0, dkp = 0;
 
-    auto a_stage = [&](int st, int hl) -> unsigned char* { return base + st * kStageBytes + hl * kABytes; };
+    auto a_stage = [&](int st, int hl) -> uint32_t {
+        return tc::smem_u32(base + st * kStageBytes + hl * kABytes);
+    };
     auto w_stage = [&](int st, int hl) -> unsigned char* {
         return base + st * kStageBytes + 2 * kABytes + hl * kWBytes;
     };
-    // gather the split features of step `step` into stage `st` (producer threads)
-    auto issue_a = [&](int step, int st) {
-        const int k0 = step * kKStep;
-        for (int idx = ptid; idx < 2 * kKStep * (kChGroup / 8); idx += 128) {
-            const int hl = idx >> 10;           // 1024 16-byte chunks per half
-            const int rem = idx & 1023;
-            const int k = rem >> 6;             // Gaussian within the step
-            const int ch16 = rem & 63;          // 8-channel chunk within the group
-            const int mb = ch16 >> 4, a = (ch16 >> 3) & 1, j = ch16 & 7;
-            const int r = k & 7, g8 = k >> 3;
-            const uint32_t dst = tc::smem_u32(a_stage(st, hl)) + mb * 4096 + a * 1024 + g8 * 2048 + r * 128 +
-                                 ((j ^ r) << 4);
-            const int kk = k0 + k;
-            const int c = c0 + ch16 * 8;
-            const __half* F = hl ? Flo : Fhi;
-            const bool ok = kk < K && c < Cp;
-            const __half* src = ok ? F + (int64_t)list[kk] * Cp + c : F;
-            tc::cp_async16(dst, src, ok ? 16u : 0u);
-        }
-    };
 
-    // stage the parameters of step `step` into prm[st] (producer threads; one field per thread)
-    auto stage_params = [&](int step, int st) {
-        float* P = reinterpret_cast<float*>(ms.prm[st].g);
-        const int k0 = step * kKStep;
-        for (int idx = ptid; idx < kKStep * 20; idx += 128) {
-            const int k = idx / 20, f = idx - k * 20;
-            const int kk = k0 + k;
-            const bool valid = kk < K;
-            const int64_t g = valid ? list[kk] : 0;
-            float val;
-            if (f < 3) val = means[g * 3 + f];
-            else if (f == 3) val = opacity[g];
-            else if (f < 13) val = cov_inv[g * 9 + (f - 4)];
-            else if (f < 16) val = __int_as_float(valid ? lb[g * 3 + (f - 13)] : 1);   // padding: empty box
-            else if (f < 19) val = __int_as_float(valid ? ub[g * 3 + (f - 16)] : 0);
-            else val = 0.0f;
-            P[k * 20 + f] = val;
-        }
-    };
-
-    // weight-thread constants
-    const int v = tid & 63, h8 = (tid >> 6) & 1;
-    int lx, ly, lz;
-    local_voxel(v, lx, ly, lz);
-    const int vx = x0 + lx, vy = y0 + ly, vz = z0 + lz;
-    const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz = voxel_centre(G, 2, vz);
-    float dsum = 0.0f;
-    bool ok = true;
-
-    if (producer) {
-        issue_a(0, 0);
-        tc::cp_async_commit();
-        stage_params(0, 0);
-    }
-    __syncthreads();
-    for (int i = 0; i < nsteps; ++i) {
-        const int st = i % kStages;
-        if (producer) {
-            if (i + 1 < nsteps) {
-                const int st1 = (i + 1) % kStages;
-                if (i + 1 >= kStages) ok = ok && tc::mbar_wait(&ms.mbar[st1], ((i + 1) / kStages - 1) & 1, err);
-                issue_a(i + 1, st1);
-                // prm[st1] was last read by the weight threads two barriers ago
-                stage_params(i + 1, st1);
-            }
-            tc::cp_async_commit();
-            tc::cp_async_wait<1>();
-        } else {
-            if (i >= kStages) ok = ok && tc::mbar_wait(&ms.mbar[st], (i / kStages - 1) & 1, err);
-            __align__(16) __half wh[8], wl[8];
-            const GParams* GP = ms.prm[st].g + h8 * 8;
+    if (warp == 0) {
+        // ---------------- producer warp ----------------
+        for (int i = 0; i < nsteps && ok; ++i) {
+            const int st = i % kStages;
+            if (i >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((i / kStages) + 1) & 1, err);
+            if (!ok) break;
+            const int k0 = i * kKStep;
+            // Gaussian rows of this step (row n is outside the tensor: zero fill for padding)
+            const int my_row = (lane < kKStep && k0 + lane < K) ? list[k0 + lane] : (int)n;
+            if (lane == 0) tc::mbar_arrive_expect_tx(&ms.full_a[st], 2 * kABytes);
+            __syncwarp();
+            // 64 gathers (2 halves x 4 M-blocks x 2 channel atoms x 4 Gaussian quads), two per lane
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 a = GP[j].w[0], b = GP[j].w[1], c = GP[j].w[2], d = GP[j].w[3], e4 = GP[j].w[4];
-                float w = 0.0f;
-                // padding Gaussians (beyond K) carry an empty box
-                if (vx >= __float_as_int(d.y) && vx <= __float_as_int(e4.x) && vy >= __float_as_int(d.z) &&
-                    vy <= __float_as_int(e4.y) && vz >= __float_as_int(d.w) && vz <= __float_as_int(e4.z)) {
-                    const float c9[9] = {b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x};
-                    float qx, qy, qz;
-                    const float e = eval_gaussian(c9, cx - a.x, cy - a.y, cz - a.z, qx, qy, qz);
-                    w = a.w * e;
-                }
-                dsum += w;
-                tc::split_half(w * wscale, wh[j], wl[j]);
+            for (int r = 0; r < 2; ++r) {
+                const int op = lane * 2 + r;
+                const int hl = op >> 5, mb = (op >> 3) & 3, a = (op >> 2) & 1, kq = op & 3;
+                const int g0 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 0);
+                const int g1 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 1);
+                const int g2 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 2);
+                const int g3 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 3);
+                const uint32_t dst = a_stage(st, hl) + mb * 4096 + a * 1024 + (kq >> 1) * 2048 + (kq & 1) * 512;
+                tc::tma_gather4(dst, hl ? (const void*)&tmap_lo : (const void*)&tmap_hi, c0 + mb * 128 + a * 64, g0,
+                                g1, g2, g3, &ms.full_a[st]);
             }
-            const int off = (v >> 3) * 256 + h8 * 128 + (v & 7) * 16;
-            *reinterpret_cast<uint4*>(w_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(wh);
-            *reinterpret_cast<uint4*>(w_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(wl);
+            // Gaussian parameters (20 fields each; zero fill for padding)
+            const uint32_t pbase = tc::smem_u32(ms.prm[st].g);
+            for (int idx = lane; idx < kKStep * 20; idx += 32) {
+                const int k = idx / 20, f = idx - k * 20;
+                const int kk = k0 + k;
+                const int64_t g = kk < K ? list[kk] : 0;
+                const void* src = opacity;
+                if (f < 3) src = means + g * 3 + f;
+                else if (f == 3) src = opacity + g;
+                else if (f < 13) src = cov_inv + g * 9 + (f - 4);
+                else if (f < 16) src = lb + g * 3 + (f - 13);
+                else if (f < 19) src = ub + g * 3 + (f - 16);
+                const uint32_t bytes = (kk < K && f < 19) ? 4u : 0u;
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(pbase + idx * 4), "l"(src),
+                             "r"(bytes)
+                             : "memory");
+            }
+            tc::cp_async_mbar_arrive_noinc(&ms.full_p[st]);
         }
-        tc::fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            if (ok && !ms.fail) {
+    } else if (warp == 1) {
+        // ---------------- MMA warp (one thread) ----------------
+        if (lane == 0) {
+            for (int i = 0; i < nsteps && ok; ++i) {
+                const int st = i % kStages;
+                const uint32_t par = (i / kStages) & 1;
+                ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
+                if (!ok) break;
+                tc::tc_fence_after();
                 const uint64_t bh = tc::smem_desc(tc::smem_u32(w_stage(st, 0)), 128, 256, tc::kLayoutNone);
                 const uint64_t bl = tc::smem_desc(tc::smem_u32(w_stage(st, 1)), 128, 256, tc::kLayoutNone);
 #pragma unroll
                 for (int mb = 0; mb < kMB; ++mb) {
-                    const uint64_t ah =
-                        tc::smem_desc(tc::smem_u32(a_stage(st, 0)) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
-                    const uint64_t al =
-                        tc::smem_desc(tc::smem_u32(a_stage(st, 1)) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                    const uint64_t ah = tc::smem_desc(a_stage(st, 0) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                    const uint64_t al = tc::smem_desc(a_stage(st, 1) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
                     const uint32_t d = tmem + mb * 64;
                     tc::mma_f16_ss(d, ah, bh, kIdesc, i > 0);
                     tc::mma_f16_ss(d, ah, bl, kIdesc, true);
                     tc::mma_f16_ss(d, al, bh, kIdesc, true);
                 }
+                tc::mma_commit(tc::smem_u32(&ms.empty[st]));
             }
-            tc::mma_commit(tc::smem_u32(&ms.mbar[st]));
+            tc::mma_commit(tc::smem_u32(&ms.mma_done));
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ---------------- weight warps: thread = (z-line (lx, ly), Gaussian pair) ----------------
+        const int t = tid - 64;
+        const int line = t >> 3, kp = t & 7;  // 16 lines x 8 pairs
+        const int lx = line >> 2, ly = line & 3;
+        const int vx = x0 + lx, vy = y0 + ly;
+        const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz0 = voxel_centre(G, 2, z0);
+        const float hz = G.h[2];
+        const float kLog2e = 1.4426950408889634f;
+        dline = line;
+        dkp = kp;
+        for (int i = 0; i < nsteps && ok; ++i) {
+            const int st = i % kStages;
+            if (i >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((i / kStages) + 1) & 1, err);
+            ok = ok && tc::mbar_wait(&ms.full_p[st], (i / kStages) & 1, err);
+            if (!ok) break;
+            float w[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int k = 2 * kp + u;
+                const GParams& gp = ms.prm[st].g[k];
+                const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
+#pragma unroll
+                for (int zz = 0; zz < 4; ++zz) w[u][zz] = 0.0f;
+                const int zlo = max(__float_as_int(d.w) - z0, 0), zhi = min(__float_as_int(e4.z) - z0, 3);
+                if (i * kKStep + k < K && vx >= __float_as_int(d.y) && vx <= __float_as_int(e4.x) &&
+                    vy >= __float_as_int(d.z) && vy <= __float_as_int(e4.y) && zlo <= zhi) {
+                    // maha(z0 + t) = A + t B + t^2 Q for the voxel centres of this z-line
+                    const float dx = cx - a.x, dy = cy - a.y, dz = cz0 - a.z;
+                    const float qx = b.x * dx + b.y * dy + b.z * dz;   // (P d)
+                    const float qy = b.w * dx + c.x * dy + c.y * dz;
+                    const float qz = c.z * dx + c.w * dy + d.x * dz;
+                    const float A = dx * qx + dy * qy + dz * qz;
+                    const float ptz = b.z * dx + c.y * dy + d.x * dz;  // (P^T d)_z
+                    const float B = hz * (qz + ptz), Q = hz * hz * d.x;
+#pragma unroll
+                    for (int zz = 0; zz < 4; ++zz) {
+                        const float m = fmaf(fmaf(Q, (float)zz, B), (float)zz, A);
+                        const float ex = exp2f(-0.5f * kLog2e * m);
+                        w[u][zz] = (zz >= zlo && zz <= zhi) ? a.w * ex : 0.0f;
+                    }
+                }
+            }
+            // store the 8 weights (4 voxels x 2 Gaussians) as half2 pairs, hi and lo, in the K-major core matrices
+#pragma unroll
+            for (int zz = 0; zz < 4; ++zz) {
+                dsum[zz] += w[0][zz] + w[1][zz];
+                __half h0, l0, h1, l1;
+                tc::split_half(w[0][zz] * wscale, h0, l0);
+                tc::split_half(w[1][zz] * wscale, h1, l1);
+                const int v = (lx * 4 + ly) * 4 + zz, k = 2 * kp;
+                const int off = (v >> 3) * 256 + (k >> 3) * 128 + (v & 7) * 16 + (k & 7) * 2;
+                *reinterpret_cast<__half2*>(w_stage(st, 0) + off) = __halves2half2(h0, h1);
+                *reinterpret_cast<__half2*>(w_stage(st, 1) + off) = __halves2half2(l0, l1);
+            }
+            tc::fence_async_smem();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
         }
     }
-    // all MMAs of this CTA are complete once the last commit has arrived
-    {
-        const int last = nsteps - 1;
-        ok = tc::mbar_wait(&ms.mbar[last % kStages], (last / kStages) & 1, err) && ok;
-    }
+    // all MMAs are complete once mma_done has arrived
+    ok = tc::mbar_wait(&ms.mma_done, 0, err) && ok;
     if (!ok) ms.fail = 1;  // benign race: every writer stores 1
-    if (!producer) ms.dpart[h8][v] = dsum;
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
+    // the stage buffers are free now: density partials [pair slot][voxel] go there
+    float* dpartk = reinterpret_cast<float*>(base);
+    if (warp >= 2 && warp < 6) {
+#pragma unroll
+        for (int zz = 0; zz < 4; ++zz) dpartk[dkp * kVoxPerTile + dline * 4 + zz] = dsum[zz];
+    }
+    __syncthreads();
     if (tid < kVoxPerTile) {
-        const float D = ms.dpart[0][tid] + ms.dpart[1][tid];
+        float D = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) D += dpartk[q * kVoxPerTile + tid];
         ms.vscale[tid] = 1.0f / (fmaxf(D, kEps) * wscale);
+        int lx, ly, lz;
+        local_voxel(tid, lx, ly, lz);
         if (grp == 0 && lx < nx && ly < ny && lz < nz) density[row0 + lx * sx + ly * sy + lz] = D;
     }
     __syncthreads();
@@ -399,10 +439,15 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
         G2V_LAUNCH_CHECK("feature_split_kernel");
     }
     const int ngroups = (C + kChGroup - 1) / kChGroup;
+    CUtensorMap th, tlo;
+    if (!encode_rows_f16_sw128(&th, hi, n, Cp, Cp, 64) || !encode_rows_f16_sw128(&tlo, lo, n, Cp, Cp, 64)) {
+        set_error("cuTensorMapEncodeTiled failed for the split features (N=%lld, Cp=%d)", (long long)n, Cp);
+        return 4;  // G2V_ERROR_CUDA
+    }
     G2V_CUDA(cudaFuncSetAttribute(splat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int64_t grid = (int64_t)num_tiles * ngroups;
     G2V_TIMED("splat_tc_kernel", s,
-              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(hi, lo, unscale, C, Cp, means, opacity,
+              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(th, tlo, unscale, C, n, means, opacity,
                                                                             cov_inv, lb, ub, tile_offsets, tile_lists,
                                                                             first_tile, ngroups, G, density,
                                                                             grid_feats, err));

@@ -134,3 +134,36 @@ __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
 
 }  // namespace tc
 }  // namespace g2v
+
+namespace g2v {
+namespace tc {
+
+// ---------------------------------------------------------------------------------------------
+// TMA and mbarrier transaction helpers (single CTA; no cluster multicast anywhere in this library).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// The mbarrier receives one arrival when all cp.async issued so far by this thread have completed.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst_saddr, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst_saddr), "l"(src) : "memory");
+}
+// Four rows (row0..row3) x one box width starting at column `col` of a 2-D tensor map, written as four
+// consecutive box rows at dst; completion is counted in bytes on `bar`.
+__device__ __forceinline__ void tma_gather4(uint32_t dst_saddr, const void* tmap, int col, int r0, int r1, int r2,
+                                            int r3, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst_saddr),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+        : "memory");
+}
+
+}  // namespace tc
+}  // namespace g2v
