@@ -65,8 +65,8 @@ __device__ __forceinline__ bool in_box(const Params& p, int x, int y, int z) {
 struct SPassSmem {
     Params P[kChunk];
     int gid[kChunk];
-    float Fs[kCh][kChunk];          // features slice [channel][gaussian]
-    float Gs[kCh][kVoxPerTile];     // upstream grid-feature gradient slice [channel][voxel]
+    alignas(16) float Fs[kCh][kChunk];       // features slice [channel][gaussian]; read as float4
+    alignas(16) float Gs[kCh][kVoxPerTile];  // upstream grid-feature gradient slice [channel][voxel]
     float S[kChunk][kVoxPerTile];   // S of the chunk [gaussian][voxel]
     float gD[kVoxPerTile], den[kVoxPerTile], e[kVoxPerTile], act[kVoxPerTile];
     int vox_ok[kVoxPerTile];

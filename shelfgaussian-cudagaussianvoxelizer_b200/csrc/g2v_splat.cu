@@ -20,8 +20,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kChunk = 64;
 
-struct SplatSmem {
-    float W[kChunk][kVoxPerTile];  // weights of the chunk, [gaussian][voxel]
+struct __align__(16) SplatSmem {
+    alignas(16) float W[kChunk][kVoxPerTile];  // weights of the chunk, [gaussian][voxel]; read as float4
     float D[kVoxPerTile];          // running density
     float mx[kChunk], my[kChunk], mz[kChunk], op[kChunk];
     float ci[9][kChunk];

@@ -19,14 +19,15 @@
 // Roles (256 threads): threads 0-127 evaluate weights (voxel = t % 64, Gaussian octet = t / 64) and
 // accumulate the density; threads 128-255 issue the feature gathers one step ahead; thread 0 issues
 // the 12 MMAs of a step and commits them to the stage's mbarrier.  Three stages; every wait is bounded.
+#include <cstddef>
+
 #include "g2v_internal.cuh"
 #include "g2v_tc.cuh"
-#include "g2v_tmap.cuh"
 
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 256;
+constexpr int kThreads = 288;          // 4 producer warps, 4 weight warps, 1 MMA warp
 constexpr int kKStep = 16;
 constexpr int kMB = 4;                   // M-blocks of 128 channels per CTA
 constexpr int kChGroup = kMB * 128;      // channels per CTA
@@ -47,20 +48,22 @@ struct StepParams {
 };
 
 struct TcMisc {
-    uint64_t full_a[kStages];   // TMA bytes of the stage's A operand landed
-    uint64_t full_p[kStages];   // the stage's Gaussian parameters landed (32 producer lanes)
+    uint64_t full_a[kStages];   // the stage's A operand and Gaussian parameters landed (128 producer threads)
     uint64_t full_w[kStages];   // the stage's weights written (4 weight warps)
     uint64_t empty[kStages];    // the MMAs reading the stage completed
     uint64_t mma_done;
     uint32_t tmem_base;
     int fail;
-    float vscale[kVoxPerTile];     // 1 / (max(D_v, eps) * weight scale)
-    float red[kThreads / 32];
+    alignas(16) float vscale[kVoxPerTile];  // 1 / (max(D_v, eps) * weight scale); read as float4
+    float red[(kThreads + 31) / 32];
     StepParams prm[kStages];
 };
 // Two CTAs per SM: 3 stages (108 KB) + TcMisc (4.3 KB) per CTA.  The 128-byte swizzle atoms need the
 // dynamic shared memory to start on a 1024-byte boundary; the kernel checks that at run time.
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(TcMisc);
+static_assert(offsetof(TcMisc, vscale) % 16 == 0 && offsetof(TcMisc, prm) % 16 == 0,
+              "vector-accessed shared fields must be 16-byte aligned");
+static_assert((kStages * kStageBytes) % 1024 == 0, "TcMisc must start 1024-byte aligned");
 // 228 KB per SM, 1 KB of it reserved per resident CTA: two CTAs need <= 113 KB of dynamic smem each
 static_assert(kSmemBytes <= (228 * 1024) / 2 - 1024, "splat_tc_kernel no longer fits two CTAs per SM");
 
@@ -111,6 +114,24 @@ __global__ void __launch_bounds__(256) feature_split_kernel(const float* __restr
     *reinterpret_cast<uint4*>(lo + r * Cp + c8) = *reinterpret_cast<const uint4*>(l);
 }
 
+// Gaussian parameters packed as GParams records (the layout the weight threads read).
+__global__ void __launch_bounds__(256) pack_params_kernel(const float* __restrict__ means,
+                                                          const float* __restrict__ opacity,
+                                                          const float* __restrict__ cov_inv,
+                                                          const int32_t* __restrict__ lb, const int32_t* __restrict__ ub,
+                                                          int64_t n, GParams* __restrict__ out) {
+    const int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const float* P = cov_inv + g * 9;
+    GParams r;
+    r.w[0] = make_float4(means[g * 3], means[g * 3 + 1], means[g * 3 + 2], opacity[g]);
+    r.w[1] = make_float4(P[0], P[1], P[2], P[3]);
+    r.w[2] = make_float4(P[4], P[5], P[6], P[7]);
+    r.w[3] = make_float4(P[8], __int_as_float(lb[g * 3]), __int_as_float(lb[g * 3 + 1]), __int_as_float(lb[g * 3 + 2]));
+    r.w[4] = make_float4(__int_as_float(ub[g * 3]), __int_as_float(ub[g * 3 + 1]), __int_as_float(ub[g * 3 + 2]), 0.0f);
+    out[g] = r;
+}
+
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -118,7 +139,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     __syncthreads();
     float m = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kThreads / 32; ++w) m = fmaxf(m, red[w]);
+    for (int w = 0; w < (kThreads + 31) / 32; ++w) m = fmaxf(m, red[w]);
     __syncthreads();
     return m;
 }
@@ -128,10 +149,9 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // w are ready and commits them to the stage's "empty" barrier; warps 2-5 evaluate the weights of a
 // step.  No CTA-wide barrier in the main loop: stages hand over through mbarriers.
 __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
-    const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
-    const float* __restrict__ unscale, int C, int64_t n, const float* __restrict__ means,
-    const float* __restrict__ opacity, const float* __restrict__ cov_inv, const int32_t* __restrict__ lb,
-    const int32_t* __restrict__ ub, const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ tile_lists,
+    const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C, int Cp,
+    const GParams* __restrict__ gparams,
+    const float* __restrict__ opacity, const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ tile_lists,
     int first_tile, int ngroups, Grid G, float* __restrict__ density, float* __restrict__ grid_feats,
     int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -178,8 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
-            tc::mbar_init(&ms.full_a[i], 1);
-            tc::mbar_init(&ms.full_p[i], 32);
+            tc::mbar_init(&ms.full_a[i], 128);
             tc::mbar_init(&ms.full_w[i], 4);
             tc::mbar_init(&ms.empty[i], 1);
         }
@@ -204,50 +223,44 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
         return base + st * kStageBytes + 2 * kABytes + hl * kWBytes;
     };
 
-    if (warp == 0) {
-        // ---------------- producer warp ----------------
+    if (warp < 4) {
+        // ---------------- producer warps: thread = (operand half, 8-channel chunk) ----------------
+        const int hl = tid >> 6, ch16 = tid & 63;
+        const int mb = ch16 >> 4, a = (ch16 >> 3) & 1, j = ch16 & 7;
+        const int c = c0 + ch16 * 8;
+        const bool cin = c < Cp;
+        const char* fbase = reinterpret_cast<const char*>(hl ? Flo : Fhi) + (int64_t)(cin ? c : 0) * 2;
+        const int64_t pitch = (int64_t)Cp * 2;
+        // lanes 0..15 of each producer warp hold the Gaussian ids of a step; step i+1's ids load early
+        int next_row = (lane < kKStep && lane < K) ? list[lane] : 0;
         for (int i = 0; i < nsteps && ok; ++i) {
             const int st = i % kStages;
+            const int k0 = i * kKStep;
+            const int my_row = next_row;
+            next_row = (lane < kKStep && k0 + kKStep + lane < K) ? list[k0 + kKStep + lane] : 0;
             if (i >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((i / kStages) + 1) & 1, err);
             if (!ok) break;
-            const int k0 = i * kKStep;
-            // Gaussian rows of this step (row n is outside the tensor: zero fill for padding)
-            const int my_row = (lane < kKStep && k0 + lane < K) ? list[k0 + lane] : (int)n;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&ms.full_a[st], 2 * kABytes);
-            __syncwarp();
-            // 64 gathers (2 halves x 4 M-blocks x 2 channel atoms x 4 Gaussian quads), two per lane
+            const uint32_t dbase = a_stage(st, hl) + mb * 4096 + a * 1024;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int op = lane * 2 + r;
-                const int hl = op >> 5, mb = (op >> 3) & 3, a = (op >> 2) & 1, kq = op & 3;
-                const int g0 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 0);
-                const int g1 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 1);
-                const int g2 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 2);
-                const int g3 = __shfl_sync(0xffffffffu, my_row, kq * 4 + 3);
-                const uint32_t dst = a_stage(st, hl) + mb * 4096 + a * 1024 + (kq >> 1) * 2048 + (kq & 1) * 512;
-                tc::tma_gather4(dst, hl ? (const void*)&tmap_lo : (const void*)&tmap_hi, c0 + mb * 128 + a * 64, g0,
-                                g1, g2, g3, &ms.full_a[st]);
+            for (int k = 0; k < kKStep; ++k) {
+                const int row = __shfl_sync(0xffffffffu, my_row, k);
+                const bool valid = cin && (k0 + k < K);
+                const uint32_t dst = dbase + (k >> 3) * 2048 + (k & 7) * 128 + ((j ^ (k & 7)) << 4);
+                tc::cp_async16(dst, fbase + (valid ? (int64_t)row * pitch : 0), valid ? 16u : 0u);
             }
-            // Gaussian parameters (20 fields each; zero fill for padding)
-            const uint32_t pbase = tc::smem_u32(ms.prm[st].g);
-            for (int idx = lane; idx < kKStep * 20; idx += 32) {
-                const int k = idx / 20, f = idx - k * 20;
-                const int kk = k0 + k;
-                const int64_t g = kk < K ? list[kk] : 0;
-                const void* src = opacity;
-                if (f < 3) src = means + g * 3 + f;
-                else if (f == 3) src = opacity + g;
-                else if (f < 13) src = cov_inv + g * 9 + (f - 4);
-                else if (f < 16) src = lb + g * 3 + (f - 13);
-                else if (f < 19) src = ub + g * 3 + (f - 16);
-                const uint32_t bytes = (kk < K && f < 19) ? 4u : 0u;
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(pbase + idx * 4), "l"(src),
-                             "r"(bytes)
-                             : "memory");
+            // Gaussian parameters: 16 records of 5 x 16 bytes (zero fill for padding)
+            {
+                const int k = min(tid / 5, kKStep - 1), wq = tid - (tid / 5) * 5;
+                const int row = __shfl_sync(0xffffffffu, my_row, k);  // whole warp takes part
+                if (tid < kKStep * 5) {
+                    const bool valid = k0 + k < K;
+                    tc::cp_async16(tc::smem_u32(ms.prm[st].g) + tid * 16, &gparams[valid ? row : 0].w[wq],
+                                   valid ? 16u : 0u);
+                }
             }
-            tc::cp_async_mbar_arrive_noinc(&ms.full_p[st]);
+            tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
         }
-    } else if (warp == 1) {
+    } else if (warp == 8) {
         // ---------------- MMA warp (one thread) ----------------
         if (lane == 0) {
             for (int i = 0; i < nsteps && ok; ++i) {
@@ -255,6 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
                 const uint32_t par = (i / kStages) & 1;
                 ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
                 if (!ok) break;
+                // the A operand was written by cp.async (generic proxy); the MMA reads it through the async proxy
+                tc::fence_async_smem();
                 tc::tc_fence_after();
                 const uint64_t bh = tc::smem_desc(tc::smem_u32(w_stage(st, 0)), 128, 256, tc::kLayoutNone);
                 const uint64_t bl = tc::smem_desc(tc::smem_u32(w_stage(st, 1)), 128, 256, tc::kLayoutNone);
@@ -272,21 +287,20 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
             tc::mma_commit(tc::smem_u32(&ms.mma_done));
         }
         __syncwarp();
-    } else if (warp < 6) {
-        // ---------------- weight warps: thread = (z-line (lx, ly), Gaussian pair) ----------------
-        const int t = tid - 64;
+    } else {
+        // ---------------- weight warps (4..7): thread = (z-line (lx, ly), Gaussian pair) ----------------
+        const int t = tid - 128;
         const int line = t >> 3, kp = t & 7;  // 16 lines x 8 pairs
         const int lx = line >> 2, ly = line & 3;
         const int vx = x0 + lx, vy = y0 + ly;
         const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz0 = voxel_centre(G, 2, z0);
         const float hz = G.h[2];
-        const float kLog2e = 1.4426950408889634f;
         dline = line;
         dkp = kp;
         for (int i = 0; i < nsteps && ok; ++i) {
             const int st = i % kStages;
             if (i >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((i / kStages) + 1) & 1, err);
-            ok = ok && tc::mbar_wait(&ms.full_p[st], (i / kStages) & 1, err);
+            ok = ok && tc::mbar_wait(&ms.full_a[st], (i / kStages) & 1, err);
             if (!ok) break;
             float w[2][4];
 #pragma unroll
@@ -310,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
 #pragma unroll
                     for (int zz = 0; zz < 4; ++zz) {
                         const float m = fmaf(fmaf(Q, (float)zz, B), (float)zz, A);
-                        const float ex = exp2f(-0.5f * kLog2e * m);
+                        const float ex = __expf(-0.5f * m);
                         w[u][zz] = (zz >= zlo && zz <= zhi) ? a.w * ex : 0.0f;
                     }
                 }
@@ -340,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     tc::tc_fence_after();
     // the stage buffers are free now: density partials [pair slot][voxel] go there
     float* dpartk = reinterpret_cast<float*>(base);
-    if (warp >= 2 && warp < 6) {
+    if (warp >= 4 && warp < 8) {
 #pragma unroll
         for (int zz = 0; zz < 4; ++zz) dpartk[dkp * kVoxPerTile + dline * 4 + zz] = dsum[zz];
     }
@@ -360,12 +374,12 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     // the 16 columns of one load are the voxels (lx, 0..3, 0..3) of x-slice lx = j
     const bool good = !ms.fail;
     const bool full = nx == kTile && ny == kTile && nz == kTile;
-    const int q = warp & 3, hh = warp >> 2;
+    const int q = warp & 3, hh = (warp >> 2) & 1;
     int64_t off[16];  // element offsets of the 16 voxels (ly, lz) of an x-slice, relative to the slice
 #pragma unroll
     for (int e = 0; e < 16; ++e) off[e] = ((int64_t)(e >> 2) * sy + (e & 3)) * C;
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < 2 && warp < 8; ++t) {
         const int mb = hh + 2 * t;
         const int c = c0 + mb * 128 + q * 32 + lane;
         const bool cok = c < C;
@@ -410,7 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
 
 size_t splat_tc_split_bytes(int64_t n, int64_t C) {
     const int64_t Cp = (C + 7) / 8 * 8;
-    return 2 * ((size_t)n * Cp * sizeof(__half) + 256) + 2 * ((size_t)Cp * 4 + 256);
+    return 2 * ((size_t)n * Cp * sizeof(__half) + 256) + 2 * ((size_t)Cp * 4 + 256) +
+           ((size_t)(n > 0 ? n : 1) * sizeof(GParams) + 256);
 }
 
 // Splits the features (per-channel power-of-two scale) into `split` (splat_tc_split_bytes) and runs the
@@ -439,16 +454,18 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
         G2V_LAUNCH_CHECK("feature_split_kernel");
     }
     const int ngroups = (C + kChGroup - 1) / kChGroup;
-    CUtensorMap th, tlo;
-    if (!encode_rows_f16_sw128(&th, hi, n, Cp, Cp, 64) || !encode_rows_f16_sw128(&tlo, lo, n, Cp, Cp, 64)) {
-        set_error("cuTensorMapEncodeTiled failed for the split features (N=%lld, Cp=%d)", (long long)n, Cp);
-        return 4;  // G2V_ERROR_CUDA
+    GParams* gp = cv.take<GParams>((size_t)(n > 0 ? n : 1));
+    if (n > 0) {
+        G2V_TIMED("pack_params_kernel", s,
+                  pack_params_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(means, opacity, cov_inv, lb, ub, n,
+                                                                                gp));
+        G2V_LAUNCH_CHECK("pack_params_kernel");
     }
     G2V_CUDA(cudaFuncSetAttribute(splat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int64_t grid = (int64_t)num_tiles * ngroups;
     G2V_TIMED("splat_tc_kernel", s,
-              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(th, tlo, unscale, C, n, means, opacity,
-                                                                            cov_inv, lb, ub, tile_offsets, tile_lists,
+              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(hi, lo, unscale, C, Cp, gp, opacity,
+                                                                            tile_offsets, tile_lists,
                                                                             first_tile, ngroups, G, density,
                                                                             grid_feats, err));
     G2V_LAUNCH_CHECK("splat_tc_kernel");
