@@ -7,6 +7,7 @@
 
 #include "g2v.h"
 #include "g2v_internal.cuh"
+#include "g2v_tc.cuh"
 
 namespace g2v {
 
@@ -50,6 +51,10 @@ int launch_fpass(const float* grad_feats, const float* means, const float* opaci
                  const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin, int nbx, int nby, int nbz,
                  const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF, int64_t block_pair_cap,
                  cudaStream_t s);
+int launch_fpass_tc(const float* grad_feats, int C, const float* density, const GParams* gparams,
+                    const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
+                    int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
+                    int64_t block_pair_cap, int* err, cudaStream_t s);
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
                     const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
                     float* grad_opacity, cudaStream_t s);
@@ -197,6 +202,7 @@ struct BackwardWs {
     void* g_scan;
     float* partial10;
     float* partialF;
+    GParams* gparams;
 };
 size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, int64_t C, BackwardWs& w) {
     Carver c(p);
@@ -216,6 +222,7 @@ size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, 
     w.g_scan = c.take<char>(scan_workspace_bytes(feats ? n : 1));
     w.partial10 = c.take<float>((size_t)(m > 0 ? m : 1) * 10);
     w.partialF = c.take<float>((size_t)(feats && mb > 0 ? mb : 1) * (size_t)(feats ? C : 1));
+    w.gparams = c.take<GParams>((size_t)(n > 0 ? n : 1));
     return c.bytes();
 }
 
@@ -552,10 +559,22 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
                                    w.block_unsorted, w.block_lists, w.block_scan, total, s)))
             return rc;
         if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s))) return rc;
-        if ((rc = launch_fpass(grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, C, density,
-                               w.block_offsets, w.block_lists, w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1],
-                               nb[2], B, tile_x_begin, tile_x_end, G, w.partialF, num_block_pairs, s)))
+        if (use_tensor_cores()) {
+            int* err = nullptr;
+            if ((rc = device_error_ptr(&err))) return rc;
+            if ((rc = launch_pack_params(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, num_gaussians,
+                                         w.gparams, s)))
+                return rc;
+            if ((rc = launch_fpass_tc(grad_grid_feats, C, density, w.gparams, w.block_offsets, w.block_lists,
+                                      w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1], nb[2], B, tile_x_begin,
+                                      tile_x_end, G, w.partialF, num_block_pairs, err, s)))
+                return rc;
+        } else if ((rc = launch_fpass(grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, C,
+                                      density, w.block_offsets, w.block_lists, w.g2b_offsets, bx_begin,
+                                      bx_end - bx_begin, nb[1], nb[2], B, tile_x_begin, tile_x_end, G, w.partialF,
+                                      num_block_pairs, s))) {
             return rc;
+        }
         if ((rc = launch_reduce_feats(w.partialF, w.g2b_offsets, valid_voxel_lb, valid_voxel_ub, num_gaussians, C, B,
                                       bx_begin, bx_end, grad_features, s)))
             return rc;

@@ -1,0 +1,338 @@
+// g2v_grad_tc.cu -- feature gradient of the backward on the tensor cores (tcgen05, kind::f16, bf16).
+//
+// For a block of tiles b and its Gaussians (the block's list, up to 256 "slots" per pass):
+//     dF[slot][c] = sum_{v in b} w_slot,v / max(D_v, 1e-6) * gF[v][c]
+// computed as D^T in TMEM: M = 128 channels (2 M-blocks = 256 channels per CTA), N = 256 slots,
+// K = 16 voxels per step (a quarter of a tile: the 16 voxels of one x-slice).  Accuracy: both operands
+// are split into bf16 pairs (x = hi + lo to ~2^-17) and hi*hi + hi*lo + lo*hi is accumulated in fp32;
+// bf16 keeps the fp32 exponent range, so no scaling is needed.
+//
+// Operands in shared memory (per stage):
+//   A = gF^T slice (256 channels x 16 voxels) MN-major, 128-byte swizzle (64-channel x 8-voxel atoms),
+//       converted from the fp32 gradient rows by the producer warps;
+//   B = weights (256 slots x 16 voxels) K-major, no swizzle (8x8 core matrices), evaluated by the weight
+//       warps from the slot's parameters: over the 4x4 voxels of an x-slice the Mahalanobis distance is a
+//       quadratic in (ly, lz), so each weight costs a few FMAs and one exp.
+// Roles (288 threads): warps 0-3 produce A, warps 4-7 produce B, warp 8 (one thread) issues the 6 MMAs
+// of a step.  Four stages handed over through mbarriers; every wait is bounded.  The epilogue writes the
+// per-(Gaussian, block) partial rows of the reference's dL/dfeatures; a deterministic CSR-order reduction
+// sums them per Gaussian.
+#include <cstddef>
+
+#include "g2v_internal.cuh"
+#include "g2v_tc.cuh"
+
+namespace g2v {
+
+namespace {
+constexpr int kThreads = 288;
+constexpr int kSlots = 256;
+constexpr int kMB = 2;                          // M-blocks of 128 channels per CTA
+constexpr int kCG = kMB * 128;                  // channels per CTA
+constexpr int kStages = 4;
+constexpr int kAHalf = kMB * 4096;              // one operand half, one stage
+constexpr int kBHalf = kSlots * 16 * 2;
+constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kSlots, /*A MN-major*/ 1, /*B K-major*/ 0);
+
+struct FMisc {
+    uint64_t full_a[kStages];
+    uint64_t full_w[kStages];
+    uint64_t empty[kStages];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int fail;
+    alignas(16) GParams prm[kSlots];
+    int64_t rowoff[kSlots];
+};
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(FMisc);
+static_assert(kSmemBytes <= 227 * 1024, "fpass_tc_kernel shared memory");
+static_assert(offsetof(FMisc, prm) % 16 == 0, "GParams records are read as float4");
+
+__global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
+    const float* __restrict__ grad_feats, int C, const float* __restrict__ density, const GParams* __restrict__ gparams,
+    const int32_t* __restrict__ block_offsets, const int32_t* __restrict__ block_lists,
+    const int32_t* __restrict__ g2b_offsets, int bx_begin, int nby, int nbz, int BX, int BY, int BZ, int tx_begin,
+    int tx_end, int ngroups, int vec, Grid G, float* __restrict__ partialF, int64_t block_pair_cap,
+    int* __restrict__ err) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = smem_raw;
+    FMisc& ms = *reinterpret_cast<FMisc*>(base + kStages * kStageBytes);
+    if ((tc::smem_u32(smem_raw) & 1023u) != 0) {
+        if (threadIdx.x == 0) atomicOr(err, 2);
+        return;
+    }
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bl = blockIdx.x / ngroups, cg = blockIdx.x - bl * ngroups;
+    const int bxr = bl / (nby * nbz), rem = bl - bxr * nby * nbz;
+    const int by = rem / nbz, bz = rem - (rem / nbz) * nbz;
+    const int bx = bx_begin + bxr;
+    const int s0 = block_offsets[bl], Kb = block_offsets[bl + 1] - s0;
+    if (Kb == 0) return;
+    const int c0 = cg * kCG;
+    const int txa = max(bx * BX, tx_begin), txb = min(bx * BX + BX, min(tx_end, G.tiles[0]));
+    const int tya = by * BY, tyb = min(tya + BY, G.tiles[1]);
+    const int tza = bz * BZ, tzb = min(tza + BZ, G.tiles[2]);
+    const int nty = tyb - tya, ntz = tzb - tza;
+    const int ntiles = max(0, txb - txa) * nty * ntz;
+    if (ntiles == 0) {  // no tile of this block in the slab: its partial rows are zero
+        for (int sl = 0; sl < Kb; ++sl) {
+            const int g = block_lists[s0 + sl];
+            const GParams& gp = gparams[g];
+            const int blx = (__float_as_int(gp.w[3].y) / kTile) / BX, bly = (__float_as_int(gp.w[3].z) / kTile) / BY;
+            const int blz = (__float_as_int(gp.w[3].w) / kTile) / BZ;
+            const int ey = (__float_as_int(gp.w[4].y) / kTile) / BY - bly + 1;
+            const int ez = (__float_as_int(gp.w[4].z) / kTile) / BZ - blz + 1;
+            const int64_t ro = (int64_t)g2b_offsets[g] + ((bx - blx) * ey + (by - bly)) * ez + (bz - blz);
+            if (ro >= block_pair_cap) continue;
+            for (int c = c0 + threadIdx.x; c < min(C, c0 + kCG); c += kThreads) partialF[ro * C + c] = 0.0f;
+        }
+        return;
+    }
+    const int nsteps = ntiles * 4;  // 4 x-slices of 16 voxels per tile
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            tc::mbar_init(&ms.full_a[i], 4);
+            tc::mbar_init(&ms.full_w[i], 4);
+            tc::mbar_init(&ms.empty[i], 1);
+        }
+        tc::mbar_init(&ms.mma_done, 1);
+        tc::mbar_fence_init();
+        ms.fail = 0;
+    }
+    if (warp == 0) tc::tmem_alloc(&ms.tmem_base, kTmemCols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = ms.tmem_base;
+    bool ok = true;
+
+    auto a_stage = [&](int st, int hl) -> unsigned char* { return base + st * kStageBytes + hl * kAHalf; };
+    auto b_stage = [&](int st, int hl) -> unsigned char* {
+        return base + st * kStageBytes + 2 * kAHalf + hl * kBHalf;
+    };
+    // tile and x-slice of step j of a pass
+    auto step_geom = [&](int j, int& x0, int& y0, int& z0, int& ks) {
+        const int t = j >> 2;
+        ks = j & 3;
+        const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
+        x0 = (txa + txi) * kTile;
+        y0 = (tya + tyi) * kTile;
+        z0 = (tza + tzi) * kTile;
+    };
+
+    int it = 0;  // global step counter across passes (stage / parity bookkeeping)
+    const int npass = (Kb + kSlots - 1) / kSlots;
+    for (int pass = 0; pass < npass; ++pass) {
+        const int p0 = pass * kSlots, ns = min(kSlots, Kb - p0);
+        // slot parameters and partial-row offsets for this pass
+        for (int i = tid; i < kSlots * 5; i += kThreads) {
+            const int sl = i / 5, wq = i - sl * 5;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (sl < ns) v = gparams[block_lists[s0 + p0 + sl]].w[wq];
+            ms.prm[sl].w[wq] = v;
+        }
+        for (int sl = tid; sl < kSlots; sl += kThreads) {
+            int64_t ro = -1;
+            if (sl < ns) {
+                const int g = block_lists[s0 + p0 + sl];
+                const GParams& gp = gparams[g];
+                const int lbx = __float_as_int(gp.w[3].y), lby = __float_as_int(gp.w[3].z), lbz = __float_as_int(gp.w[3].w);
+                const int ubx = __float_as_int(gp.w[4].x), uby = __float_as_int(gp.w[4].y), ubz = __float_as_int(gp.w[4].z);
+                const int blx = (lbx / kTile) / BX, bly = (lby / kTile) / BY, blz = (lbz / kTile) / BZ;
+                const int ey = (uby / kTile) / BY - bly + 1, ez = (ubz / kTile) / BZ - blz + 1;
+                ro = (int64_t)g2b_offsets[g] + ((bx - blx) * ey + (by - bly)) * ez + (bz - blz);
+                if (ro >= block_pair_cap) ro = -1;  // offsets come from the caller
+            }
+            ms.rowoff[sl] = ro;
+        }
+        __syncthreads();
+
+        if (warp < 4) {
+            // ---------------- producers: A = gF^T, thread = (voxel row r of the step, 32-channel chunk) ----
+            const int r = tid >> 3, ch = (tid & 7) * 32;  // 16 rows x 8 chunks
+            const int ly_r = r >> 2, lz_r = r & 3;
+            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                const int st = it % kStages;
+                int x0, y0, z0, ks;
+                step_geom(j, x0, y0, z0, ks);
+                if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
+                if (!ok) break;
+                const int x = x0 + ks, y = y0 + ly_r, z = z0 + lz_r;
+                const bool vok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
+                const int64_t row = ((int64_t)x * G.dims[1] + y) * G.dims[2] + z;
+                const float* src = grad_feats + row * C + c0 + ch;
+                const int mb = ch >> 7, a = (ch >> 6) & 1;
+                const int g8 = r >> 3, rr = r & 7;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {  // 8 channels per 16-byte chunk
+                    const int c = c0 + ch + q * 8;
+                    float f[8];
+                    if (vok && c + 7 < C && vec) {
+                        const float4 u = *reinterpret_cast<const float4*>(src + q * 8);
+                        const float4 w4 = *reinterpret_cast<const float4*>(src + q * 8 + 4);
+                        f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+                        f[4] = w4.x; f[5] = w4.y; f[6] = w4.z; f[7] = w4.w;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = (vok && c + e < C) ? src[q * 8 + e] : 0.0f;
+                    }
+                    __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) tc::split_bf16(f[e], h[e], l[e]);
+                    const int jj = ((ch & 63) >> 3) + q;  // 16-byte chunk within the 64-channel atom row
+                    const int off = mb * 4096 + a * 1024 + g8 * 2048 + rr * 128 + ((jj ^ rr) << 4);
+                    *reinterpret_cast<uint4*>(a_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(h);
+                    *reinterpret_cast<uint4*>(a_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(l);
+                }
+                tc::fence_async_smem();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&ms.full_a[st]);
+            }
+        } else if (warp < 8) {
+            // ---------------- weight warps: thread = slots (t, t + 128), 16 voxels of the x-slice -------
+            const int t = tid - 128;
+            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                const int st = it % kStages;
+                int x0, y0, z0, ks;
+                step_geom(j, x0, y0, z0, ks);
+                if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
+                if (!ok) break;
+                const int x = x0 + ks;
+                // 1 / max(D, eps) of the 16 voxels (ly, lz): lanes 0..15 load one each
+                float rd = 0.0f;
+                if (lane < 16) {
+                    const int y = y0 + (lane >> 2), z = z0 + (lane & 3);
+                    if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
+                        rd = 1.0f / fmaxf(density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z], kEps);
+                }
+                const float cx = voxel_centre(G, 0, x), cy0 = voxel_centre(G, 1, y0), cz0 = voxel_centre(G, 2, z0);
+                const float hy = G.h[1], hz = G.h[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int sl = t + u * 128;
+                    float w[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) w[e] = 0.0f;
+                    const GParams& gp = ms.prm[sl];
+                    const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
+                    const bool live = sl < ns && x >= __float_as_int(d.y) && x <= __float_as_int(e4.x);
+                    if (live) {
+                        const int ylo = __float_as_int(d.z) - y0, yhi = __float_as_int(e4.y) - y0;
+                        const int zlo = __float_as_int(d.w) - z0, zhi = __float_as_int(e4.z) - z0;
+                        const float dx = cx - a.x, dy = cy0 - a.y, dz = cz0 - a.z;
+                        const float qx = b.x * dx + b.y * dy + b.z * dz;
+                        const float qy = b.w * dx + c.x * dy + c.y * dz;
+                        const float qz = c.z * dx + c.w * dy + d.x * dz;
+                        const float A = dx * qx + dy * qy + dz * qz;
+                        const float pty = b.y * dx + c.x * dy + c.w * dz;  // (P^T d)_y
+                        const float ptz = b.z * dx + c.y * dy + d.x * dz;  // (P^T d)_z
+                        const float By = hy * (qy + pty), Bz = hz * (qz + ptz);
+                        const float Qyy = hy * hy * c.x, Qzz = hz * hz * d.x, Qyz = hy * hz * (c.y + c.w);
+#pragma unroll
+                        for (int ly = 0; ly < 4; ++ly) {
+                            const float Ay = fmaf(fmaf(Qyy, (float)ly, By), (float)ly, A);
+                            const float By2 = fmaf(Qyz, (float)ly, Bz);
+#pragma unroll
+                            for (int lz = 0; lz < 4; ++lz) {
+                                const float m = fmaf(fmaf(Qzz, (float)lz, By2), (float)lz, Ay);
+                                const float ex = __expf(-0.5f * m);
+                                const bool in = ly >= ylo && ly <= yhi && lz >= zlo && lz <= zhi;
+                                w[ly * 4 + lz] = in ? a.w * ex : 0.0f;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) w[e] *= __shfl_sync(0xffffffffu, rd, e);
+                    __align__(16) __nv_bfloat16 h[16], l[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) tc::split_bf16(w[e], h[e], l[e]);
+                    const int off = (sl >> 3) * 256 + (sl & 7) * 16;
+                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(h);
+                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off + 128) = *reinterpret_cast<const uint4*>(h + 8);
+                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(l);
+                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off + 128) = *reinterpret_cast<const uint4*>(l + 8);
+                }
+                tc::fence_async_smem();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
+            }
+        } else if (lane == 0) {
+            // ---------------- MMA thread ----------------
+            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                const int st = it % kStages;
+                const uint32_t par = (it / kStages) & 1;
+                ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint64_t bh = tc::smem_desc(tc::smem_u32(b_stage(st, 0)), 128, 256, tc::kLayoutNone);
+                const uint64_t blo = tc::smem_desc(tc::smem_u32(b_stage(st, 1)), 128, 256, tc::kLayoutNone);
+#pragma unroll
+                for (int mb = 0; mb < kMB; ++mb) {
+                    const uint64_t ah = tc::smem_desc(tc::smem_u32(a_stage(st, 0)) + mb * 4096, 1024, 2048,
+                                                      tc::kLayoutSw128);
+                    const uint64_t al = tc::smem_desc(tc::smem_u32(a_stage(st, 1)) + mb * 4096, 1024, 2048,
+                                                      tc::kLayoutSw128);
+                    const uint32_t dcol = tmem + mb * kSlots;
+                    tc::mma_f16_ss(dcol, ah, bh, kIdesc, j > 0);
+                    tc::mma_f16_ss(dcol, ah, blo, kIdesc, true);
+                    tc::mma_f16_ss(dcol, al, bh, kIdesc, true);
+                }
+                tc::mma_commit(tc::smem_u32(&ms.empty[st]));
+            }
+            tc::mma_commit(tc::smem_u32(&ms.mma_done));
+        } else {
+            it += nsteps;
+        }
+
+        ok = tc::mbar_wait_drain(&ms.mma_done, pass & 1, err) && ok;
+        if (!ok) ms.fail = 1;
+        tc::tc_fence_before();
+        __syncthreads();
+        tc::tc_fence_after();
+        // epilogue: warp w < 8 reads lanes 32*(w%4).. (channels) of M-block w/4, 256 slot columns
+        if (warp < 8 && !ms.fail) {
+            const int q = warp & 3, mb = warp >> 2;
+            const int c = c0 + mb * 128 + q * 32 + lane;
+            for (int jc = 0; jc < kSlots / 16; ++jc) {
+                if (jc * 16 >= ns) break;  // warp-uniform
+                float vals[16];
+                tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + mb * kSlots + jc * 16, vals);
+                if (c < C) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int64_t ro = ms.rowoff[jc * 16 + e];
+                        if (ro >= 0) partialF[ro * C + c] = vals[e];
+                    }
+                }
+            }
+        }
+        tc::tc_fence_before();
+        __syncthreads();
+        tc::tc_fence_after();
+    }
+    if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
+}
+}  // namespace
+
+int launch_fpass_tc(const float* grad_feats, int C, const float* density, const GParams* gparams,
+                    const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
+                    int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
+                    int64_t block_pair_cap, int* err, cudaStream_t s) {
+    const int64_t nblocks = (int64_t)nbx * nby * nbz;
+    if (nblocks <= 0 || C <= 0) return 0;
+    const int ngroups = (C + kCG - 1) / kCG;
+    const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0);
+    G2V_CUDA(cudaFuncSetAttribute(fpass_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    const int64_t grid = nblocks * ngroups;
+    G2V_TIMED("fpass_tc_kernel", s,
+              fpass_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(
+                  grad_feats, C, density, gparams, block_offsets, block_lists, g2b_offsets, bx_begin, nby, nbz, B[0],
+                  B[1], B[2], tx_begin, tx_end, ngroups, vec, G, partialF, block_pair_cap, err));
+    G2V_LAUNCH_CHECK("fpass_tc_kernel");
+    return 0;
+}
+
+}  // namespace g2v

@@ -38,11 +38,7 @@ constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
 constexpr uint32_t kTmemCols = kMB * 64;
 constexpr uint32_t kIdesc = tc::idesc_f16_f32(128, 64, /*a MN-major*/ 1, /*b K-major*/ 0);
 
-// Parameters of one Gaussian as five 16-byte words: (mean, opacity), P[0..3], P[4..7], (P[8], lb.xyz),
-// (ub.xyz, pad).  The producer threads stage the 16 Gaussians of a step one step ahead.
-struct __align__(16) GParams {
-    float4 w[5];
-};
+// The producer threads stage the GParams records of the 16 Gaussians of a step one step ahead.
 struct StepParams {
     GParams g[kKStep];
 };
@@ -347,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
         }
     }
     // all MMAs are complete once mma_done has arrived
-    ok = tc::mbar_wait(&ms.mma_done, 0, err) && ok;
+    ok = tc::mbar_wait_drain(&ms.mma_done, 0, err) && ok;
     if (!ok) ms.fail = 1;  // benign race: every writer stores 1
     tc::tc_fence_before();
     __syncthreads();
@@ -422,6 +418,15 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
 }
 }  // namespace
 
+int launch_pack_params(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
+                       const int32_t* ub, int64_t n, GParams* out, cudaStream_t s) {
+    if (n <= 0) return 0;
+    G2V_TIMED("pack_params_kernel", s,
+              pack_params_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(means, opacity, cov_inv, lb, ub, n, out));
+    G2V_LAUNCH_CHECK("pack_params_kernel");
+    return 0;
+}
+
 size_t splat_tc_split_bytes(int64_t n, int64_t C) {
     const int64_t Cp = (C + 7) / 8 * 8;
     return 2 * ((size_t)n * Cp * sizeof(__half) + 256) + 2 * ((size_t)Cp * 4 + 256) +
@@ -455,12 +460,8 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
     }
     const int ngroups = (C + kChGroup - 1) / kChGroup;
     GParams* gp = cv.take<GParams>((size_t)(n > 0 ? n : 1));
-    if (n > 0) {
-        G2V_TIMED("pack_params_kernel", s,
-                  pack_params_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(means, opacity, cov_inv, lb, ub, n,
-                                                                                gp));
-        G2V_LAUNCH_CHECK("pack_params_kernel");
-    }
+    int rc = launch_pack_params(means, opacity, cov_inv, lb, ub, n, gp, s);
+    if (rc) return rc;
     G2V_CUDA(cudaFuncSetAttribute(splat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int64_t grid = (int64_t)num_tiles * ngroups;
     G2V_TIMED("splat_tc_kernel", s,

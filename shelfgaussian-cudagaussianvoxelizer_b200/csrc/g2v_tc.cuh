@@ -3,6 +3,7 @@
 // of the descriptors matches cute/arch/mma_sm100_desc.hpp).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -112,6 +113,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Wait for a commit that is always issued (the end-of-work commit of the MMA thread), also after another
+// wait has given up, so that no MMA is in flight when the kernel frees its TMEM.  Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < (1u << 22); ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return *reinterpret_cast<volatile int*>(err) == 0;
+    }
+    atomicOr(err, kErrWaitTimeout);
+    return false;
+}
+
 // ---------------------------------------------------------------------------------------------
 // cp.async (16 bytes; src_bytes = 0 fills zeros) and the async-proxy fence for operands written with
 // ordinary stores.
@@ -130,6 +150,18 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
     hi = __float2half_rn(x);
     lo = __float2half_rn(x - __half2float(hi));
+}
+
+// float -> (hi, lo) bf16 pair with x ~= hi + lo to ~2^-17 relative (full float range, no scaling needed).
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+    hi = __float2bfloat16_rn(x);
+    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+
+// Instruction descriptor of kind::f16 with bf16 A/B and f32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace tc
@@ -169,4 +201,15 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst_saddr, const void* tmap
 }
 
 }  // namespace tc
+}  // namespace g2v
+
+namespace g2v {
+// Parameters of one Gaussian as five 16-byte words: (mean, opacity), P[0..3], P[4..7], (P[8], lb.xyz),
+// (ub.xyz, pad); lb/ub are int32 bit patterns.  Built by launch_pack_params, read by the tensor-core
+// kernels with 16-byte loads.
+struct __align__(16) GParams {
+    float4 w[5];
+};
+int launch_pack_params(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
+                       const int32_t* ub, int64_t n, GParams* out, cudaStream_t s);
 }  // namespace g2v

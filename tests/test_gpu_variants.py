@@ -67,3 +67,55 @@ def test_device_error_word_is_clear():
     _lib.check(_lib.load().g2v_device_error(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(w)),
                "g2v_device_error")
     assert w.value == 0
+
+
+def _with_variant(variant, fn):
+    old = os.environ.get("G2V_VARIANT")
+    os.environ["G2V_VARIANT"] = variant
+    try:
+        out = fn()
+        torch.cuda.synchronize()
+    finally:
+        if old is None:
+            del os.environ["G2V_VARIANT"]
+        else:
+            os.environ["G2V_VARIANT"] = old
+    return out
+
+
+@pytest.mark.parametrize("n,c,seed,half,var_max,xt", [
+    (300, 24, 1, 6.0, 2.5, None),      # one slot pass, one channel group
+    (2000, 37, 2, 8.0, 2.5, None),     # C not a multiple of 4 (scalar gradient loads)
+    (3000, 300, 3, 6.0, 8.0, None),    # > 256 Gaussians per block (several slot passes), 2 channel groups
+    (4000, 520, 4, 10.0, 2.5, (3, 9)),  # x-slab of tiles (partial rows of blocks cut by the slab)
+])
+def test_tensor_core_backward_matches_oracle_and_fp32_variant(n, c, seed, half, var_max, xt):
+    from CudaGaussianVoxelizer import _C
+    size, rng = [0.4] * 3, [-half, -half, -1.0, half, half, 5.4]
+    m, o, cv, f = oracle.generate_inputs(n, c, rng, seed=seed, num_outside=n // 20, var_max=var_max)
+    m, o, cv, f = m.numpy(), o.numpy(), cv.numpy(), f.numpy()
+    dims = oracle.grid_shape(size, rng)[0]
+    g = torch.Generator().manual_seed(seed + 3)
+    gD = torch.randn(*dims, generator=g)
+    gF = torch.randn(*dims, c, generator=g)
+    mt, ot, ct, ft = dev(m, o, cv, f)
+    out = _C.gaussian_voxelizer_forward(mt, ot, ct, size, rng, ft)
+    density, cov_inv, lb, ub, nvox, grid_feats, off, ids, _ = out
+    gDt, gFt = gD.cuda(), gF.cuda()
+
+    def bwd():
+        return [t.cpu().numpy() for t in _C.gaussian_voxelizer_backward(
+            gDt, gFt, mt, ot, cov_inv, size, rng, lb, ub, nvox, off, ids, density, grid_feats, ft,
+            tile_x_range=xt)[:4]]
+
+    tc = _with_variant("tc", bwd)
+    fp = _with_variant("simt", bwd)
+    names = ("grad_means", "grad_cov", "grad_opacity", "grad_features")
+    for name, a, b in zip(names, tc, fp):
+        assert_close(f"{name} tc vs simt", a, b)
+    xr = None if xt is None else (xt[0] * 4, min(xt[1] * 4, dims[0]))
+    lb_h, ub_h = lb.cpu().numpy(), ub.cpu().numpy()
+    dref, fref = oracle.forward(m, o, cv, f, lb_h, ub_h, size, rng, dims, x_range=xr)
+    ref = oracle.backward(m, o, cv, f, lb_h, ub_h, size, rng, dims, gD.numpy(), gF.numpy(), dref, fref, x_range=xr)
+    for name, a, b in zip(names, tc, ref):
+        assert_close(name, a, b)
