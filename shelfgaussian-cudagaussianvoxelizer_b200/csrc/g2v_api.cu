@@ -55,6 +55,11 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
                     const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
                     int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
                     int64_t block_pair_cap, int* err, cudaStream_t s);
+size_t spass_tc_split_bytes(int64_t n, int64_t C);
+int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
+                    const float* density, const GParams* gparams, const int32_t* g2t_offsets,
+                    const int32_t* tile_offsets, const int32_t* tile_lists, int first_tile, int num_tiles,
+                    const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s);
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
                     const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
                     float* grad_opacity, cudaStream_t s);
@@ -203,6 +208,7 @@ struct BackwardWs {
     float* partial10;
     float* partialF;
     GParams* gparams;
+    void* fsplit;
 };
 size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, int64_t C, BackwardWs& w) {
     Carver c(p);
@@ -223,6 +229,7 @@ size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, 
     w.partial10 = c.take<float>((size_t)(m > 0 ? m : 1) * 10);
     w.partialF = c.take<float>((size_t)(feats && mb > 0 ? mb : 1) * (size_t)(feats ? C : 1));
     w.gparams = c.take<GParams>((size_t)(n > 0 ? n : 1));
+    w.fsplit = c.take<char>(feats ? spass_tc_split_bytes(n, C) : 1);
     return c.bytes();
 }
 
@@ -540,10 +547,22 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
         return rc;
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
-    if ((rc = launch_spass(grad_density, grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub,
-                           features, C, density, g2t_offsets, w.t2g.tile_offsets, w.t2g.lists, first_tile, nt, G,
-                           w.partial10, num_pairs, s)))
+    const bool tcore = C > 0 && num_gaussians > 0 && use_tensor_cores();
+    int* err = nullptr;
+    if (tcore) {
+        if ((rc = device_error_ptr(&err))) return rc;
+        if ((rc = launch_pack_params(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, num_gaussians,
+                                     w.gparams, s)))
+            return rc;
+        if ((rc = launch_spass_tc(grad_density, grad_grid_feats, features, num_gaussians, C, density, w.gparams,
+                                  g2t_offsets, w.t2g.tile_offsets, w.t2g.lists, first_tile, nt, G, w.partial10,
+                                  num_pairs, w.fsplit, err, s)))
+            return rc;
+    } else if ((rc = launch_spass(grad_density, grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb,
+                                  valid_voxel_ub, features, C, density, g2t_offsets, w.t2g.tile_offsets, w.t2g.lists,
+                                  first_tile, nt, G, w.partial10, num_pairs, s))) {
         return rc;
+    }
     if ((rc = launch_reduce10(w.partial10, g2t_offsets, g2t_tile_ids, num_gaussians, G, tile_x_begin, tile_x_end,
                               grad_means3d, grad_covariances, grad_opacity, s)))
         return rc;
@@ -559,12 +578,7 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
                                    w.block_unsorted, w.block_lists, w.block_scan, total, s)))
             return rc;
         if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s))) return rc;
-        if (use_tensor_cores()) {
-            int* err = nullptr;
-            if ((rc = device_error_ptr(&err))) return rc;
-            if ((rc = launch_pack_params(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, num_gaussians,
-                                         w.gparams, s)))
-                return rc;
+        if (tcore) {
             if ((rc = launch_fpass_tc(grad_grid_feats, C, density, w.gparams, w.block_offsets, w.block_lists,
                                       w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1], nb[2], B, tile_x_begin,
                                       tile_x_end, G, w.partialF, num_block_pairs, err, s)))
