@@ -135,6 +135,8 @@ def make_inputs(cfg, seed):
 def algorithmic_bytes(kernel, n, c, V, M, MB, ntiles):
     """Algorithmic HBM bytes of one launch over the whole grid (per-unit figures of the design doc)."""
     per_gauss = n * (12 + 4 + 36 + 24)  # mean, opacity, cov_inv, lb/ub
+    kernel = {"splat_tc_kernel": "splat_tile_kernel", "spass_tc_kernel": "spass_kernel",
+              "fpass_tc_kernel": "fpass_kernel"}.get(kernel, kernel)
     if kernel == "splat_tile_kernel":
         return 4 * V * c + 4 * V + 4 * n * c + per_gauss + 4 * M + 4 * (ntiles + 1)
     if kernel == "spass_kernel":

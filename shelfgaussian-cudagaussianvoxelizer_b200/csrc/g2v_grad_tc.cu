@@ -13,19 +13,28 @@
 //   B = weights (256 slots x 16 voxels) K-major, no swizzle (8x8 core matrices), evaluated by the weight
 //       warps from the slot's parameters: over the 4x4 voxels of an x-slice the Mahalanobis distance is a
 //       quadratic in (ly, lz), so each weight costs a few FMAs and one exp.
-// Roles (288 threads): warps 0-3 produce A, warps 4-7 produce B, warp 8 (one thread) issues the 6 MMAs
-// of a step.  Four stages handed over through mbarriers; every wait is bounded.  The epilogue writes the
+// The fp32 gradient rows of a step (16 voxels x 256 channels, 16 KB) arrive in a staging ring through
+// one tiled TMA load of the 4-D tensor map {C, Z, Y, X} (zero fill beyond the grid and beyond C); when
+// the map cannot be built (C % 4 != 0, unaligned base) the converting threads load the rows themselves.
+// 1 / max(D, eps) of the block's voxels is computed once per CTA into shared memory.
+// Roles (320 threads): warps 0-3 convert A, warps 4-7 produce B, warp 8 (one thread) issues the 6 MMAs
+// of a step, warp 9 (one thread) issues the TMA loads.  Four operand stages and four staging stages are
+// handed over through mbarriers; every wait is bounded.  The epilogue writes the
 // per-(Gaussian, block) partial rows of the reference's dL/dfeatures; a deterministic CSR-order reduction
 // sums them per Gaussian.
 #include <cstddef>
 
+#include <cstring>
+
+#include "g2v.h"
 #include "g2v_internal.cuh"
 #include "g2v_tc.cuh"
+#include "g2v_tmap.cuh"
 
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 288;
+constexpr int kThreads = 320;
 constexpr int kSlots = 256;
 constexpr int kMB = 2;                          // M-blocks of 128 channels per CTA
 constexpr int kCG = kMB * 128;                  // channels per CTA
@@ -34,6 +43,9 @@ constexpr int kAHalf = kMB * 4096;              // one operand half, one stage
 constexpr int kBHalf = kSlots * 16 * 2;
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kGS = 4;                          // staging stages of the fp32 gradient
+constexpr int kGBytes = 16 * kCG * 4;           // 16 KB: [ly][lz][256 channels]
+constexpr int kMaxBlockTiles = 16;              // tiles per block (2 x 2 x 4)
 constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kSlots, /*A MN-major*/ 1, /*B K-major*/ 0);
 
 struct FMisc {
@@ -43,22 +55,27 @@ struct FMisc {
     uint64_t mma_done;
     uint32_t tmem_base;
     int fail;
+    uint64_t gfull[kGS];   // TMA bytes of a staged step
+    uint64_t gempty[kGS];  // 4 converter-warp arrivals
     alignas(16) GParams prm[kSlots];
     int64_t rowoff[kSlots];
+    float rden[kMaxBlockTiles * kVoxPerTile];  // 1 / max(D, eps) of the block's voxels, 0 outside the grid
 };
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(FMisc);
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(FMisc);
 static_assert(kSmemBytes <= 227 * 1024, "fpass_tc_kernel shared memory");
 static_assert(offsetof(FMisc, prm) % 16 == 0, "GParams records are read as float4");
 
+template <bool kTma>
 __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
-    const float* __restrict__ grad_feats, int C, const float* __restrict__ density, const GParams* __restrict__ gparams,
+    const __grid_constant__ CUtensorMap gmap, const float* __restrict__ grad_feats, int C, const float* __restrict__ density, const GParams* __restrict__ gparams,
     const int32_t* __restrict__ block_offsets, const int32_t* __restrict__ block_lists,
     const int32_t* __restrict__ g2b_offsets, int bx_begin, int nby, int nbz, int BX, int BY, int BZ, int tx_begin,
     int tx_end, int ngroups, int vec, Grid G, float* __restrict__ partialF, int64_t block_pair_cap,
     int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
-    FMisc& ms = *reinterpret_cast<FMisc*>(base + kStages * kStageBytes);
+    unsigned char* gstage = base + kStages * kStageBytes;
+    FMisc& ms = *reinterpret_cast<FMisc*>(gstage + kGS * kGBytes);
     if ((tc::smem_u32(smem_raw) & 1023u) != 0) {
         if (threadIdx.x == 0) atomicOr(err, 2);
         return;
@@ -91,6 +108,22 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         return;
     }
     const int nsteps = ntiles * 4;  // 4 x-slices of 16 voxels per tile
+    if (ntiles > kMaxBlockTiles) {  // the host sizes blocks within the limit
+        if (tid == 0) atomicOr(err, 4);
+        return;
+    }
+    // 1 / max(D, eps) of every voxel of the block's tiles (tile order of the steps)
+    for (int i = tid; i < ntiles * kVoxPerTile; i += kThreads) {
+        const int t = i >> 6;
+        int lx, ly, lz;
+        local_voxel(i & 63, lx, ly, lz);
+        const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
+        const int x = (txa + txi) * kTile + lx, y = (tya + tyi) * kTile + ly, z = (tza + tzi) * kTile + lz;
+        float r = 0.0f;
+        if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
+            r = 1.0f / fmaxf(density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z], kEps);
+        ms.rden[i] = r;
+    }
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -99,6 +132,10 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             tc::mbar_init(&ms.empty[i], 1);
         }
         tc::mbar_init(&ms.mma_done, 1);
+        for (int i = 0; i < kGS; ++i) {
+            tc::mbar_init(&ms.gfull[i], 1);
+            tc::mbar_init(&ms.gempty[i], 4);
+        }
         tc::mbar_fence_init();
         ms.fail = 0;
     }
@@ -124,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     };
 
     int it = 0;  // global step counter across passes (stage / parity bookkeeping)
+    int issued = 0;  // TMA thread: staged steps issued
     const int npass = (Kb + kSlots - 1) / kSlots;
     for (int pass = 0; pass < npass; ++pass) {
         const int p0 = pass * kSlots, ns = min(kSlots, Kb - p0);
@@ -151,45 +189,54 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         __syncthreads();
 
         if (warp < 4) {
-            // ---------------- producers: A = gF^T, thread = (voxel row r of the step, 32-channel chunk) ----
-            const int r = tid >> 3, ch = (tid & 7) * 32;  // 16 rows x 8 chunks
-            const int ly_r = r >> 2, lz_r = r & 3;
+            // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 4 voxel rows) ----------
+            const int jc = lane;                                     // channels c0 + 8 jc .. + 7
+            const int mb = jc >> 4, a = (jc >> 3) & 1, jj = jc & 7;
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                const int st = it % kStages;
+                const int st = it % kStages, gs = it % kGS;
                 int x0, y0, z0, ks;
                 step_geom(j, x0, y0, z0, ks);
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
+                if (kTma && ok) ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
                 if (!ok) break;
-                const int x = x0 + ks, y = y0 + ly_r, z = z0 + lz_r;
-                const bool vok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
-                const int64_t row = ((int64_t)x * G.dims[1] + y) * G.dims[2] + z;
-                const float* src = grad_feats + row * C + c0 + ch;
-                const int mb = ch >> 7, a = (ch >> 6) & 1;
-                const int g8 = r >> 3, rr = r & 7;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {  // 8 channels per 16-byte chunk
-                    const int c = c0 + ch + q * 8;
+                for (int i = 0; i < 4; ++i) {
+                    const int r = warp * 4 + i;  // voxel row of the step: (ly, lz) = (r / 4, r % 4)
                     float f[8];
-                    if (vok && c + 7 < C && vec) {
-                        const float4 u = *reinterpret_cast<const float4*>(src + q * 8);
-                        const float4 w4 = *reinterpret_cast<const float4*>(src + q * 8 + 4);
+                    if (kTma) {
+                        const float4* src = reinterpret_cast<const float4*>(gstage + gs * kGBytes + r * (kCG * 4) + jc * 32);
+                        const float4 u = src[0], w4 = src[1];
                         f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
                         f[4] = w4.x; f[5] = w4.y; f[6] = w4.z; f[7] = w4.w;
                     } else {
+                        const int x = x0 + ks, y = y0 + (r >> 2), z = z0 + (r & 3);
+                        const bool vok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
+                        const int c = c0 + jc * 8;
+                        const float* src = grad_feats + (((int64_t)x * G.dims[1] + y) * G.dims[2] + z) * C + c;
+                        if (vok && c + 7 < C && vec) {
+                            const float4 u = *reinterpret_cast<const float4*>(src);
+                            const float4 w4 = *reinterpret_cast<const float4*>(src + 4);
+                            f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+                            f[4] = w4.x; f[5] = w4.y; f[6] = w4.z; f[7] = w4.w;
+                        } else {
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) f[e] = (vok && c + e < C) ? src[q * 8 + e] : 0.0f;
+                            for (int e = 0; e < 8; ++e) f[e] = (vok && c + e < C) ? src[e] : 0.0f;
+                        }
                     }
                     __align__(16) __nv_bfloat16 h[8], l[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) tc::split_bf16(f[e], h[e], l[e]);
-                    const int jj = ((ch & 63) >> 3) + q;  // 16-byte chunk within the 64-channel atom row
+                    const int g8 = r >> 3, rr = r & 7;
                     const int off = mb * 4096 + a * 1024 + g8 * 2048 + rr * 128 + ((jj ^ rr) << 4);
                     *reinterpret_cast<uint4*>(a_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(h);
                     *reinterpret_cast<uint4*>(a_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(l);
                 }
                 tc::fence_async_smem();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&ms.full_a[st]);
+                if (lane == 0) {
+                    tc::mbar_arrive(&ms.full_a[st]);
+                    if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
+                }
             }
         } else if (warp < 8) {
             // ---------------- weight warps: thread = slots (t, t + 128), 16 voxels of the x-slice -------
@@ -201,13 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                 if (!ok) break;
                 const int x = x0 + ks;
-                // 1 / max(D, eps) of the 16 voxels (ly, lz): lanes 0..15 load one each
-                float rd = 0.0f;
-                if (lane < 16) {
-                    const int y = y0 + (lane >> 2), z = z0 + (lane & 3);
-                    if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
-                        rd = 1.0f / fmaxf(density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z], kEps);
-                }
+                // 1 / max(D, eps) of the 16 voxels (ly, lz) of the slice: lanes 0..15 hold one each
+                const float rd = lane < 16 ? ms.rden[(j >> 2) * kVoxPerTile + ks * 16 + lane] : 0.0f;
                 const float cx = voxel_centre(G, 0, x), cy0 = voxel_centre(G, 1, y0), cz0 = voxel_centre(G, 2, z0);
                 const float hy = G.h[1], hz = G.h[2];
 #pragma unroll
@@ -259,7 +301,19 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
             }
-        } else if (lane == 0) {
+        } else if (kTma && warp == 9 && lane == 0) {
+            // ---------------- TMA thread: the step's gradient rows into the staging ring ----------------
+            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                const int gs = it % kGS;
+                int x0, y0, z0, ks;
+                step_geom(j, x0, y0, z0, ks);
+                if (it >= kGS) ok = tc::mbar_wait(&ms.gempty[gs], ((it / kGS) + 1) & 1, err);
+                if (!ok) break;
+                tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
+                tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, c0, z0, y0, x0 + ks, &ms.gfull[gs]);
+                issued = it + 1;
+            }
+        } else if (warp == 8 && lane == 0) {
             // ---------------- MMA thread ----------------
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
@@ -313,6 +367,10 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         __syncthreads();
         tc::tc_fence_after();
     }
+    // no copy may still be in flight when the CTA's shared memory is released (matters after a wait gave up)
+    if (kTma && warp == 9 && lane == 0)
+        for (int k = max(0, issued - kGS); k < issued; ++k) tc::mbar_wait_drain(&ms.gfull[k % kGS], (k / kGS) & 1, err);
+    __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 }  // namespace
@@ -325,11 +383,19 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
     if (nblocks <= 0 || C <= 0) return 0;
     const int ngroups = (C + kCG - 1) / kCG;
     const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0);
-    G2V_CUDA(cudaFuncSetAttribute(fpass_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    if (B[0] * B[1] * B[2] > kMaxBlockTiles) {
+        set_error("fpass_tc: block of %dx%dx%d tiles exceeds %d", B[0], B[1], B[2], kMaxBlockTiles);
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    CUtensorMap gmap;
+    memset(&gmap, 0, sizeof(gmap));
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kCG, kTile, kTile, 1);
+    auto kern = tma ? fpass_tc_kernel<true> : fpass_tc_kernel<false>;
+    G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int64_t grid = nblocks * ngroups;
     G2V_TIMED("fpass_tc_kernel", s,
-              fpass_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(
-                  grad_feats, C, density, gparams, block_offsets, block_lists, g2b_offsets, bx_begin, nby, nbz, B[0],
+              kern<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(
+                  gmap, grad_feats, C, density, gparams, block_offsets, block_lists, g2b_offsets, bx_begin, nby, nbz, B[0],
                   B[1], B[2], tx_begin, tx_end, ngroups, vec, G, partialF, block_pair_cap, err));
     G2V_LAUNCH_CHECK("fpass_tc_kernel");
     return 0;

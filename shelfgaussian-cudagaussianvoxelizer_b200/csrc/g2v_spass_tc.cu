@@ -15,21 +15,29 @@
 // hi/lo by the producer threads.  hi*hi + hi*lo + lo*hi is accumulated in fp32 (~2^-16 relative per
 // product; bf16 keeps the fp32 exponent range, so no scaling is needed).
 //
-// Roles (288 threads): warps 0-7 produce both operands, warp 8 (one thread) issues the MMAs; after a
-// pass's MMAs have drained, warps 0-7 run the epilogue with one thread per Gaussian slot (TMEM lane).
+// The upstream gradient of a step (the tile's 4x4x4 voxels x 32 channels, 8 KB) arrives in a staging
+// ring through one tiled TMA load of the 4-D tensor map {C, Z, Y, X} (zero fill beyond the grid), so the
+// HBM latency is hidden by the ring instead of stalling the converting threads; when the tensor map
+// cannot be built (C % 4 != 0, unaligned base) the converting threads load the rows themselves.
+//
+// Roles (320 threads): warps 0-7 copy the feature rows and convert the staged gradient rows, warp 8
+// (one thread) issues the MMAs, warp 9 (one thread) issues the TMA loads; after a pass's MMAs have
+// drained, warps 0-7 run the epilogue with one thread per Gaussian slot (TMEM lane).
 // Tiles with at most 512 Gaussians keep all of S in TMEM (two passes x 128 columns); longer lists run
 // two sweeps (phase 1 over all passes, then the MMAs again for phase 2).  Two CTAs share an SM so that
 // one's epilogue overlaps the other's main loop.  Every mbarrier wait is bounded.
 #include <algorithm>
 #include <cstddef>
+#include <cstring>
 
 #include "g2v_internal.cuh"
 #include "g2v_tc.cuh"
+#include "g2v_tmap.cuh"
 
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 288;
+constexpr int kThreads = 320;
 constexpr int kSlots = 256;                       // Gaussians per pass
 constexpr int kKC = 32;                           // channels per pipeline step
 constexpr int kStages = 2;
@@ -38,6 +46,8 @@ constexpr int kBHalf = kVoxPerTile * kKC * 2;     // 4 KB: 64 rows x 64 bytes
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
 constexpr int kRowGroupBytes = (kKC / 8) * 128;   // 8 rows x kKC channels: 4 core matrices along K
 constexpr int kMBlockBytes = 16 * kRowGroupBytes; // 128 rows
+constexpr int kGS = 3;                            // staging stages of the fp32 gradient
+constexpr int kGBytes = kVoxPerTile * kKC * 4;    // 8 KB: [x][y][z][32 channels]
 constexpr uint32_t kTmemCols = 256;
 constexpr int kKeepPasses = 2;                    // passes whose S stays in TMEM (128 columns each)
 constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kVoxPerTile, /*A K-major*/ 0, /*B K-major*/ 0);
@@ -47,13 +57,15 @@ struct SMisc {
     uint64_t full_b[kStages];  // 8 warp arrivals (gradient rows)
     uint64_t empty[kStages];   // MMA commit
     uint64_t mma_done;
+    uint64_t gfull[kGS];       // TMA bytes of a staged gradient step
+    uint64_t gempty[kGS];      // 8 converter-warp arrivals
     uint32_t tmem_base;
     int fail;
     float gD[kVoxPerTile], rden[kVoxPerTile], act[kVoxPerTile], e[kVoxPerTile];
     float epart[8][kVoxPerTile];
     int64_t vrow[kVoxPerTile];  // linear voxel index, -1 outside the grid
 };
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(SMisc);
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(SMisc);
 static_assert(kSmemBytes * 2 + 2048 <= 228 * 1024, "spass_tc_kernel: two CTAs per SM");
 
 // 16 per-lane values -> each lane pair (2i, 2i+1) holds the warp sum of value i (fixed order).
@@ -88,15 +100,18 @@ __device__ __forceinline__ float warp_reduce_scatter16(float (&p)[16], int lane)
     return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);  // value index (lane >> 1)
 }
 
+template <bool kTma>
 __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
-    const float* __restrict__ grad_density, const float* __restrict__ grad_feats,
+    const __grid_constant__ CUtensorMap gmap, const float* __restrict__ grad_density,
+    const float* __restrict__ grad_feats,
     const __nv_bfloat16* __restrict__ Fh, const __nv_bfloat16* __restrict__ Fl, int C, int Cp, int vec,
     const float* __restrict__ density, const GParams* __restrict__ gparams, const int32_t* __restrict__ g2t_offsets,
     const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ tile_lists, int first_tile, Grid G,
     float* __restrict__ partial10, int64_t pair_cap, int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
-    SMisc& ms = *reinterpret_cast<SMisc*>(base + kStages * kStageBytes);
+    unsigned char* gstage = base + kStages * kStageBytes;
+    SMisc& ms = *reinterpret_cast<SMisc*>(gstage + kGS * kGBytes);
     if ((tc::smem_u32(smem_raw) & 127u) != 0) {  // never expected; fail loudly
         if (threadIdx.x == 0) atomicOr(err, 2);
         return;
@@ -130,6 +145,10 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
             tc::mbar_init(&ms.empty[i], 1);
         }
         tc::mbar_init(&ms.mma_done, 1);
+        for (int i = 0; i < kGS; ++i) {
+            tc::mbar_init(&ms.gfull[i], 1);
+            tc::mbar_init(&ms.gempty[i], 8);
+        }
         tc::mbar_fence_init();
         ms.fail = 0;
     }
@@ -145,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
     const int64_t pitch = (int64_t)Cp * 2;  // bytes per split feature row
     bool ok = true;
     int it = 0;   // pipeline step counter (stage / parity bookkeeping), the same in every role
+    int issued = 0;  // TMA thread: staged steps issued
     int ndone = 0;  // completed mma_done phases
 
     auto a_half = [&](int st, int hl) -> uint32_t { return tc::smem_u32(base + st * kStageBytes + hl * kAHalf); };
@@ -188,8 +208,16 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
                 tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
                 // B: 8 channels of the voxel's gradient row -> bf16 hi / lo
                 const int c = c0 + kcb * 8;
+                const int gs = it % kGS;
                 float f[8];
-                if (vrow >= 0 && vec && c + 7 < C) {
+                if (kTma) {
+                    ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
+                    if (!ok) break;
+                    const float4* src = reinterpret_cast<const float4*>(gstage + gs * kGBytes + v * (kKC * 4) + kcb * 32);
+                    const float4 u0 = src[0], u1 = src[1];
+                    f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
+                    f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
+                } else if (vrow >= 0 && vec && c + 7 < C) {
                     const float4 u0 = *reinterpret_cast<const float4*>(grad_feats + vrow * C + c);
                     const float4 u1 = *reinterpret_cast<const float4*>(grad_feats + vrow * C + c + 4);
                     f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
@@ -211,9 +239,22 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
                              : "memory");
                 tc::fence_async_smem();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&ms.full_b[st]);
+                if (lane == 0) {
+                    tc::mbar_arrive(&ms.full_b[st]);
+                    if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
+                }
             }
-        } else if (lane == 0) {
+        } else if (kTma && warp == 9 && lane == 0) {
+            // ---- TMA thread: the gradient box of each step into the staging ring ----
+            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                const int gs = it % kGS;
+                if (it >= kGS) ok = tc::mbar_wait(&ms.gempty[gs], ((it / kGS) + 1) & 1, err);
+                if (!ok) break;
+                tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
+                tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, j * kKC, z0, y0, x0, &ms.gfull[gs]);
+                issued = it + 1;
+            }
+        } else if (warp == 8 && lane == 0) {
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
                 const uint32_t par = (it / kStages) & 1;
@@ -409,6 +450,10 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
             sync_tc();
         }
     }
+    // no copy may still be in flight when the CTA's shared memory is released (matters after a wait gave up)
+    if (kTma && warp == 9 && lane == 0)
+        for (int k = max(0, issued - kGS); k < issued; ++k) tc::mbar_wait_drain(&ms.gfull[k % kGS], (k / kGS) & 1, err);
+    tc::cp_async_wait<0>();
     sync_tc();
     if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
@@ -456,10 +501,14 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
         G2V_LAUNCH_CHECK("feature_split_bf16_kernel");
     }
     const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0);
-    G2V_CUDA(cudaFuncSetAttribute(spass_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    CUtensorMap gmap;
+    memset(&gmap, 0, sizeof(gmap));
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kKC, kTile, kTile, kTile);
+    auto kern = tma ? spass_tc_kernel<true> : spass_tc_kernel<false>;
+    G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     G2V_TIMED("spass_tc_kernel", s,
-              spass_tc_kernel<<<(unsigned)num_tiles, kThreads, kSmemBytes, s>>>(
-                  grad_density, grad_feats, Fh, Fl, C, Cp, vec, density, gparams, g2t_offsets, tile_offsets,
+              kern<<<(unsigned)num_tiles, kThreads, kSmemBytes, s>>>(
+                  gmap, grad_density, grad_feats, Fh, Fl, C, Cp, vec, density, gparams, g2t_offsets, tile_offsets,
                   tile_lists, first_tile, G, partial10, pair_cap, err));
     G2V_LAUNCH_CHECK("spass_tc_kernel");
     return 0;

@@ -12,6 +12,9 @@ namespace tc {
 
 // Error bit set in the caller-provided device error word when a bounded wait gives up.
 constexpr int kErrWaitTimeout = 1;
+// Suspend-time hint of one try_wait (ns) and the limit of one bounded wait (ns).
+constexpr uint32_t kWaitHintNs = 1000000u;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -92,41 +95,53 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
-// Wait until the phase with the given parity has completed.  Bounded: after ~2^22 polls it records
-// kErrWaitTimeout in *err and returns false instead of spinning forever; once any wait of any CTA has
-// given up (*err != 0), every later wait returns false at once so that the whole grid drains quickly.
+// Global nanosecond timer (bounds of the waits below).
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// One try_wait with a suspend-time hint: the thread sleeps until the phase completes (or the hint
+// elapses) instead of returning at once, so hand-offs cost no polling loop.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_saddr, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar_saddr), "r"(parity), "r"(kWaitHintNs)
+        : "memory");
+    return done != 0;
+}
+
+// Wait until the phase with the given parity has completed.  Bounded: after kWaitLimitNs of waiting it
+// records kErrWaitTimeout in *err and returns false instead of waiting forever; once any wait of any CTA
+// has given up (*err != 0), later waits that do not complete at once return false, so that the whole
+// grid drains quickly.  The error word (global memory) is read only on that slow path.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t it = 0; it < (1u << 22); ++it) {
-        if ((it & 1023u) == 0 && *reinterpret_cast<volatile int*>(err) != 0) return false;
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+        if (global_ns() - t0 > kWaitLimitNs) break;
     }
     atomicOr(err, kErrWaitTimeout);
     return false;
 }
 
-// Wait for a commit that is always issued (the end-of-work commit of the MMA thread), also after another
-// wait has given up, so that no MMA is in flight when the kernel frees its TMEM.  Bounded like mbar_wait.
+// Wait for a commit that is always issued (the end-of-work commit of the MMA thread, the completion of
+// a copy already issued), also after another wait has given up, so that nothing is in flight when the
+// kernel frees its TMEM or shared memory.  Bounded like mbar_wait; returns false when *err is set.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t it = 0; it < (1u << 22); ++it) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return *reinterpret_cast<volatile int*>(err) == 0;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(a, parity)) return *reinterpret_cast<volatile int*>(err) == 0;
+        if (global_ns() - t0 > kWaitLimitNs) break;
     }
     atomicOr(err, kErrWaitTimeout);
     return false;
@@ -197,6 +212,17 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst_saddr, const void* tmap
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst_saddr),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Tiled 4-D load of one box at coordinates (c0 innermost .. c3) into shared memory; completion is
+// counted in bytes on `bar`.  c0 * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst_saddr, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst_saddr),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
         : "memory");
 }
 
