@@ -16,9 +16,11 @@
 // The fp32 gradient rows of a step (16 voxels x 256 channels, 16 KB) arrive in a staging ring through
 // one tiled TMA load of the 4-D tensor map {C, Z, Y, X} (zero fill beyond the grid and beyond C); when
 // the map cannot be built (C % 4 != 0, unaligned base) the converting threads load the rows themselves.
-// 1 / max(D, eps) of the block's voxels is computed once per CTA into shared memory.
-// Roles (320 threads): warps 0-3 convert A, warps 4-7 produce B, warp 8 (one thread) issues the 6 MMAs
-// of a step, warp 9 (one thread) issues the TMA loads.  Four operand stages and four staging stages are
+// log2(1 / max(D, eps)) of the block's voxels is computed once per CTA into shared memory and folded,
+// with the box masks (-inf), into the base-2 exponent of each weight: w / den = o * 2^(quadratic + L_v).
+// Roles (576 threads): warps 0-7 convert A (two voxel rows each), warps 8-15 produce B (one Gaussian
+// slot per thread), warp 16 (one thread) issues the 6 MMAs of a step, warp 17 (one thread) issues the
+// TMA loads; two warps of each producer role per scheduler hide the latency of the dependent math.  Four operand stages and four staging stages are
 // handed over through mbarriers; every wait is bounded.  The epilogue writes the
 // per-(Gaussian, block) partial rows of the reference's dL/dfeatures; a deterministic CSR-order reduction
 // sums them per Gaussian.
@@ -34,7 +36,7 @@
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;
 constexpr int kSlots = 256;
 constexpr int kMB = 2;                          // M-blocks of 128 channels per CTA
 constexpr int kCG = kMB * 128;                  // channels per CTA
@@ -46,7 +48,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr int kGS = 4;                          // staging stages of the fp32 gradient
 constexpr int kGBytes = 16 * kCG * 4;           // 16 KB: [ly][lz][256 channels]
 constexpr int kMaxBlockTiles = 16;              // tiles per block (2 x 2 x 4)
-constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kSlots, /*A MN-major*/ 1, /*B K-major*/ 0);
+// N of a pass = its slot count rounded up to 16 (a pass that is not full issues narrower MMAs)
 
 struct FMisc {
     uint64_t full_a[kStages];
@@ -56,10 +58,11 @@ struct FMisc {
     uint32_t tmem_base;
     int fail;
     uint64_t gfull[kGS];   // TMA bytes of a staged step
-    uint64_t gempty[kGS];  // 4 converter-warp arrivals
+    uint64_t gempty[kGS];  // 8 converter-warp arrivals
     alignas(16) GParams prm[kSlots];
     int64_t rowoff[kSlots];
-    float rden[kMaxBlockTiles * kVoxPerTile];  // 1 / max(D, eps) of the block's voxels, 0 outside the grid
+    alignas(16) float lrd[kMaxBlockTiles * kVoxPerTile];  // log2(1 / max(D, eps)), -inf outside the grid
+    int4 org[kMaxBlockTiles];  // voxel origin of each tile of the block, in step order
 };
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(FMisc);
 static_assert(kSmemBytes <= 227 * 1024, "fpass_tc_kernel shared memory");
@@ -112,29 +115,33 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         if (tid == 0) atomicOr(err, 4);
         return;
     }
-    // 1 / max(D, eps) of every voxel of the block's tiles (tile order of the steps)
+    // log2(1 / max(D, eps)) of every voxel of the block's tiles (tile order of the steps)
     for (int i = tid; i < ntiles * kVoxPerTile; i += kThreads) {
         const int t = i >> 6;
         int lx, ly, lz;
         local_voxel(i & 63, lx, ly, lz);
         const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
         const int x = (txa + txi) * kTile + lx, y = (tya + tyi) * kTile + ly, z = (tza + tzi) * kTile + lz;
-        float r = 0.0f;
+        float r = -INFINITY;
         if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
-            r = 1.0f / fmaxf(density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z], kEps);
-        ms.rden[i] = r;
+            r = -log2f(fmaxf(density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z], kEps));
+        ms.lrd[i] = r;
+    }
+    for (int t = tid; t < ntiles; t += kThreads) {
+        const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
+        ms.org[t] = make_int4((txa + txi) * kTile, (tya + tyi) * kTile, (tza + tzi) * kTile, 0);
     }
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
-            tc::mbar_init(&ms.full_a[i], 4);
-            tc::mbar_init(&ms.full_w[i], 4);
+            tc::mbar_init(&ms.full_a[i], 8);
+            tc::mbar_init(&ms.full_w[i], 8);
             tc::mbar_init(&ms.empty[i], 1);
         }
         tc::mbar_init(&ms.mma_done, 1);
         for (int i = 0; i < kGS; ++i) {
             tc::mbar_init(&ms.gfull[i], 1);
-            tc::mbar_init(&ms.gempty[i], 4);
+            tc::mbar_init(&ms.gempty[i], 8);
         }
         tc::mbar_fence_init();
         ms.fail = 0;
@@ -152,12 +159,11 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     };
     // tile and x-slice of step j of a pass
     auto step_geom = [&](int j, int& x0, int& y0, int& z0, int& ks) {
-        const int t = j >> 2;
+        const int4 o = ms.org[j >> 2];
         ks = j & 3;
-        const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
-        x0 = (txa + txi) * kTile;
-        y0 = (tya + tyi) * kTile;
-        z0 = (tza + tzi) * kTile;
+        x0 = o.x;
+        y0 = o.y;
+        z0 = o.z;
     };
 
     int it = 0;  // global step counter across passes (stage / parity bookkeeping)
@@ -165,6 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     const int npass = (Kb + kSlots - 1) / kSlots;
     for (int pass = 0; pass < npass; ++pass) {
         const int p0 = pass * kSlots, ns = min(kSlots, Kb - p0);
+        const int nn = (ns + 15) & ~15;  // MMA N of this pass
+        const uint32_t idesc = tc::idesc_bf16_f32(128, nn, /*A MN-major*/ 1, /*B K-major*/ 0);
         // slot parameters and partial-row offsets for this pass
         for (int i = tid; i < kSlots * 5; i += kThreads) {
             const int sl = i / 5, wq = i - sl * 5;
@@ -188,8 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         }
         __syncthreads();
 
-        if (warp < 4) {
-            // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 4 voxel rows) ----------
+        if (warp < 8) {
+            // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 2 voxel rows) ----------
             const int jc = lane;                                     // channels c0 + 8 jc .. + 7
             const int mb = jc >> 4, a = (jc >> 3) & 1, jj = jc & 7;
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
@@ -200,8 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 if (kTma && ok) ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
                 if (!ok) break;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int r = warp * 4 + i;  // voxel row of the step: (ly, lz) = (r / 4, r % 4)
+                for (int i = 0; i < 2; ++i) {
+                    const int r = warp * 2 + i;  // voxel row of the step: (ly, lz) = (r / 4, r % 4)
                     float f[8];
                     if (kTma) {
                         const float4* src = reinterpret_cast<const float4*>(gstage + gs * kGBytes + r * (kCG * 4) + jc * 32);
@@ -223,13 +231,15 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                             for (int e = 0; e < 8; ++e) f[e] = (vok && c + e < C) ? src[e] : 0.0f;
                         }
                     }
-                    __align__(16) __nv_bfloat16 h[8], l[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) tc::split_bf16(f[e], h[e], l[e]);
+                    uint4 h, l;
+                    tc::split_bf16x2(f[0], f[1], h.x, l.x);
+                    tc::split_bf16x2(f[2], f[3], h.y, l.y);
+                    tc::split_bf16x2(f[4], f[5], h.z, l.z);
+                    tc::split_bf16x2(f[6], f[7], h.w, l.w);
                     const int g8 = r >> 3, rr = r & 7;
                     const int off = mb * 4096 + a * 1024 + g8 * 2048 + rr * 128 + ((jj ^ rr) << 4);
-                    *reinterpret_cast<uint4*>(a_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(h);
-                    *reinterpret_cast<uint4*>(a_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(l);
+                    *reinterpret_cast<uint4*>(a_stage(st, 0) + off) = h;
+                    *reinterpret_cast<uint4*>(a_stage(st, 1) + off) = l;
                 }
                 tc::fence_async_smem();
                 __syncwarp();
@@ -238,9 +248,9 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
                 }
             }
-        } else if (warp < 8) {
-            // ---------------- weight warps: thread = slots (t, t + 128), 16 voxels of the x-slice -------
-            const int t = tid - 128;
+        } else if (warp < 16) {
+            // ---------------- weight warps: thread = slot t, the 16 voxels of the step's x-slice -----------
+            const int t = tid - 256;
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
                 int x0, y0, z0, ks;
@@ -248,60 +258,66 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                 if (!ok) break;
                 const int x = x0 + ks;
-                // 1 / max(D, eps) of the 16 voxels (ly, lz) of the slice: lanes 0..15 hold one each
-                const float rd = lane < 16 ? ms.rden[(j >> 2) * kVoxPerTile + ks * 16 + lane] : 0.0f;
-                const float cx = voxel_centre(G, 0, x), cy0 = voxel_centre(G, 1, y0), cz0 = voxel_centre(G, 2, z0);
-                const float hy = G.h[1], hz = G.h[2];
+                if (t < nn) {  // rows >= N are not read by the MMAs
+                float w[16];
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int sl = t + u * 128;
-                    float w[16];
+                for (int e = 0; e < 16; ++e) w[e] = 0.0f;
+                const GParams& gp = ms.prm[t];
+                const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
+                const bool live = t < ns && x >= __float_as_int(d.y) && x <= __float_as_int(e4.x);
+                if (live) {
+                    const float cx = voxel_centre(G, 0, x), cy0 = voxel_centre(G, 1, y0), cz0 = voxel_centre(G, 2, z0);
+                    const float hy = G.h[1], hz = G.h[2];
+                    const int ylo = __float_as_int(d.z) - y0, yhi = __float_as_int(e4.y) - y0;
+                    const int zlo = __float_as_int(d.w) - z0, zhi = __float_as_int(e4.z) - z0;
+                    const float dx = cx - a.x, dy = cy0 - a.y, dz = cz0 - a.z;
+                    const float qx = b.x * dx + b.y * dy + b.z * dz;
+                    const float qy = b.w * dx + c.x * dy + c.y * dz;
+                    const float qz = c.z * dx + c.w * dy + d.x * dz;
+                    const float pty = b.y * dx + c.x * dy + c.w * dz;  // (P^T d)_y
+                    const float ptz = b.z * dx + c.y * dy + d.x * dz;  // (P^T d)_z
+                    // base-2 exponent of voxel (ly, lz):
+                    //   k (A + By ly + Qyy ly^2 + (Bz + Qyz ly) lz + Qzz lz^2) + log2(1 / den_v),  k = -log2(e) / 2
+                    const float k = tc::kNegHalfLog2e;
+                    const float A = k * (dx * qx + dy * qy + dz * qz);
+                    const float By = k * hy * (qy + pty), Bz = k * hz * (qz + ptz);
+                    const float Qyy = k * hy * hy * c.x, Qzz = k * hz * hz * d.x, Qyz = k * hy * hz * (c.y + c.w);
+                    const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[(j >> 2) * kVoxPerTile + ks * 16]);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) w[e] = 0.0f;
-                    const GParams& gp = ms.prm[sl];
-                    const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
-                    const bool live = sl < ns && x >= __float_as_int(d.y) && x <= __float_as_int(e4.x);
-                    if (live) {
-                        const int ylo = __float_as_int(d.z) - y0, yhi = __float_as_int(e4.y) - y0;
-                        const int zlo = __float_as_int(d.w) - z0, zhi = __float_as_int(e4.z) - z0;
-                        const float dx = cx - a.x, dy = cy0 - a.y, dz = cz0 - a.z;
-                        const float qx = b.x * dx + b.y * dy + b.z * dz;
-                        const float qy = b.w * dx + c.x * dy + c.y * dz;
-                        const float qz = c.z * dx + c.w * dy + d.x * dz;
-                        const float A = dx * qx + dy * qy + dz * qz;
-                        const float pty = b.y * dx + c.x * dy + c.w * dz;  // (P^T d)_y
-                        const float ptz = b.z * dx + c.y * dy + d.x * dz;  // (P^T d)_z
-                        const float By = hy * (qy + pty), Bz = hz * (qz + ptz);
-                        const float Qyy = hy * hy * c.x, Qzz = hz * hz * d.x, Qyz = hy * hz * (c.y + c.w);
+                    for (int ly = 0; ly < 4; ++ly) {
+                        const float4 L = L4[ly];  // the 4 voxels (ly, 0..3); box mask: -inf outside
+                        const float my = (ly >= ylo && ly <= yhi) ? 0.0f : -INFINITY;
+                        const float Ay = fmaf(fmaf(Qyy, (float)ly, By), (float)ly, A) + my;
+                        const float By2 = fmaf(Qyz, (float)ly, Bz);
+                        const float Lz[4] = {L.x, L.y, L.z, L.w};
 #pragma unroll
-                        for (int ly = 0; ly < 4; ++ly) {
-                            const float Ay = fmaf(fmaf(Qyy, (float)ly, By), (float)ly, A);
-                            const float By2 = fmaf(Qyz, (float)ly, Bz);
-#pragma unroll
-                            for (int lz = 0; lz < 4; ++lz) {
-                                const float m = fmaf(fmaf(Qzz, (float)lz, By2), (float)lz, Ay);
-                                const float ex = __expf(-0.5f * m);
-                                const bool in = ly >= ylo && ly <= yhi && lz >= zlo && lz <= zhi;
-                                w[ly * 4 + lz] = in ? a.w * ex : 0.0f;
-                            }
+                        for (int lz = 0; lz < 4; ++lz) {
+                            const float mz = (lz >= zlo && lz <= zhi) ? Lz[lz] : -INFINITY;
+                            const float m = fmaf(fmaf(Qzz, (float)lz, By2), (float)lz, Ay) + mz;
+                            w[ly * 4 + lz] = a.w * tc::exp2_approx(m);
                         }
                     }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) w[e] *= __shfl_sync(0xffffffffu, rd, e);
-                    __align__(16) __nv_bfloat16 h[16], l[16];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) tc::split_bf16(w[e], h[e], l[e]);
-                    const int off = (sl >> 3) * 256 + (sl & 7) * 16;
-                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off) = *reinterpret_cast<const uint4*>(h);
-                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off + 128) = *reinterpret_cast<const uint4*>(h + 8);
-                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off) = *reinterpret_cast<const uint4*>(l);
-                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off + 128) = *reinterpret_cast<const uint4*>(l + 8);
+                }
+                uint4 h0, h1, l0, l1;
+                tc::split_bf16x2(w[0], w[1], h0.x, l0.x);
+                tc::split_bf16x2(w[2], w[3], h0.y, l0.y);
+                tc::split_bf16x2(w[4], w[5], h0.z, l0.z);
+                tc::split_bf16x2(w[6], w[7], h0.w, l0.w);
+                tc::split_bf16x2(w[8], w[9], h1.x, l1.x);
+                tc::split_bf16x2(w[10], w[11], h1.y, l1.y);
+                tc::split_bf16x2(w[12], w[13], h1.z, l1.z);
+                tc::split_bf16x2(w[14], w[15], h1.w, l1.w);
+                const int off = (t >> 3) * 256 + (t & 7) * 16;
+                *reinterpret_cast<uint4*>(b_stage(st, 0) + off) = h0;
+                *reinterpret_cast<uint4*>(b_stage(st, 0) + off + 128) = h1;
+                *reinterpret_cast<uint4*>(b_stage(st, 1) + off) = l0;
+                *reinterpret_cast<uint4*>(b_stage(st, 1) + off + 128) = l1;
                 }
                 tc::fence_async_smem();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
             }
-        } else if (kTma && warp == 9 && lane == 0) {
+        } else if (kTma && warp == 17 && lane == 0) {
             // ---------------- TMA thread: the step's gradient rows into the staging ring ----------------
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int gs = it % kGS;
@@ -313,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, c0, z0, y0, x0 + ks, &ms.gfull[gs]);
                 issued = it + 1;
             }
-        } else if (warp == 8 && lane == 0) {
+        } else if (warp == 16 && lane == 0) {
             // ---------------- MMA thread ----------------
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
@@ -330,9 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     const uint64_t al = tc::smem_desc(tc::smem_u32(a_stage(st, 1)) + mb * 4096, 1024, 2048,
                                                       tc::kLayoutSw128);
                     const uint32_t dcol = tmem + mb * kSlots;
-                    tc::mma_f16_ss(dcol, ah, bh, kIdesc, j > 0);
-                    tc::mma_f16_ss(dcol, ah, blo, kIdesc, true);
-                    tc::mma_f16_ss(dcol, al, bh, kIdesc, true);
+                    tc::mma_f16_ss(dcol, ah, bh, idesc, j > 0);
+                    tc::mma_f16_ss(dcol, ah, blo, idesc, true);
+                    tc::mma_f16_ss(dcol, al, bh, idesc, true);
                 }
                 tc::mma_commit(tc::smem_u32(&ms.empty[st]));
             }
@@ -368,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         tc::tc_fence_after();
     }
     // no copy may still be in flight when the CTA's shared memory is released (matters after a wait gave up)
-    if (kTma && warp == 9 && lane == 0)
+    if (kTma && warp == 17 && lane == 0)
         for (int k = max(0, issued - kGS); k < issued; ++k) tc::mbar_wait_drain(&ms.gfull[k % kGS], (k / kGS) & 1, err);
     __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);

@@ -226,16 +226,14 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
 #pragma unroll
                     for (int e = 0; e < 8; ++e) f[e] = (vrow >= 0 && c + e < C) ? grad_feats[vrow * C + c + e] : 0.0f;
                 }
-                __align__(16) __nv_bfloat16 h[8], l[8];
+                uint32_t h[4], l[4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) tc::split_bf16(f[e], h[e], l[e]);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b_half(st, 0) + boff),
-                             "r"(reinterpret_cast<const uint32_t*>(h)[0]), "r"(reinterpret_cast<const uint32_t*>(h)[1]),
-                             "r"(reinterpret_cast<const uint32_t*>(h)[2]), "r"(reinterpret_cast<const uint32_t*>(h)[3])
+                for (int e = 0; e < 4; ++e) tc::split_bf16x2(f[2 * e], f[2 * e + 1], h[e], l[e]);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b_half(st, 0) + boff), "r"(h[0]),
+                             "r"(h[1]), "r"(h[2]), "r"(h[3])
                              : "memory");
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b_half(st, 1) + boff),
-                             "r"(reinterpret_cast<const uint32_t*>(l)[0]), "r"(reinterpret_cast<const uint32_t*>(l)[1]),
-                             "r"(reinterpret_cast<const uint32_t*>(l)[2]), "r"(reinterpret_cast<const uint32_t*>(l)[3])
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b_half(st, 1) + boff), "r"(l[0]),
+                             "r"(l[1]), "r"(l[2]), "r"(l[3])
                              : "memory");
                 tc::fence_async_smem();
                 __syncwarp();

@@ -173,6 +173,23 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bflo
     lo = __float2bfloat16_rn(x - __bfloat162float(hi));
 }
 
+// Two floats -> packed bf16x2 hi / lo words (element x0 in the low half, like consecutive bf16 in
+// memory) with x ~= hi + lo as in split_bf16; three instructions per element.
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+    const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(x1 - h1), "f"(x0 - h0));
+}
+
+// 2^x with the hardware approximation (ex2.approx.ftz).
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// -1/2 * log2(e): exp(-m/2) = 2^(kNegHalfLog2e * m).
+constexpr float kNegHalfLog2e = -0.72134752044448170368f;
+
 // Instruction descriptor of kind::f16 with bf16 A/B and f32 accumulation.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, int b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
