@@ -56,9 +56,10 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
                     int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
                     int64_t block_pair_cap, int* err, cudaStream_t s);
 size_t spass_tc_split_bytes(int64_t n, int64_t C);
+void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]);
 int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
                     const float* density, const GParams* gparams, const int32_t* g2t_offsets,
-                    const int32_t* tile_offsets, const int32_t* tile_lists, int first_tile, int num_tiles,
+                    const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
                     const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s);
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
                     const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
@@ -540,14 +541,17 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
     if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
     carve_backward(workspace, num_gaussians, num_pairs, num_block_pairs, G, C, w);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int one[3] = {1, 1, 1};
-    if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
+    const bool tcore = C > 0 && num_gaussians > 0 && use_tensor_cores();
+    // Tile->Gaussian lists for the FP32-FMA tile pass, or the lists of the tensor-core pass's units
+    // (z pairs of tiles); both fit the tile-sized buffers (fewer cells, at most M entries)
+    int cell[3] = {1, 1, 1}, ncells[3] = {G.tiles[0], G.tiles[1], G.tiles[2]};
+    if (tcore) spass_tc_unit_shape(G, cell, ncells);
+    if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
                                tile_x_end, g2t_offsets, nullptr, 0, nullptr, w.t2g.counts, w.t2g.tile_offsets,
                                w.t2g.unsorted, w.t2g.lists, w.t2g.scan, w.t2g.total, s)))
         return rc;
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
-    const bool tcore = C > 0 && num_gaussians > 0 && use_tensor_cores();
     int* err = nullptr;
     if (tcore) {
         if ((rc = device_error_ptr(&err))) return rc;
@@ -555,8 +559,8 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
                                      w.gparams, s)))
             return rc;
         if ((rc = launch_spass_tc(grad_density, grad_grid_feats, features, num_gaussians, C, density, w.gparams,
-                                  g2t_offsets, w.t2g.tile_offsets, w.t2g.lists, first_tile, nt, G, w.partial10,
-                                  num_pairs, w.fsplit, err, s)))
+                                  g2t_offsets, w.t2g.tile_offsets, w.t2g.lists, tile_x_begin, tile_x_end, G,
+                                  w.partial10, num_pairs, w.fsplit, err, s)))
             return rc;
     } else if ((rc = launch_spass(grad_density, grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb,
                                   valid_voxel_ub, features, C, density, g2t_offsets, w.t2g.tile_offsets, w.t2g.lists,

@@ -1,31 +1,32 @@
 // g2v_spass_tc.cu -- tile pass of the backward on the tensor cores (tcgen05, kind::f16, bf16).
 //
-// For one tile and the Gaussians of its list (reference ComputeGaussian2VoxelGradientTileWithFeats,
+// For the Gaussians of a tile (reference ComputeGaussian2VoxelGradientTileWithFeats,
 // src/cuda_gaussian_voxelizer.cu:1376-1482, with e_v formed from S instead of reading grid_feats):
-//   S_gv  = sum_c f_gc gF_vc                        (tensor cores, D = S in TMEM)
+//   S_gv  = sum_c f_gc gF_vc                        (tensor cores, S in TMEM)
 //   e_v   = sum_g (w_gv / den_v) S_gv               (epilogue, phase 1)
 //   a_gv  = gD_v + (S_gv - [D_v >= eps] e_v) / den_v
 //   the ten gradient partials of every (Gaussian, tile) pair = sums over the tile's voxels (phase 2),
 // written at the pair's position in the Gaussian->Tile CSR like the FP32-FMA variant (g2v_grad.cu).
 //
-// MMA shape: M = 128 Gaussians (two M-blocks = 256 "slots" per pass), N = the tile's 64 voxels,
-// K = 32 channels per pipeline step.  Both operands are K-major without swizzle (8-row x 16-byte core
-// matrices): A rows are the features, pre-split once into bf16 hi/lo rows padded to Cp channels and
-// copied with 16-byte cp.async; B rows are the upstream gradient of the voxels, converted fp32 -> bf16
-// hi/lo by the producer threads.  hi*hi + hi*lo + lo*hi is accumulated in fp32 (~2^-16 relative per
-// product; bf16 keeps the fp32 exponent range, so no scaling is needed).
+// Unit of work: a pair of z-adjacent tiles (4 x 4 x 8 = 128 voxels) with the union of their Gaussian
+// lists (ascending ids).  Pairing halves the feature-row gathers and doubles the MMA's N against the
+// per-tile shape, at the price of the Gaussians that reach only one of the two tiles.
+// MMA: M = 128 Gaussians (two M-blocks = 256 slots per pass), N = the unit's 128 voxels, K = 32
+// channels per pipeline step; both operands K-major without swizzle (8-row x 16-byte core matrices).
+// A rows are the features, pre-split once into bf16 hi/lo rows padded to Cp channels and gathered with
+// 16-byte cp.async; B rows are the upstream gradient of the unit's voxels, brought in by one tiled TMA
+// load of the 4-D tensor map {C, Z, Y, X} per step and converted fp32 -> bf16 hi/lo in shared memory
+// (zero fill beyond the grid).  hi*hi + hi*lo + lo*hi is accumulated in fp32 (~2^-16 relative per
+// product).  When the tensor map cannot be built (C % 4 != 0, unaligned base) the converting threads
+// load the gradient rows themselves.
 //
-// The upstream gradient of a step (the tile's 4x4x4 voxels x 32 channels, 8 KB) arrives in a staging
-// ring through one tiled TMA load of the 4-D tensor map {C, Z, Y, X} (zero fill beyond the grid), so the
-// HBM latency is hidden by the ring instead of stalling the converting threads; when the tensor map
-// cannot be built (C % 4 != 0, unaligned base) the converting threads load the rows themselves.
-//
-// Roles (320 threads): warps 0-7 copy the feature rows and convert the staged gradient rows, warp 8
-// (one thread) issues the MMAs, warp 9 (one thread) issues the TMA loads; after a pass's MMAs have
-// drained, warps 0-7 run the epilogue with one thread per Gaussian slot (TMEM lane).
-// Tiles with at most 512 Gaussians keep all of S in TMEM (two passes x 128 columns); longer lists run
-// two sweeps (phase 1 over all passes, then the MMAs again for phase 2).  Two CTAs share an SM so that
-// one's epilogue overlaps the other's main loop.  Every mbarrier wait is bounded.
+// Persistent CTAs (one per SM) walk the units with a fixed stride; the S of one job (a pass of a unit)
+// fills half of TMEM (256 columns), so the epilogue of one job overlaps the main loop of the next.
+// Roles (576 threads): warps 0-7 gather feature rows and convert gradient rows, warp 8 (one thread)
+// issues the MMAs, warp 9 (one thread) issues the TMA loads, warps 10-17 run the epilogue with one
+// thread per Gaussian slot (TMEM lane).  A unit of one pass is one job (phase 1 then phase 2 on the same
+// S); a longer list runs every pass twice, phase 1 over all passes first, then the MMAs again for
+// phase 2.  Every mbarrier wait is bounded.
 #include <algorithm>
 #include <cstddef>
 #include <cstring>
@@ -37,36 +38,39 @@
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;
 constexpr int kSlots = 256;                       // Gaussians per pass
 constexpr int kKC = 32;                           // channels per pipeline step
-constexpr int kStages = 2;
-constexpr int kAHalf = kSlots * kKC * 2;          // 16 KB: 256 rows x 64 bytes
-constexpr int kBHalf = kVoxPerTile * kKC * 2;     // 4 KB: 64 rows x 64 bytes
+constexpr int kStages = 3;
+constexpr int kGS = 3;                            // staging stages of the fp32 gradient
+constexpr int kUV = 128;                          // voxels of a unit: x 4, y 4, z 8 (two tiles)
+constexpr int kAHalf = kSlots * kKC * 2;          // 16 KB
+constexpr int kBHalf = kUV * kKC * 2;             // 8 KB
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
+constexpr int kGBytes = kUV * kKC * 4;            // 16 KB: [x][y][z8][32 channels]
 constexpr int kRowGroupBytes = (kKC / 8) * 128;   // 8 rows x kKC channels: 4 core matrices along K
 constexpr int kMBlockBytes = 16 * kRowGroupBytes; // 128 rows
-constexpr int kGS = 3;                            // staging stages of the fp32 gradient
-constexpr int kGBytes = kVoxPerTile * kKC * 4;    // 8 KB: [x][y][z][32 channels]
-constexpr uint32_t kTmemCols = 256;
-constexpr int kKeepPasses = 2;                    // passes whose S stays in TMEM (128 columns each)
-constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kVoxPerTile, /*A K-major*/ 0, /*B K-major*/ 0);
+constexpr uint32_t kTmemCols = 512;
+constexpr int kBufCols = 256;                     // one job: 2 M-blocks x 128 voxel columns
+constexpr int kEpiWarp0 = 10;                     // first epilogue warp
+constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kUV, /*A K-major*/ 0, /*B K-major*/ 0);
 
 struct SMisc {
     uint64_t full_a[kStages];  // 256 cp.async arrivals (feature rows)
     uint64_t full_b[kStages];  // 8 warp arrivals (gradient rows)
     uint64_t empty[kStages];   // MMA commit
-    uint64_t mma_done;
-    uint64_t gfull[kGS];       // TMA bytes of a staged gradient step
+    uint64_t gfull[kGS];       // TMA bytes of a staged step
     uint64_t gempty[kGS];      // 8 converter-warp arrivals
+    uint64_t tfull[2];         // MMA commit: a job's S is complete in TMEM buffer b
+    uint64_t tempty[2];        // 8 epilogue-warp arrivals: buffer b has been read
     uint32_t tmem_base;
-    int fail;
-    float gD[kVoxPerTile], rden[kVoxPerTile], act[kVoxPerTile], e[kVoxPerTile];
-    float epart[8][kVoxPerTile];
-    int64_t vrow[kVoxPerTile];  // linear voxel index, -1 outside the grid
+    alignas(16) float lrd[kUV];   // log2(1 / max(D, eps)), -inf outside the grid
+    alignas(16) float2 va[kUV];   // phase 2: a_gv = S_gv * va.x + va.y  (va.x = 1/den, va.y = gD - act e / den)
+    float gD[kUV], act[kUV], rden[kUV], e[kUV];
+    float epart[8][kUV];
 };
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(SMisc);
-static_assert(kSmemBytes * 2 + 2048 <= 228 * 1024, "spass_tc_kernel: two CTAs per SM");
+static_assert(kSmemBytes <= 227 * 1024, "spass_tc_kernel shared memory");
 
 // 16 per-lane values -> each lane pair (2i, 2i+1) holds the warp sum of value i (fixed order).
 __device__ __forceinline__ float warp_reduce_scatter16(float (&p)[16], int lane) {
@@ -100,14 +104,31 @@ __device__ __forceinline__ float warp_reduce_scatter16(float (&p)[16], int lane)
     return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);  // value index (lane >> 1)
 }
 
+// Named barrier of the 8 epilogue warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void epi_barrier() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Unit u of the slab -> tile coordinates (tx, ty) and z-pair index of its first tile.
+struct UnitGeom {
+    int tx, ty, tzp;
+};
+__device__ __forceinline__ UnitGeom unit_geom(int u, int ty_n, int tzp_n, int tx_begin) {
+    UnitGeom g;
+    const int yz = ty_n * tzp_n;
+    g.tx = tx_begin + u / yz;
+    const int r = u - (u / yz) * yz;
+    g.ty = r / tzp_n;
+    g.tzp = r - g.ty * tzp_n;
+    return g;
+}
+
 template <bool kTma>
-__global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
+__global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
     const __grid_constant__ CUtensorMap gmap, const float* __restrict__ grad_density,
-    const float* __restrict__ grad_feats,
-    const __nv_bfloat16* __restrict__ Fh, const __nv_bfloat16* __restrict__ Fl, int C, int Cp, int vec,
-    const float* __restrict__ density, const GParams* __restrict__ gparams, const int32_t* __restrict__ g2t_offsets,
-    const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ tile_lists, int first_tile, Grid G,
-    float* __restrict__ partial10, int64_t pair_cap, int* __restrict__ err) {
+    const float* __restrict__ grad_feats, const __nv_bfloat16* __restrict__ Fh, const __nv_bfloat16* __restrict__ Fl,
+    int C, int Cp, const float* __restrict__ density, const GParams* __restrict__ gparams,
+    const int32_t* __restrict__ g2t_offsets, const int32_t* __restrict__ unit_offsets,
+    const int32_t* __restrict__ unit_lists, int num_units, int tx_begin, Grid G, float* __restrict__ partial10,
+    int64_t pair_cap, int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
     unsigned char* gstage = base + kStages * kStageBytes;
@@ -116,343 +137,388 @@ __global__ void __launch_bounds__(kThreads, 2) spass_tc_kernel(
         if (threadIdx.x == 0) atomicOr(err, 2);
         return;
     }
-    const int tl = blockIdx.x;
-    const int s0 = tile_offsets[tl], K = tile_offsets[tl + 1] - s0;
-    if (K == 0) return;
-    const int32_t* list = tile_lists + s0;
-    int tx, ty, tz;
-    decode_tile(first_tile + tl, G, tx, ty, tz);
-    const int x0 = tx * kTile, y0 = ty * kTile, z0 = tz * kTile;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tzp_n = (G.tiles[2] + 1) / 2;
+    const int nsteps = Cp / kKC;
+    const int64_t pitch = (int64_t)Cp * 2;  // bytes per split feature row
 
-    if (tid < kVoxPerTile) {
-        int lx, ly, lz;
-        local_voxel(tid, lx, ly, lz);
-        const int x = x0 + lx, y = y0 + ly, z = z0 + lz;
-        const bool in = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
-        const int64_t row = in ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : 0;
-        const float D = in ? density[row] : 0.0f;
-        ms.vrow[tid] = in ? row : -1;
-        ms.gD[tid] = in ? grad_density[row] : 0.0f;
-        ms.rden[tid] = 1.0f / fmaxf(D, kEps);
-        ms.act[tid] = D >= kEps ? 1.0f : 0.0f;
-        ms.e[tid] = 0.0f;
-    }
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(&ms.full_a[i], 256);
             tc::mbar_init(&ms.full_b[i], 8);
             tc::mbar_init(&ms.empty[i], 1);
         }
-        tc::mbar_init(&ms.mma_done, 1);
         for (int i = 0; i < kGS; ++i) {
             tc::mbar_init(&ms.gfull[i], 1);
             tc::mbar_init(&ms.gempty[i], 8);
         }
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&ms.tfull[i], 1);
+            tc::mbar_init(&ms.tempty[i], 8);
+        }
         tc::mbar_fence_init();
-        ms.fail = 0;
     }
     if (warp == 0) tc::tmem_alloc(&ms.tmem_base, kTmemCols);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = ms.tmem_base;
-
-    const int npass = (K + kSlots - 1) / kSlots;
-    const bool keep = npass <= kKeepPasses;
-    const int nsteps = Cp / kKC;
-    const int64_t pitch = (int64_t)Cp * 2;  // bytes per split feature row
     bool ok = true;
-    int it = 0;   // pipeline step counter (stage / parity bookkeeping), the same in every role
-    int issued = 0;  // TMA thread: staged steps issued
-    int ndone = 0;  // completed mma_done phases
 
     auto a_half = [&](int st, int hl) -> uint32_t { return tc::smem_u32(base + st * kStageBytes + hl * kAHalf); };
     auto b_half = [&](int st, int hl) -> uint32_t {
         return tc::smem_u32(base + st * kStageBytes + 2 * kAHalf + hl * kBHalf);
     };
 
-    // ---- main loop of one pass: S of slots [p*256, p*256+256) into TMEM columns cg*128 .. +127 ----
-    auto mainloop = [&](int p, int cg, bool commit_done) {
-        const int ns = min(kSlots, K - p * kSlots);
-        const int nmb = ns > 128 ? 2 : 1;
-        if (warp < 8) {
-            // feature rows: thread = (row r of each 64-row quarter, 16-byte chunk kc)
-            const int kc = lane & 3;
-            int64_t goff[4];
+    if (warp < 8) {
+        // ============ producers: feature rows (cp.async) and gradient rows (staged fp32 -> bf16) ============
+        int it = 0;
+        const int kc = lane & 3;               // A: 16-byte chunk of a row
+        const int v = tid >> 1, hv = tid & 1;  // B: voxel row, 16-channel half of the step
+        const int boff0 = (v >> 3) * kRowGroupBytes + (2 * hv) * 128 + (v & 7) * 16;
+        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+            const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            if (K == 0) continue;
+            const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+            const int x = ug.tx * kTile + (v >> 5), y = ug.ty * kTile + ((v >> 3) & 3), z = ug.tzp * 8 + (v & 7);
+            const bool vin = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
+            const int64_t vrow = vin ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : -1;
+            const int npass = (K + kSlots - 1) / kSlots;
+            const int njobs = npass == 1 ? 1 : 2 * npass;
+            for (int jb = 0; jb < njobs && ok; ++jb) {
+                const int p = npass == 1 ? 0 : jb % npass;
+                const int ns = min(kSlots, K - p * kSlots);
+                const int nmb = ns > 128 ? 2 : 1;
+                int64_t goff[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int slot = u * 64 + warp * 8 + (lane >> 2);
-                goff[u] = slot < ns ? (int64_t)list[p * kSlots + slot] * pitch : -1;
-            }
-            // gradient rows: thread = (voxel v, 16-byte chunk kcb)
-            const int v = tid >> 2, kcb = tid & 3;
-            const int64_t vrow = ms.vrow[v];
-            const uint32_t boff = (v >> 3) * kRowGroupBytes + kcb * 128 + (v & 7) * 16;
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                const int st = it % kStages;
-                if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
-                if (!ok) break;
-                const int c0 = j * kKC;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int slot = u * 64 + warp * 8 + (lane >> 2);
-                    if (slot < nmb * 128) {
-                        const uint32_t aoff = (slot >> 3) * kRowGroupBytes + kc * 128 + (slot & 7) * 16;
-                        const int64_t src = goff[u] >= 0 ? goff[u] + (int64_t)(c0 + kc * 8) * 2 : 0;
-                        const uint32_t nb = goff[u] >= 0 ? 16u : 0u;
-                        tc::cp_async16(a_half(st, 0) + aoff, reinterpret_cast<const char*>(Fh) + src, nb);
-                        tc::cp_async16(a_half(st, 1) + aoff, reinterpret_cast<const char*>(Fl) + src, nb);
-                    }
+                for (int q = 0; q < 4; ++q) {
+                    const int slot = q * 64 + warp * 8 + (lane >> 2);
+                    goff[q] = slot < ns ? (int64_t)unit_lists[s0 + p * kSlots + slot] * pitch : -1;
                 }
-                tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
-                // B: 8 channels of the voxel's gradient row -> bf16 hi / lo
-                const int c = c0 + kcb * 8;
-                const int gs = it % kGS;
-                float f[8];
-                if (kTma) {
-                    ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
+                for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                    const int st = it % kStages, gs = it % kGS;
+                    if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                     if (!ok) break;
-                    const float4* src = reinterpret_cast<const float4*>(gstage + gs * kGBytes + v * (kKC * 4) + kcb * 32);
-                    const float4 u0 = src[0], u1 = src[1];
-                    f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
-                    f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
-                } else if (vrow >= 0 && vec && c + 7 < C) {
-                    const float4 u0 = *reinterpret_cast<const float4*>(grad_feats + vrow * C + c);
-                    const float4 u1 = *reinterpret_cast<const float4*>(grad_feats + vrow * C + c + 4);
-                    f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
-                    f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
-                } else {
+                    const int c0 = j * kKC;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = (vrow >= 0 && c + e < C) ? grad_feats[vrow * C + c + e] : 0.0f;
-                }
-                uint32_t h[4], l[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) tc::split_bf16x2(f[2 * e], f[2 * e + 1], h[e], l[e]);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b_half(st, 0) + boff), "r"(h[0]),
-                             "r"(h[1]), "r"(h[2]), "r"(h[3])
-                             : "memory");
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(b_half(st, 1) + boff), "r"(l[0]),
-                             "r"(l[1]), "r"(l[2]), "r"(l[3])
-                             : "memory");
-                tc::fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    tc::mbar_arrive(&ms.full_b[st]);
-                    if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
-                }
-            }
-        } else if (kTma && warp == 9 && lane == 0) {
-            // ---- TMA thread: the gradient box of each step into the staging ring ----
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                const int gs = it % kGS;
-                if (it >= kGS) ok = tc::mbar_wait(&ms.gempty[gs], ((it / kGS) + 1) & 1, err);
-                if (!ok) break;
-                tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
-                tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, j * kKC, z0, y0, x0, &ms.gfull[gs]);
-                issued = it + 1;
-            }
-        } else if (warp == 8 && lane == 0) {
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                const int st = it % kStages;
-                const uint32_t par = (it / kStages) & 1;
-                ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_b[st], par, err);
-                if (!ok) break;
-                tc::tc_fence_after();
-#pragma unroll
-                for (int ks = 0; ks < kKC / 16; ++ks) {
-                    const uint64_t bh = tc::smem_desc(b_half(st, 0) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
-                    const uint64_t bl = tc::smem_desc(b_half(st, 1) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
-                    for (int mb = 0; mb < nmb; ++mb) {
-                        const uint32_t ao = mb * kMBlockBytes + ks * 256;
-                        const uint64_t ah = tc::smem_desc(a_half(st, 0) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
-                        const uint64_t al = tc::smem_desc(a_half(st, 1) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
-                        const uint32_t d = tmem + (uint32_t)((cg * 2 + mb) * kVoxPerTile);
-                        tc::mma_f16_ss(d, ah, bh, kIdesc, j > 0 || ks > 0);
-                        tc::mma_f16_ss(d, ah, bl, kIdesc, true);
-                        tc::mma_f16_ss(d, al, bh, kIdesc, true);
-                    }
-                }
-                tc::mma_commit(tc::smem_u32(&ms.empty[st]));
-            }
-            if (commit_done) tc::mma_commit(tc::smem_u32(&ms.mma_done));
-        } else {
-            it += nsteps;
-        }
-    };
-
-    auto drain = [&]() {
-        ok = tc::mbar_wait_drain(&ms.mma_done, ndone & 1, err) && ok;
-        ++ndone;
-        if (!ok) ms.fail = 1;
-        tc::tc_fence_before();
-        __syncthreads();
-        tc::tc_fence_after();
-    };
-
-    // voxel centres of the tile along each axis
-    float cxs[kTile], cys[kTile], czs[kTile];
-#pragma unroll
-    for (int i = 0; i < kTile; ++i) {
-        cxs[i] = voxel_centre(G, 0, x0 + i);
-        cys[i] = voxel_centre(G, 1, y0 + i);
-        czs[i] = voxel_centre(G, 2, z0 + i);
-    }
-
-    // ---- phase 1: e_v += sum over the pass's slots of (w_gv / den_v) S_gv ----
-    auto phase1 = [&](int p, int cg) {
-        if (warp < 8 && !ms.fail) {
-            const int mb = warp >> 2, q = warp & 3;
-            const int slot0 = p * kSlots + mb * 128 + q * 32;
-            if (slot0 < K) {  // warp-uniform
-                const int slot = slot0 + lane;
-                const bool live = slot < K;
-                const GParams& gp = gparams[live ? list[slot] : list[0]];
-                const float4 A = gp.w[0], P0 = gp.w[1], P1 = gp.w[2], P2 = gp.w[3], U = gp.w[4];
-                const int lbx = __float_as_int(P2.y), lby = __float_as_int(P2.z), lbz = __float_as_int(P2.w);
-                const int ubx = __float_as_int(U.x), uby = __float_as_int(U.y), ubz = __float_as_int(U.z);
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((cg * 2 + mb) * kVoxPerTile);
-#pragma unroll 1
-                for (int lx = 0; lx < kTile; ++lx) {
-                    float Sv[16];
-                    tc::tmem_ld16(taddr + lx * 16, Sv);
-                    const float dx = cxs[lx] - A.x;
-                    const bool inx = live && x0 + lx >= lbx && x0 + lx <= ubx;
-#pragma unroll
-                    for (int ly = 0; ly < kTile; ++ly) {
-                        const float dy = cys[ly] - A.y;
-                        const bool iny = inx && y0 + ly >= lby && y0 + ly <= uby;
-                        const float tx_ = fmaf(P0.y, dy, P0.x * dx);
-                        const float ty_ = fmaf(P1.x, dy, P0.w * dx);
-                        const float tz_ = fmaf(P1.w, dy, P1.z * dx);
-#pragma unroll
-                        for (int lz = 0; lz < kTile; ++lz) {
-                            const float dz = czs[lz] - A.z;
-                            const float qx = fmaf(P0.z, dz, tx_), qy = fmaf(P1.y, dz, ty_), qz = fmaf(P2.x, dz, tz_);
-                            const float m = dx * qx + dy * qy + dz * qz;
-                            const bool in = iny && z0 + lz >= lbz && z0 + lz <= ubz;
-                            const int v = ly * 4 + lz;
-                            Sv[v] = in ? A.w * __expf(-0.5f * m) * ms.rden[lx * 16 + v] * Sv[v] : 0.0f;
+                    for (int q = 0; q < 4; ++q) {
+                        const int slot = q * 64 + warp * 8 + (lane >> 2);
+                        if (slot < nmb * 128) {
+                            const uint32_t aoff = (slot >> 3) * kRowGroupBytes + kc * 128 + (slot & 7) * 16;
+                            const int64_t src = goff[q] >= 0 ? goff[q] + (int64_t)(c0 + kc * 8) * 2 : 0;
+                            const uint32_t nb = goff[q] >= 0 ? 16u : 0u;
+                            tc::cp_async16(a_half(st, 0) + aoff, reinterpret_cast<const char*>(Fh) + src, nb);
+                            tc::cp_async16(a_half(st, 1) + aoff, reinterpret_cast<const char*>(Fl) + src, nb);
                         }
                     }
-                    const float r = warp_reduce_scatter16(Sv, lane);
-                    if ((lane & 1) == 0) ms.epart[warp][lx * 16 + (lane >> 1)] = r;
+                    tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
+                    // B: 16 channels of the voxel's gradient row -> bf16 hi / lo
+                    float f[16];
+                    if (kTma) {
+                        ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
+                        if (!ok) break;
+                        const float4* src =
+                            reinterpret_cast<const float4*>(gstage + gs * kGBytes + v * (kKC * 4) + hv * 64);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float4 t = src[q];
+                            f[4 * q] = t.x;
+                            f[4 * q + 1] = t.y;
+                            f[4 * q + 2] = t.z;
+                            f[4 * q + 3] = t.w;
+                        }
+                    } else {
+                        const int c = c0 + hv * 16;
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            f[e] = (vrow >= 0 && c + e < C) ? grad_feats[vrow * C + c + e] : 0.0f;
+                    }
+                    uint4 h0, h1, l0, l1;
+                    tc::split_bf16x2(f[0], f[1], h0.x, l0.x);
+                    tc::split_bf16x2(f[2], f[3], h0.y, l0.y);
+                    tc::split_bf16x2(f[4], f[5], h0.z, l0.z);
+                    tc::split_bf16x2(f[6], f[7], h0.w, l0.w);
+                    tc::split_bf16x2(f[8], f[9], h1.x, l1.x);
+                    tc::split_bf16x2(f[10], f[11], h1.y, l1.y);
+                    tc::split_bf16x2(f[12], f[13], h1.z, l1.z);
+                    tc::split_bf16x2(f[14], f[15], h1.w, l1.w);
+                    unsigned char* bst = base + st * kStageBytes + 2 * kAHalf + boff0;
+                    *reinterpret_cast<uint4*>(bst) = h0;
+                    *reinterpret_cast<uint4*>(bst + 128) = h1;
+                    *reinterpret_cast<uint4*>(bst + kBHalf) = l0;
+                    *reinterpret_cast<uint4*>(bst + kBHalf + 128) = l1;
+                    tc::fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc::mbar_arrive(&ms.full_b[st]);
+                        if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
+                    }
                 }
-            } else {
-                for (int v = lane; v < kVoxPerTile; v += 32) ms.epart[warp][v] = 0.0f;
             }
         }
-        __syncthreads();
-        if (tid < kVoxPerTile && !ms.fail) {
-            float acc = ms.epart[0][tid];
+        tc::cp_async_wait<0>();  // no copy in flight when the shared memory is released
+    } else if (warp == 8) {
+        // ============ MMA thread ============
+        if (lane == 0) {
+            int it = 0, job = 0;
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const int K = unit_offsets[u + 1] - unit_offsets[u];
+                if (K == 0) continue;
+                const int npass = (K + kSlots - 1) / kSlots;
+                const int njobs = npass == 1 ? 1 : 2 * npass;
+                for (int jb = 0; jb < njobs && ok; ++jb, ++job) {
+                    const int p = npass == 1 ? 0 : jb % npass;
+                    const int ns = min(kSlots, K - p * kSlots);
+                    const int nmb = ns > 128 ? 2 : 1;
+                    const int buf = job & 1;
+                    if (job >= 2) ok = tc::mbar_wait(&ms.tempty[buf], ((job / 2) + 1) & 1, err);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                        const int st = it % kStages;
+                        const uint32_t par = (it / kStages) & 1;
+                        ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_b[st], par, err);
+                        if (!ok) break;
+                        tc::tc_fence_after();
 #pragma unroll
-            for (int w = 1; w < 8; ++w) acc += ms.epart[w][tid];
-            ms.e[tid] += acc;
+                        for (int ks = 0; ks < kKC / 16; ++ks) {
+                            const uint64_t bh =
+                                tc::smem_desc(b_half(st, 0) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
+                            const uint64_t bl =
+                                tc::smem_desc(b_half(st, 1) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
+                            for (int mb = 0; mb < nmb; ++mb) {
+                                const uint32_t ao = mb * kMBlockBytes + ks * 256;
+                                const uint64_t ah =
+                                    tc::smem_desc(a_half(st, 0) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
+                                const uint64_t al =
+                                    tc::smem_desc(a_half(st, 1) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
+                                const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
+                                tc::mma_f16_ss(d, ah, bh, kIdesc, j > 0 || ks > 0);
+                                tc::mma_f16_ss(d, ah, bl, kIdesc, true);
+                                tc::mma_f16_ss(d, al, bh, kIdesc, true);
+                            }
+                        }
+                        tc::mma_commit(tc::smem_u32(&ms.empty[st]));
+                    }
+                    tc::mma_commit(tc::smem_u32(&ms.tfull[buf]));
+                }
+            }
         }
-        __syncthreads();
-    };
-
-    // ---- phase 2: the ten gradient partials of each slot's (Gaussian, tile) pair ----
-    auto phase2 = [&](int p, int cg) {
-        if (warp < 8 && !ms.fail) {
-            const int mb = warp >> 2, q = warp & 3;
-            const int slot0 = p * kSlots + mb * 128 + q * 32;
-            if (slot0 < K) {  // warp-uniform
-                const int slot = slot0 + lane;
+    } else if (warp == 9) {
+        // ============ TMA thread: the unit's gradient box of each step into the staging ring ============
+        if (kTma && lane == 0) {
+            int it = 0, issued = 0;
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const int K = unit_offsets[u + 1] - unit_offsets[u];
+                if (K == 0) continue;
+                const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+                const int npass = (K + kSlots - 1) / kSlots;
+                const int njobs = npass == 1 ? 1 : 2 * npass;
+                for (int jb = 0; jb < njobs && ok; ++jb) {
+                    for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                        const int gs = it % kGS;
+                        if (it >= kGS) ok = tc::mbar_wait(&ms.gempty[gs], ((it / kGS) + 1) & 1, err);
+                        if (!ok) break;
+                        tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
+                        tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, j * kKC, ug.tzp * 8,
+                                        ug.ty * kTile, ug.tx * kTile, &ms.gfull[gs]);
+                        issued = it + 1;
+                    }
+                }
+            }
+            // no copy may still be in flight when the shared memory is released
+            for (int k = max(0, issued - kGS); k < issued; ++k)
+                tc::mbar_wait_drain(&ms.gfull[k % kGS], (k / kGS) & 1, err);
+        }
+    } else {
+        // ============ epilogue warps: thread = Gaussian slot (TMEM lane) ============
+        const int et = tid - kEpiWarp0 * 32;     // 0..255
+        const int q = warp & 3;                  // TMEM lane quarter of this warp
+        const int ew = warp - kEpiWarp0;         // 0..7
+        const int mb = ew >> 2;                  // M-block
+        const int sl = mb * 128 + q * 32 + lane; // slot within a pass
+        const float k2 = tc::kNegHalfLog2e;
+        const float hz = G.h[2];
+        int job = 0;
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+            const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            if (K == 0) continue;
+            const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+            const int x0 = ug.tx * kTile, y0 = ug.ty * kTile, z0 = ug.tzp * 8;
+            // voxel data of the unit (the previous unit's epilogue is complete: barrier at its end)
+            if (et < kUV) {
+                const int x = x0 + (et >> 5), y = y0 + ((et >> 3) & 3), z = z0 + (et & 7);
+                const bool in = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
+                const int64_t row = in ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : 0;
+                const float D = in ? density[row] : 0.0f;
+                const float den = fmaxf(D, kEps);
+                ms.lrd[et] = in ? -log2f(den) : -INFINITY;
+                ms.gD[et] = in ? grad_density[row] : 0.0f;
+                ms.rden[et] = in ? 1.0f / den : 0.0f;
+                ms.act[et] = D >= kEps ? 1.0f : 0.0f;
+                ms.e[et] = 0.0f;
+            }
+            epi_barrier();
+            const float cz0 = voxel_centre(G, 2, z0);
+            const int npass = (K + kSlots - 1) / kSlots;
+            const int njobs = npass == 1 ? 1 : 2 * npass;
+            for (int jb = 0; jb < njobs; ++jb, ++job) {
+                const int p = npass == 1 ? 0 : jb % npass;
+                const bool do1 = npass == 1 || jb < npass;   // phase 1 of this job
+                const bool do2 = npass == 1 || jb >= npass;  // phase 2 of this job
+                const int buf = job & 1;
+                const bool good = ok && tc::mbar_wait(&ms.tfull[buf], (job / 2) & 1, err);
+                if (!good) ok = false;
+                tc::tc_fence_after();
+                const int slot0 = p * kSlots + mb * 128 + q * 32;  // first list index of this warp
+                const bool wact = good && slot0 < K;                 // warp-uniform
+                const int slot = p * kSlots + sl;
                 const bool live = slot < K;
-                const int g = live ? list[slot] : list[0];
+                const int g = unit_lists[s0 + (live ? slot : 0)];
                 const GParams& gp = gparams[g];
                 const float4 A = gp.w[0], P0 = gp.w[1], P1 = gp.w[2], P2 = gp.w[3], U = gp.w[4];
                 const int lbx = __float_as_int(P2.y), lby = __float_as_int(P2.z), lbz = __float_as_int(P2.w);
                 const int ubx = __float_as_int(U.x), uby = __float_as_int(U.y), ubz = __float_as_int(U.z);
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((cg * 2 + mb) * kVoxPerTile);
-                float gr[10];
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kBufCols + mb * kUV);
+                // z mask of the 8 z voxels of the unit for this Gaussian (-inf outside its box)
+                float mz[8];
 #pragma unroll
-                for (int i = 0; i < 10; ++i) gr[i] = 0.0f;
+                for (int i = 0; i < 8; ++i) mz[i] = (live && z0 + i >= lbz && z0 + i <= ubz) ? 0.0f : -INFINITY;
+                const float dz0 = cz0 - A.z;
+                // along z the exponent is a quadratic in lz: k2 (a + b lz + P8 hz^2 lz^2)
+                const float Qz = k2 * hz * hz * P2.x;
+                if (do1) {
+                    if (wact) {
 #pragma unroll 1
-                for (int lx = 0; lx < kTile; ++lx) {
-                    float Sv[16];
-                    tc::tmem_ld16(taddr + lx * 16, Sv);
-                    const float dx = cxs[lx] - A.x;
-                    const bool inx = live && x0 + lx >= lbx && x0 + lx <= ubx;
+                        for (int lx = 0; lx < kTile; ++lx) {
+                            const float dx = voxel_centre(G, 0, x0 + lx) - A.x;
+                            const bool inx = live && x0 + lx >= lbx && x0 + lx <= ubx;
+#pragma unroll 1
+                            for (int ly2 = 0; ly2 < 2; ++ly2) {
+                                float Sv[16];
+                                tc::tmem_ld16(taddr + lx * 32 + ly2 * 16, Sv);
 #pragma unroll
-                    for (int ly = 0; ly < kTile; ++ly) {
-                        const float dy = cys[ly] - A.y;
-                        const bool iny = inx && y0 + ly >= lby && y0 + ly <= uby;
-                        const float tx_ = fmaf(P0.y, dy, P0.x * dx);
-                        const float ty_ = fmaf(P1.x, dy, P0.w * dx);
-                        const float tz_ = fmaf(P1.w, dy, P1.z * dx);
+                                for (int h = 0; h < 2; ++h) {
+                                    const int ly = ly2 * 2 + h;
+                                    const float dy = voxel_centre(G, 1, y0 + ly) - A.y;
+                                    const bool iny = inx && y0 + ly >= lby && y0 + ly <= uby;
+                                    const float qx = fmaf(P0.z, dz0, fmaf(P0.y, dy, P0.x * dx));
+                                    const float qy = fmaf(P1.y, dz0, fmaf(P1.x, dy, P0.w * dx));
+                                    const float qz = fmaf(P2.x, dz0, fmaf(P1.w, dy, P1.z * dx));
+                                    const float ptz = fmaf(P2.x, dz0, fmaf(P1.y, dy, P0.z * dx));  // (P^T d)_z
+                                    const float a0 = k2 * (dx * qx + dy * qy + dz0 * qz);
+                                    const float b0 = k2 * hz * (qz + ptz);
+                                    const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[lx * 32 + ly * 8]);
+                                    const float4 La = L4[0], Lb = L4[1];
+                                    const float L[8] = {La.x, La.y, La.z, La.w, Lb.x, Lb.y, Lb.z, Lb.w};
 #pragma unroll
-                        for (int lz = 0; lz < kTile; ++lz) {
-                            const int v = ly * 4 + lz, vt = lx * 16 + v;
-                            const bool in = iny && z0 + lz >= lbz && z0 + lz <= ubz;
-                            if (in) {
-                                const float dz = czs[lz] - A.z;
-                                const float qx = fmaf(P0.z, dz, tx_), qy = fmaf(P1.y, dz, ty_),
-                                            qz = fmaf(P2.x, dz, tz_);
-                                const float m = dx * qx + dy * qy + dz * qz;
-                                const float ex = __expf(-0.5f * m);
-                                const float a = fmaf(fmaf(-ms.act[vt], ms.e[vt], Sv[v]), ms.rden[vt], ms.gD[vt]);
-                                const float aw = a * A.w * ex;
-                                gr[0] = fmaf(aw, qx, gr[0]);
-                                gr[1] = fmaf(aw, qy, gr[1]);
-                                gr[2] = fmaf(aw, qz, gr[2]);
-                                const float h = 0.5f * aw;
-                                gr[3] = fmaf(h * qx, qx, gr[3]);
-                                gr[4] = fmaf(h * qy, qy, gr[4]);
-                                gr[5] = fmaf(h * qz, qz, gr[5]);
-                                gr[6] = fmaf(h * qx, qy, gr[6]);
-                                gr[7] = fmaf(h * qx, qz, gr[7]);
-                                gr[8] = fmaf(h * qy, qz, gr[8]);
-                                gr[9] = fmaf(a, ex, gr[9]);
+                                    for (int lz = 0; lz < 8; ++lz) {
+                                        const float m =
+                                            fmaf(fmaf(Qz, (float)lz, b0), (float)lz, a0) + (L[lz] + mz[lz]);
+                                        const float w = iny ? A.w * tc::exp2_approx(m) : 0.0f;
+                                        Sv[h * 8 + lz] *= w;
+                                    }
+                                }
+                                const float r = warp_reduce_scatter16(Sv, lane);
+                                if ((lane & 1) == 0) ms.epart[ew][lx * 32 + ly2 * 16 + (lane >> 1)] = r;
+                            }
+                        }
+                    } else {
+                        for (int i = lane; i < kUV; i += 32) ms.epart[ew][i] = 0.0f;
+                    }
+                    epi_barrier();
+                    if (et < kUV) {
+                        float acc = ms.epart[0][et];
+#pragma unroll
+                        for (int w = 1; w < 8; ++w) acc += ms.epart[w][et];
+                        const float ev = ms.e[et] + acc;
+                        ms.e[et] = ev;
+                        // a = gD + (S - act e) / den = S * rden + (gD - act e rden)
+                        ms.va[et] = make_float2(ms.rden[et], fmaf(-ms.act[et] * ev, ms.rden[et], ms.gD[et]));
+                    }
+                    epi_barrier();
+                }
+                if (do2 && wact) {
+                    // the two tiles of the unit: lz 0..3 and 4..7
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        const int tz = ug.tzp * 2 + t;
+                        if (tz >= G.tiles[2]) break;
+                        const bool tin = live && tz * kTile + 3 >= lbz && tz * kTile <= ubz;
+                        if (!__any_sync(0xffffffffu, tin)) continue;
+                        float gr[10];
+#pragma unroll
+                        for (int i = 0; i < 10; ++i) gr[i] = 0.0f;
+#pragma unroll 1
+                        for (int lx = 0; lx < kTile; ++lx) {
+                            const float dx = voxel_centre(G, 0, x0 + lx) - A.x;
+                            const bool inx = tin && x0 + lx >= lbx && x0 + lx <= ubx;
+#pragma unroll 1
+                            for (int ly2 = 0; ly2 < 2; ++ly2) {
+                                float Sv[16];
+                                tc::tmem_ld16(taddr + lx * 32 + ly2 * 16, Sv);
+#pragma unroll
+                                for (int h = 0; h < 2; ++h) {
+                                    const int ly = ly2 * 2 + h;
+                                    const float dy = voxel_centre(G, 1, y0 + ly) - A.y;
+                                    if (!(inx && y0 + ly >= lby && y0 + ly <= uby)) continue;
+                                    const float tqx = fmaf(P0.y, dy, P0.x * dx);
+                                    const float tqy = fmaf(P1.x, dy, P0.w * dx);
+                                    const float tqz = fmaf(P1.w, dy, P1.z * dx);
+                                    const float4* V4 =
+                                        reinterpret_cast<const float4*>(&ms.va[lx * 32 + ly * 8 + t * 4]);
+                                    const float4 va01 = V4[0], va23 = V4[1];
+                                    const float vax[4] = {va01.x, va01.z, va23.x, va23.z};
+                                    const float vay[4] = {va01.y, va01.w, va23.y, va23.w};
+#pragma unroll
+                                    for (int lz = 0; lz < 4; ++lz) {
+                                        const int zz = t * 4 + lz;
+                                        const float dz = fmaf((float)zz, hz, dz0);
+                                        const float qx = fmaf(P0.z, dz, tqx), qy = fmaf(P1.y, dz, tqy),
+                                                    qz = fmaf(P2.x, dz, tqz);
+                                        const float m = k2 * (dx * qx + dy * qy + dz * qz) + mz[zz];
+                                        const float ex = tc::exp2_approx(m);
+                                        const float a = fmaf(Sv[h * 8 + zz], vax[lz], vay[lz]);
+                                        const float aw = a * A.w * ex;
+                                        gr[0] = fmaf(aw, qx, gr[0]);
+                                        gr[1] = fmaf(aw, qy, gr[1]);
+                                        gr[2] = fmaf(aw, qz, gr[2]);
+                                        const float hh = 0.5f * aw;
+                                        gr[3] = fmaf(hh * qx, qx, gr[3]);
+                                        gr[4] = fmaf(hh * qy, qy, gr[4]);
+                                        gr[5] = fmaf(hh * qz, qz, gr[5]);
+                                        gr[6] = fmaf(hh * qx, qy, gr[6]);
+                                        gr[7] = fmaf(hh * qx, qz, gr[7]);
+                                        gr[8] = fmaf(hh * qy, qz, gr[8]);
+                                        gr[9] = fmaf(a, ex, gr[9]);
+                                    }
+                                }
+                            }
+                        }
+                        if (tin) {
+                            const int tlx = lbx / kTile, tly = lby / kTile, tlz = lbz / kTile;
+                            const int ey = uby / kTile - tly + 1, ez = ubz / kTile - tlz + 1;
+                            const int64_t idx =
+                                (int64_t)g2t_offsets[g] + ((ug.tx - tlx) * ey + (ug.ty - tly)) * ez + (tz - tlz);
+                            if (idx >= 0 && idx < pair_cap) {  // offsets come from the caller
+                                float* out = partial10 + idx * 10;
+#pragma unroll
+                                for (int i = 0; i < 10; ++i) out[i] = gr[i];
                             }
                         }
                     }
                 }
-                if (live) {
-                    const int tlx = lbx / kTile, tly = lby / kTile, tlz = lbz / kTile;
-                    const int ey = uby / kTile - tly + 1, ez = ubz / kTile - tlz + 1;
-                    const int64_t idx = (int64_t)g2t_offsets[g] + ((tx - tlx) * ey + (ty - tly)) * ez + (tz - tlz);
-                    if (idx >= 0 && idx < pair_cap) {  // offsets come from the caller
-                        float* out = partial10 + idx * 10;
-#pragma unroll
-                        for (int i = 0; i < 10; ++i) out[i] = gr[i];
-                    }
-                }
+                // this job's S has been read: hand the buffer back to the MMA thread
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&ms.tempty[buf]);
             }
-        }
-    };
-
-    auto sync_tc = [&]() {
-        tc::tc_fence_before();
-        __syncthreads();
-        tc::tc_fence_after();
-    };
-
-    if (keep) {
-        for (int p = 0; p < npass; ++p) mainloop(p, p, p == npass - 1);
-        drain();
-        for (int p = 0; p < npass; ++p) phase1(p, p);
-        for (int p = 0; p < npass; ++p) phase2(p, p);
-    } else {
-        for (int p = 0; p < npass; ++p) {
-            mainloop(p, 0, true);
-            drain();
-            phase1(p, 0);
-            sync_tc();
-        }
-        for (int p = 0; p < npass; ++p) {
-            mainloop(p, 0, true);
-            drain();
-            phase2(p, 0);
-            sync_tc();
+            epi_barrier();  // the unit's voxel data may be overwritten now
         }
     }
-    // no copy may still be in flight when the CTA's shared memory is released (matters after a wait gave up)
-    if (kTma && warp == 9 && lane == 0)
-        for (int k = max(0, issued - kGS); k < issued; ++k) tc::mbar_wait_drain(&ms.gfull[k % kGS], (k / kGS) & 1, err);
-    tc::cp_async_wait<0>();
-    sync_tc();
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
     if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
@@ -464,14 +530,16 @@ __global__ void feature_split_bf16_kernel(const float* __restrict__ f, int64_t n
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t g = i / cpr;
         const int c = (int)(i - g * cpr) * 8;
-        __align__(16) __nv_bfloat16 h[8], l[8];
+        float x[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float x = c + e < C ? f[g * C + c + e] : 0.0f;
-            tc::split_bf16(x, h[e], l[e]);
-        }
-        *reinterpret_cast<uint4*>(hi + g * Cp + c) = *reinterpret_cast<const uint4*>(h);
-        *reinterpret_cast<uint4*>(lo + g * Cp + c) = *reinterpret_cast<const uint4*>(l);
+        for (int e = 0; e < 8; ++e) x[e] = c + e < C ? f[g * C + c + e] : 0.0f;
+        uint4 h, l;
+        tc::split_bf16x2(x[0], x[1], h.x, l.x);
+        tc::split_bf16x2(x[2], x[3], h.y, l.y);
+        tc::split_bf16x2(x[4], x[5], h.z, l.z);
+        tc::split_bf16x2(x[6], x[7], h.w, l.w);
+        *reinterpret_cast<uint4*>(hi + g * Cp + c) = h;
+        *reinterpret_cast<uint4*>(lo + g * Cp + c) = l;
     }
 }
 }  // namespace
@@ -482,11 +550,22 @@ size_t spass_tc_split_bytes(int64_t n, int64_t C) {
     return (size_t)2 * (size_t)(n > 0 ? n : 1) * (size_t)spass_tc_padded_channels(C) * sizeof(__nv_bfloat16) + 256;
 }
 
+// The pass works on cells of 1 x 1 x 2 tiles (z pairs).
+void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]) {
+    cell[0] = 1;
+    cell[1] = 1;
+    cell[2] = 2;
+    ncells[0] = G.tiles[0];
+    ncells[1] = G.tiles[1];
+    ncells[2] = (G.tiles[2] + 1) / 2;
+}
+
 int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
                     const float* density, const GParams* gparams, const int32_t* g2t_offsets,
-                    const int32_t* tile_offsets, const int32_t* tile_lists, int first_tile, int num_tiles,
+                    const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
                     const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s) {
-    if (num_tiles <= 0 || C <= 0 || n <= 0) return 0;
+    const int num_units = (tile_x_end - tile_x_begin) * G.tiles[1] * ((G.tiles[2] + 1) / 2);
+    if (num_units <= 0 || C <= 0 || n <= 0) return 0;
     const int Cp = (int)spass_tc_padded_channels(C);
     uintptr_t p = (reinterpret_cast<uintptr_t>(split) + 255) & ~uintptr_t(255);
     __nv_bfloat16* Fh = reinterpret_cast<__nv_bfloat16*>(p);
@@ -498,16 +577,20 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
                   feature_split_bf16_kernel<<<blocks, 256, 0, s>>>(features, n, C, Cp, Fh, Fl));
         G2V_LAUNCH_CHECK("feature_split_bf16_kernel");
     }
-    const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0);
     CUtensorMap gmap;
     memset(&gmap, 0, sizeof(gmap));
-    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kKC, kTile, kTile, kTile);
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kKC, 8, kTile, kTile);
     auto kern = tma ? spass_tc_kernel<true> : spass_tc_kernel<false>;
     G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    int dev = 0, sms = 148;
+    G2V_CUDA(cudaGetDevice(&dev));
+    G2V_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = std::min(num_units, sms);
     G2V_TIMED("spass_tc_kernel", s,
-              kern<<<(unsigned)num_tiles, kThreads, kSmemBytes, s>>>(
-                  gmap, grad_density, grad_feats, Fh, Fl, C, Cp, vec, density, gparams, g2t_offsets, tile_offsets,
-                  tile_lists, first_tile, G, partial10, pair_cap, err));
+              kern<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(gmap, grad_density, grad_feats, Fh, Fl, C, Cp,
+                                                                  density, gparams, g2t_offsets, unit_offsets,
+                                                                  unit_lists, num_units, tile_x_begin, G, partial10,
+                                                                  pair_cap, err));
     G2V_LAUNCH_CHECK("spass_tc_kernel");
     return 0;
 }
