@@ -22,7 +22,8 @@
 //
 // Persistent CTAs (one per SM) walk the units with a fixed stride; the S of one job (a pass of a unit)
 // fills half of TMEM (256 columns), so the epilogue of one job overlaps the main loop of the next.
-// Roles (576 threads): warps 0-7 gather feature rows and convert gradient rows, warp 8 (one thread)
+// Roles (576 threads): warps 0-3 gather feature rows (4-stage ring, L2 evict_last), warps 4-7 convert
+// gradient rows (2-stage ring; the fp32 rows stream through L2 with evict_first), warp 8 (one thread)
 // issues the MMAs, warp 9 (one thread) issues the TMA loads, warps 10-17 run the epilogue with one
 // thread per Gaussian slot (TMEM lane).  A unit of one pass is one job (phase 1 then phase 2 on the same
 // S); a longer list runs every pass twice, phase 1 over all passes first, then the MMAs again for
@@ -41,13 +42,16 @@ namespace {
 constexpr int kThreads = 576;
 constexpr int kSlots = 256;                       // Gaussians per pass
 constexpr int kKC = 32;                           // channels per pipeline step
-constexpr int kStages = 3;
+constexpr int kSA = 4;                            // feature-row (A) stages
+constexpr int kSB = 2;                            // converted gradient-row (B) stages
 constexpr int kGS = 3;                            // staging stages of the fp32 gradient
 constexpr int kUV = 128;                          // voxels of a unit: x 4, y 4, z 8 (two tiles)
 constexpr int kAHalf = kSlots * kKC * 2;          // 16 KB
 constexpr int kBHalf = kUV * kKC * 2;             // 8 KB
-constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
-constexpr int kGBytes = kUV * kKC * 4;            // 16 KB: [x][y][z8][32 channels]
+constexpr int kAStage = 2 * kAHalf;               // hi + lo
+constexpr int kBStage = 2 * kBHalf;
+constexpr int kGBytes = kUV * kKC * 4;            // 16 KB: [x][y][z8][32 channels], 128-byte swizzle
+static_assert(kKC * 4 == 128, "the staging rows are one 128-byte swizzle span");
 constexpr int kRowGroupBytes = (kKC / 8) * 128;   // 8 rows x kKC channels: 4 core matrices along K
 constexpr int kMBlockBytes = 16 * kRowGroupBytes; // 128 rows
 constexpr uint32_t kTmemCols = 512;
@@ -56,11 +60,12 @@ constexpr int kEpiWarp0 = 10;                     // first epilogue warp
 constexpr uint32_t kIdesc = tc::idesc_bf16_f32(128, kUV, /*A K-major*/ 0, /*B K-major*/ 0);
 
 struct SMisc {
-    uint64_t full_a[kStages];  // 256 cp.async arrivals (feature rows)
-    uint64_t full_b[kStages];  // 8 warp arrivals (gradient rows)
-    uint64_t empty[kStages];   // MMA commit
+    uint64_t full_a[kSA];      // 128 cp.async arrivals (feature rows)
+    uint64_t empty_a[kSA];     // MMA commit
+    uint64_t full_b[kSB];      // 4 warp arrivals (gradient rows)
+    uint64_t empty_b[kSB];     // MMA commit
     uint64_t gfull[kGS];       // TMA bytes of a staged step
-    uint64_t gempty[kGS];      // 8 converter-warp arrivals
+    uint64_t gempty[kGS];      // 4 converter-warp arrivals
     uint64_t tfull[2];         // MMA commit: a job's S is complete in TMEM buffer b
     uint64_t tempty[2];        // 8 epilogue-warp arrivals: buffer b has been read
     uint32_t tmem_base;
@@ -69,7 +74,8 @@ struct SMisc {
     float gD[kUV], act[kUV], rden[kUV], e[kUV];
     float epart[8][kUV];
 };
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(SMisc);
+constexpr size_t kSmemBytes =
+    (size_t)kSA * kAStage + (size_t)kSB * kBStage + (size_t)kGS * kGBytes + sizeof(SMisc);
 static_assert(kSmemBytes <= 227 * 1024, "spass_tc_kernel shared memory");
 
 // 16 per-lane values -> each lane pair (2i, 2i+1) holds the warp sum of value i (fixed order).
@@ -131,7 +137,8 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
     int64_t pair_cap, int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
-    unsigned char* gstage = base + kStages * kStageBytes;
+    unsigned char* bring = base + kSA * kAStage;
+    unsigned char* gstage = bring + kSB * kBStage;
     SMisc& ms = *reinterpret_cast<SMisc*>(gstage + kGS * kGBytes);
     if ((tc::smem_u32(smem_raw) & 127u) != 0) {  // never expected; fail loudly
         if (threadIdx.x == 0) atomicOr(err, 2);
@@ -143,14 +150,17 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
     const int64_t pitch = (int64_t)Cp * 2;  // bytes per split feature row
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            tc::mbar_init(&ms.full_a[i], 256);
-            tc::mbar_init(&ms.full_b[i], 8);
-            tc::mbar_init(&ms.empty[i], 1);
+        for (int i = 0; i < kSA; ++i) {
+            tc::mbar_init(&ms.full_a[i], 128);
+            tc::mbar_init(&ms.empty_a[i], 1);
+        }
+        for (int i = 0; i < kSB; ++i) {
+            tc::mbar_init(&ms.full_b[i], 4);
+            tc::mbar_init(&ms.empty_b[i], 1);
         }
         for (int i = 0; i < kGS; ++i) {
             tc::mbar_init(&ms.gfull[i], 1);
-            tc::mbar_init(&ms.gempty[i], 8);
+            tc::mbar_init(&ms.gempty[i], 4);
         }
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&ms.tfull[i], 1);
@@ -165,19 +175,58 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
     const uint32_t tmem = ms.tmem_base;
     bool ok = true;
 
-    auto a_half = [&](int st, int hl) -> uint32_t { return tc::smem_u32(base + st * kStageBytes + hl * kAHalf); };
-    auto b_half = [&](int st, int hl) -> uint32_t {
-        return tc::smem_u32(base + st * kStageBytes + 2 * kAHalf + hl * kBHalf);
-    };
+    auto a_half = [&](int st, int hl) -> uint32_t { return tc::smem_u32(base + st * kAStage + hl * kAHalf); };
+    auto b_half = [&](int st, int hl) -> uint32_t { return tc::smem_u32(bring + st * kBStage + hl * kBHalf); };
 
-    if (warp < 8) {
-        // ============ producers: feature rows (cp.async) and gradient rows (staged fp32 -> bf16) ============
+    if (warp < 4) {
+        // ============ feature-row producers (cp.async, kept in L2: evict_last) ============
+        // lane = (row rs of an 8-row group, 16-byte chunk kc): 8 lanes fill one 128-byte core-matrix column
+        const int kc = lane >> 3, rs = lane & 7;
+        const uint64_t pol = tc::l2_policy_evict_last();
         int it = 0;
-        const int kc = lane & 3;               // A: 16-byte chunk of a row
-        const int v = tid >> 1, hv = tid & 1;  // B: voxel row, 16-channel half of the step
-        const int boff0 = (v >> 3) * kRowGroupBytes + (2 * hv) * 128 + (v & 7) * 16;
         for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
             const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            if (K == 0) continue;
+            const int npass = (K + kSlots - 1) / kSlots;
+            const int njobs = npass == 1 ? 1 : 2 * npass;
+            for (int jb = 0; jb < njobs && ok; ++jb) {
+                const int p = npass == 1 ? 0 : jb % npass;
+                const int ns = min(kSlots, K - p * kSlots);
+                const int nrows = ns > 128 ? 256 : 128;  // rows of the M-blocks in use
+                int64_t goff[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int slot = q * 32 + warp * 8 + rs;
+                    goff[q] = slot < ns ? (int64_t)unit_lists[s0 + p * kSlots + slot] * pitch : -1;
+                }
+                for (int j = 0; j < nsteps && ok; ++j, ++it) {
+                    const int sa = it % kSA;
+                    if (it >= kSA) ok = tc::mbar_wait(&ms.empty_a[sa], ((it / kSA) + 1) & 1, err);
+                    if (!ok) break;
+                    const int c0 = j * kKC;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int slot = q * 32 + warp * 8 + rs;
+                        if (slot < nrows) {
+                            const uint32_t aoff = (slot >> 3) * kRowGroupBytes + kc * 128 + (slot & 7) * 16;
+                            const int64_t src = goff[q] >= 0 ? goff[q] + (int64_t)(c0 + kc * 8) * 2 : 0;
+                            const uint32_t nb = goff[q] >= 0 ? 16u : 0u;
+                            tc::cp_async16_hint(a_half(sa, 0) + aoff, reinterpret_cast<const char*>(Fh) + src, nb, pol);
+                            tc::cp_async16_hint(a_half(sa, 1) + aoff, reinterpret_cast<const char*>(Fl) + src, nb, pol);
+                        }
+                    }
+                    tc::cp_async_mbar_arrive_noinc(&ms.full_a[sa]);
+                }
+            }
+        }
+        tc::cp_async_wait<0>();  // no copy in flight when the shared memory is released
+    } else if (warp < 8) {
+        // ============ gradient-row converters: staged fp32 -> bf16 hi / lo; thread = voxel row v ============
+        const int v = tid - 128;
+        const int boff0 = (v >> 3) * kRowGroupBytes + (v & 7) * 16;
+        int it = 0;
+        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+            const int K = unit_offsets[u + 1] - unit_offsets[u];
             if (K == 0) continue;
             const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
             const int x = ug.tx * kTile + (v >> 5), y = ug.ty * kTile + ((v >> 3) & 3), z = ug.tzp * 8 + (v & 7);
@@ -186,77 +235,56 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
             const int npass = (K + kSlots - 1) / kSlots;
             const int njobs = npass == 1 ? 1 : 2 * npass;
             for (int jb = 0; jb < njobs && ok; ++jb) {
-                const int p = npass == 1 ? 0 : jb % npass;
-                const int ns = min(kSlots, K - p * kSlots);
-                const int nmb = ns > 128 ? 2 : 1;
-                int64_t goff[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int slot = q * 64 + warp * 8 + (lane >> 2);
-                    goff[q] = slot < ns ? (int64_t)unit_lists[s0 + p * kSlots + slot] * pitch : -1;
-                }
                 for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                    const int st = it % kStages, gs = it % kGS;
-                    if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
+                    const int sb = it % kSB, gs = it % kGS;
+                    if (it >= kSB) ok = tc::mbar_wait(&ms.empty_b[sb], ((it / kSB) + 1) & 1, err);
+                    if (kTma && ok) ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
                     if (!ok) break;
-                    const int c0 = j * kKC;
+                    unsigned char* bst = bring + sb * kBStage + boff0;
+                    // 128-byte swizzled staging row: logical chunk c sits at chunk c ^ (v % 8)
+                    const unsigned char* row = gstage + gs * kGBytes + v * (kKC * 4);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int slot = q * 64 + warp * 8 + (lane >> 2);
-                        if (slot < nmb * 128) {
-                            const uint32_t aoff = (slot >> 3) * kRowGroupBytes + kc * 128 + (slot & 7) * 16;
-                            const int64_t src = goff[q] >= 0 ? goff[q] + (int64_t)(c0 + kc * 8) * 2 : 0;
-                            const uint32_t nb = goff[q] >= 0 ? 16u : 0u;
-                            tc::cp_async16(a_half(st, 0) + aoff, reinterpret_cast<const char*>(Fh) + src, nb);
-                            tc::cp_async16(a_half(st, 1) + aoff, reinterpret_cast<const char*>(Fl) + src, nb);
+                    for (int hv = 0; hv < 2; ++hv) {  // 16 channels at a time
+                        float f[16];
+                        if (kTma) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const float4 t =
+                                    *reinterpret_cast<const float4*>(row + (((hv * 4 + q) ^ (v & 7)) << 4));
+                                f[4 * q] = t.x;
+                                f[4 * q + 1] = t.y;
+                                f[4 * q + 2] = t.z;
+                                f[4 * q + 3] = t.w;
+                            }
+                        } else {
+                            const int c = j * kKC + hv * 16;
+#pragma unroll
+                            for (int e = 0; e < 16; ++e)
+                                f[e] = (vrow >= 0 && c + e < C) ? grad_feats[vrow * C + c + e] : 0.0f;
                         }
+                        uint4 h0, h1, l0, l1;
+                        tc::split_bf16x2(f[0], f[1], h0.x, l0.x);
+                        tc::split_bf16x2(f[2], f[3], h0.y, l0.y);
+                        tc::split_bf16x2(f[4], f[5], h0.z, l0.z);
+                        tc::split_bf16x2(f[6], f[7], h0.w, l0.w);
+                        tc::split_bf16x2(f[8], f[9], h1.x, l1.x);
+                        tc::split_bf16x2(f[10], f[11], h1.y, l1.y);
+                        tc::split_bf16x2(f[12], f[13], h1.z, l1.z);
+                        tc::split_bf16x2(f[14], f[15], h1.w, l1.w);
+                        *reinterpret_cast<uint4*>(bst + hv * 256) = h0;
+                        *reinterpret_cast<uint4*>(bst + hv * 256 + 128) = h1;
+                        *reinterpret_cast<uint4*>(bst + kBHalf + hv * 256) = l0;
+                        *reinterpret_cast<uint4*>(bst + kBHalf + hv * 256 + 128) = l1;
                     }
-                    tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
-                    // B: 16 channels of the voxel's gradient row -> bf16 hi / lo
-                    float f[16];
-                    if (kTma) {
-                        ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
-                        if (!ok) break;
-                        const float4* src =
-                            reinterpret_cast<const float4*>(gstage + gs * kGBytes + v * (kKC * 4) + hv * 64);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const float4 t = src[q];
-                            f[4 * q] = t.x;
-                            f[4 * q + 1] = t.y;
-                            f[4 * q + 2] = t.z;
-                            f[4 * q + 3] = t.w;
-                        }
-                    } else {
-                        const int c = c0 + hv * 16;
-#pragma unroll
-                        for (int e = 0; e < 16; ++e)
-                            f[e] = (vrow >= 0 && c + e < C) ? grad_feats[vrow * C + c + e] : 0.0f;
-                    }
-                    uint4 h0, h1, l0, l1;
-                    tc::split_bf16x2(f[0], f[1], h0.x, l0.x);
-                    tc::split_bf16x2(f[2], f[3], h0.y, l0.y);
-                    tc::split_bf16x2(f[4], f[5], h0.z, l0.z);
-                    tc::split_bf16x2(f[6], f[7], h0.w, l0.w);
-                    tc::split_bf16x2(f[8], f[9], h1.x, l1.x);
-                    tc::split_bf16x2(f[10], f[11], h1.y, l1.y);
-                    tc::split_bf16x2(f[12], f[13], h1.z, l1.z);
-                    tc::split_bf16x2(f[14], f[15], h1.w, l1.w);
-                    unsigned char* bst = base + st * kStageBytes + 2 * kAHalf + boff0;
-                    *reinterpret_cast<uint4*>(bst) = h0;
-                    *reinterpret_cast<uint4*>(bst + 128) = h1;
-                    *reinterpret_cast<uint4*>(bst + kBHalf) = l0;
-                    *reinterpret_cast<uint4*>(bst + kBHalf + 128) = l1;
                     tc::fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tc::mbar_arrive(&ms.full_b[st]);
+                        tc::mbar_arrive(&ms.full_b[sb]);
                         if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
                     }
                 }
             }
         }
-        tc::cp_async_wait<0>();  // no copy in flight when the shared memory is released
     } else if (warp == 8) {
         // ============ MMA thread ============
         if (lane == 0) {
@@ -275,30 +303,31 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                     if (!ok) break;
                     tc::tc_fence_after();
                     for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                        const int st = it % kStages;
-                        const uint32_t par = (it / kStages) & 1;
-                        ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_b[st], par, err);
+                        const int sa = it % kSA, sb = it % kSB;
+                        ok = tc::mbar_wait(&ms.full_a[sa], (it / kSA) & 1, err) &&
+                             tc::mbar_wait(&ms.full_b[sb], (it / kSB) & 1, err);
                         if (!ok) break;
                         tc::tc_fence_after();
 #pragma unroll
                         for (int ks = 0; ks < kKC / 16; ++ks) {
                             const uint64_t bh =
-                                tc::smem_desc(b_half(st, 0) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
+                                tc::smem_desc(b_half(sb, 0) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
                             const uint64_t bl =
-                                tc::smem_desc(b_half(st, 1) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
+                                tc::smem_desc(b_half(sb, 1) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
                             for (int mb = 0; mb < nmb; ++mb) {
                                 const uint32_t ao = mb * kMBlockBytes + ks * 256;
                                 const uint64_t ah =
-                                    tc::smem_desc(a_half(st, 0) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
+                                    tc::smem_desc(a_half(sa, 0) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
                                 const uint64_t al =
-                                    tc::smem_desc(a_half(st, 1) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
+                                    tc::smem_desc(a_half(sa, 1) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
                                 const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
                                 tc::mma_f16_ss(d, ah, bh, kIdesc, j > 0 || ks > 0);
                                 tc::mma_f16_ss(d, ah, bl, kIdesc, true);
                                 tc::mma_f16_ss(d, al, bh, kIdesc, true);
                             }
                         }
-                        tc::mma_commit(tc::smem_u32(&ms.empty[st]));
+                        tc::mma_commit(tc::smem_u32(&ms.empty_a[sa]));
+                        tc::mma_commit(tc::smem_u32(&ms.empty_b[sb]));
                     }
                     tc::mma_commit(tc::smem_u32(&ms.tfull[buf]));
                 }
@@ -308,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
         // ============ TMA thread: the unit's gradient box of each step into the staging ring ============
         if (kTma && lane == 0) {
             int it = 0, issued = 0;
+            const uint64_t pol = tc::l2_policy_evict_first();  // the gradient is streamed once per pass
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int K = unit_offsets[u + 1] - unit_offsets[u];
                 if (K == 0) continue;
@@ -320,8 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                         if (it >= kGS) ok = tc::mbar_wait(&ms.gempty[gs], ((it / kGS) + 1) & 1, err);
                         if (!ok) break;
                         tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
-                        tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, j * kKC, ug.tzp * 8,
-                                        ug.ty * kTile, ug.tx * kTile, &ms.gfull[gs]);
+                        tc::tma_load_4d_hint(tc::smem_u32(gstage + gs * kGBytes), &gmap, j * kKC, ug.tzp * 8,
+                                             ug.ty * kTile, ug.tx * kTile, &ms.gfull[gs], pol);
                         issued = it + 1;
                     }
                 }
@@ -406,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                                     const float qy = fmaf(P1.y, dz0, fmaf(P1.x, dy, P0.w * dx));
                                     const float qz = fmaf(P2.x, dz0, fmaf(P1.w, dy, P1.z * dx));
                                     const float ptz = fmaf(P2.x, dz0, fmaf(P1.y, dy, P0.z * dx));  // (P^T d)_z
-                                    const float a0 = k2 * (dx * qx + dy * qy + dz0 * qz);
+                                    const float a0 = iny ? k2 * (dx * qx + dy * qy + dz0 * qz) : -INFINITY;
                                     const float b0 = k2 * hz * (qz + ptz);
                                     const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[lx * 32 + ly * 8]);
                                     const float4 La = L4[0], Lb = L4[1];
@@ -415,8 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                                     for (int lz = 0; lz < 8; ++lz) {
                                         const float m =
                                             fmaf(fmaf(Qz, (float)lz, b0), (float)lz, a0) + (L[lz] + mz[lz]);
-                                        const float w = iny ? A.w * tc::exp2_approx(m) : 0.0f;
-                                        Sv[h * 8 + lz] *= w;
+                                        Sv[h * 8 + lz] *= A.w * tc::exp2_approx(m);
                                     }
                                 }
                                 const float r = warp_reduce_scatter16(Sv, lane);
@@ -439,7 +468,15 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                     epi_barrier();
                 }
                 if (do2 && wact) {
-                    // the two tiles of the unit: lz 0..3 and 4..7
+                    // Per x-slice of a tile, with q = P d = q0 + ly u + lz w (u = hy P e_y, w = hz P e_z):
+                    //   sum aw q    = q0 M00 + u M10 + w M01
+                    //   sum aw q q' = q0 q0' M00 + (q0 u' + u q0') M10 + (q0 w' + w q0') M01
+                    //                 + u u' M20 + (u w' + w u') M11 + w w' M02
+                    // with the moments M_ab = sum over the slice of a ex ly^a lz^b (aw = o a ex; o applied at the end)
+                    const float hy = G.h[1];
+                    const float ux = hy * P0.y, uy = hy * P1.x, uz = hy * P1.w;  // hy P[:, 1]
+                    const float wx = hz * P0.z, wy = hz * P1.y, wz = hz * P2.x;  // hz P[:, 2]
+                    const float Qyy = k2 * hy * hy * P1.x, Qyz = k2 * hy * hz * (P1.y + P1.w);
 #pragma unroll
                     for (int t = 0; t < 2; ++t) {
                         const int tz = ug.tzp * 2 + t;
@@ -449,22 +486,31 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                         float gr[10];
 #pragma unroll
                         for (int i = 0; i < 10; ++i) gr[i] = 0.0f;
+                        const float dzt = fmaf((float)(4 * t), hz, dz0);  // slice origin z offset
+                        const float dy0 = voxel_centre(G, 1, y0) - A.y;
 #pragma unroll 1
                         for (int lx = 0; lx < kTile; ++lx) {
                             const float dx = voxel_centre(G, 0, x0 + lx) - A.x;
                             const bool inx = tin && x0 + lx >= lbx && x0 + lx <= ubx;
-#pragma unroll 1
+                            // slice origin: q0 = P d0, the exponent k2 (d' P d) as a quadratic in (ly, lz)
+                            const float q0x = fmaf(P0.z, dzt, fmaf(P0.y, dy0, P0.x * dx));
+                            const float q0y = fmaf(P1.y, dzt, fmaf(P1.x, dy0, P0.w * dx));
+                            const float q0z = fmaf(P2.x, dzt, fmaf(P1.w, dy0, P1.z * dx));
+                            const float pty = fmaf(P1.w, dzt, fmaf(P1.x, dy0, P0.y * dx));  // (P' d0)_y
+                            const float ptz = fmaf(P2.x, dzt, fmaf(P1.y, dy0, P0.z * dx));  // (P' d0)_z
+                            const float a0 = inx ? k2 * (dx * q0x + dy0 * q0y + dzt * q0z) : -INFINITY;
+                            const float by = k2 * hy * (q0y + pty), bz = k2 * hz * (q0z + ptz);
+                            float M00 = 0.f, M10 = 0.f, M01 = 0.f, M20 = 0.f, M11 = 0.f, M02 = 0.f;
+#pragma unroll
                             for (int ly2 = 0; ly2 < 2; ++ly2) {
                                 float Sv[16];
                                 tc::tmem_ld16(taddr + lx * 32 + ly2 * 16, Sv);
 #pragma unroll
                                 for (int h = 0; h < 2; ++h) {
                                     const int ly = ly2 * 2 + h;
-                                    const float dy = voxel_centre(G, 1, y0 + ly) - A.y;
-                                    if (!(inx && y0 + ly >= lby && y0 + ly <= uby)) continue;
-                                    const float tqx = fmaf(P0.y, dy, P0.x * dx);
-                                    const float tqy = fmaf(P1.x, dy, P0.w * dx);
-                                    const float tqz = fmaf(P1.w, dy, P1.z * dx);
+                                    const bool iny = y0 + ly >= lby && y0 + ly <= uby;
+                                    const float ay = iny ? fmaf(fmaf(Qyy, (float)ly, by), (float)ly, a0) : -INFINITY;
+                                    const float bzy = fmaf(Qyz, (float)ly, bz);
                                     const float4* V4 =
                                         reinterpret_cast<const float4*>(&ms.va[lx * 32 + ly * 8 + t * 4]);
                                     const float4 va01 = V4[0], va23 = V4[1];
@@ -472,30 +518,40 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                                     const float vay[4] = {va01.y, va01.w, va23.y, va23.w};
 #pragma unroll
                                     for (int lz = 0; lz < 4; ++lz) {
-                                        const int zz = t * 4 + lz;
-                                        const float dz = fmaf((float)zz, hz, dz0);
-                                        const float qx = fmaf(P0.z, dz, tqx), qy = fmaf(P1.y, dz, tqy),
-                                                    qz = fmaf(P2.x, dz, tqz);
-                                        const float m = k2 * (dx * qx + dy * qy + dz * qz) + mz[zz];
+                                        const float m = fmaf(fmaf(Qz, (float)lz, bzy), (float)lz, ay) + mz[t * 4 + lz];
                                         const float ex = tc::exp2_approx(m);
-                                        const float a = fmaf(Sv[h * 8 + zz], vax[lz], vay[lz]);
-                                        const float aw = a * A.w * ex;
-                                        gr[0] = fmaf(aw, qx, gr[0]);
-                                        gr[1] = fmaf(aw, qy, gr[1]);
-                                        gr[2] = fmaf(aw, qz, gr[2]);
-                                        const float hh = 0.5f * aw;
-                                        gr[3] = fmaf(hh * qx, qx, gr[3]);
-                                        gr[4] = fmaf(hh * qy, qy, gr[4]);
-                                        gr[5] = fmaf(hh * qz, qz, gr[5]);
-                                        gr[6] = fmaf(hh * qx, qy, gr[6]);
-                                        gr[7] = fmaf(hh * qx, qz, gr[7]);
-                                        gr[8] = fmaf(hh * qy, qz, gr[8]);
-                                        gr[9] = fmaf(a, ex, gr[9]);
+                                        const float ae = fmaf(Sv[h * 8 + t * 4 + lz], vax[lz], vay[lz]) * ex;
+                                        M00 += ae;
+                                        M10 = fmaf(ae, (float)ly, M10);
+                                        M01 = fmaf(ae, (float)lz, M01);
+                                        M20 = fmaf(ae, (float)(ly * ly), M20);
+                                        M11 = fmaf(ae, (float)(ly * lz), M11);
+                                        M02 = fmaf(ae, (float)(lz * lz), M02);
                                     }
                                 }
                             }
+                            gr[9] += M00;
+                            gr[0] = fmaf(q0x, M00, fmaf(ux, M10, fmaf(wx, M01, gr[0])));
+                            gr[1] = fmaf(q0y, M00, fmaf(uy, M10, fmaf(wy, M01, gr[1])));
+                            gr[2] = fmaf(q0z, M00, fmaf(uz, M10, fmaf(wz, M01, gr[2])));
+                            // (i, j) component of sum aw q q'
+                            auto qq = [&](float q0i, float ui, float wi, float q0j, float uj, float wj) {
+                                return q0i * q0j * M00 + (q0i * uj + ui * q0j) * M10 + (q0i * wj + wi * q0j) * M01 +
+                                       ui * uj * M20 + (ui * wj + wi * uj) * M11 + wi * wj * M02;
+                            };
+                            gr[3] += qq(q0x, ux, wx, q0x, ux, wx);
+                            gr[4] += qq(q0y, uy, wy, q0y, uy, wy);
+                            gr[5] += qq(q0z, uz, wz, q0z, uz, wz);
+                            gr[6] += qq(q0x, ux, wx, q0y, uy, wy);
+                            gr[7] += qq(q0x, ux, wx, q0z, uz, wz);
+                            gr[8] += qq(q0y, uy, wy, q0z, uz, wz);
                         }
                         if (tin) {
+                            const float o = A.w, oh = 0.5f * A.w;
+#pragma unroll
+                            for (int i = 0; i < 3; ++i) gr[i] *= o;
+#pragma unroll
+                            for (int i = 3; i < 9; ++i) gr[i] *= oh;
                             const int tlx = lbx / kTile, tly = lby / kTile, tlz = lbz / kTile;
                             const int ey = uby / kTile - tly + 1, ez = ubz / kTile - tlz + 1;
                             const int64_t idx =
@@ -579,7 +635,7 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
     }
     CUtensorMap gmap;
     memset(&gmap, 0, sizeof(gmap));
-    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kKC, 8, kTile, kTile);
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kKC, 8, kTile, kTile, /*swizzle128*/ true);
     auto kern = tma ? spass_tc_kernel<true> : spass_tc_kernel<false>;
     G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     int dev = 0, sms = 148;

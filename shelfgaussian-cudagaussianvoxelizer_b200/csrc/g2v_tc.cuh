@@ -243,6 +243,34 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst_saddr, const void* tmap
         : "memory");
 }
 
+// L2 eviction-priority policies (createpolicy) for the cache-hinted copies below.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// cp_async16 with an L2 cache policy.
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst_saddr, const void* src, uint32_t src_bytes,
+                                                uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(dst_saddr), "l"(src),
+                 "r"(src_bytes), "l"(policy)
+                 : "memory");
+}
+// tma_load_4d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst_saddr, const void* tmap, int c0, int c1, int c2, int c3,
+                                                 uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst_saddr),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 }  // namespace tc
 }  // namespace g2v
 
