@@ -130,6 +130,22 @@ G2V_API int g2v_backward_plan(const int32_t* valid_voxel_lb, const int32_t* vali
 /* Workspace of g2v_backward_plan (N-sized). */
 G2V_API int g2v_backward_plan_workspace_size(int64_t num_gaussians, size_t* bytes);
 
+/*
+ * g2v_forward_prepare and g2v_backward_plan in one call with a single stream synchronisation: the same
+ * outputs as g2v_forward_prepare plus *num_block_pairs (0 when channels == 0).  For training loops that
+ * run the backward after every forward; saves the backward's planning round trip.
+ * Replaces cu:1484-1631 like g2v_forward_prepare (the planning part has no reference counterpart).
+ */
+G2V_API int g2v_forward_prepare_plan(const float* means3d, const float* covariances, int64_t num_gaussians,
+                                     const float voxel_size[3], const float voxel_range[6], float* cov_inv,
+                                     int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
+                                     int32_t* g2t_offsets, int64_t channels, void* workspace,
+                                     size_t workspace_bytes, void* stream, int64_t* num_pairs,
+                                     int64_t* num_block_pairs);
+
+/* Workspace of g2v_forward_prepare_plan (N-sized). */
+G2V_API int g2v_forward_prepare_plan_workspace_size(int64_t num_gaussians, size_t* bytes);
+
 /* Workspace of g2v_backward. */
 G2V_API int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs, int64_t num_block_pairs,
                                 const int dims[3], int64_t channels, size_t* bytes);

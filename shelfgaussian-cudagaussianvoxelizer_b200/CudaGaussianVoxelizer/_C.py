@@ -82,7 +82,8 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
-def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False):
+def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False,
+                  plan=False):
     lib = _lib.load()
     size_h = _host_values(voxel_size, 3, "voxel_size")
     range_h = _host_values(voxel_range, 6, "voxel_range")
@@ -113,16 +114,29 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
         nvox = torch.empty((n,), **i32)
         g2t_offsets = torch.empty((n + 1,), **i32)
         nbytes = ctypes.c_size_t()
-        _lib.check(lib.g2v_forward_prepare_workspace_size(n, ctypes.byref(nbytes)), "g2v_forward_prepare_workspace_size")
+        if plan:
+            _lib.check(lib.g2v_forward_prepare_plan_workspace_size(n, ctypes.byref(nbytes)),
+                       "g2v_forward_prepare_plan_workspace_size")
+        else:
+            _lib.check(lib.g2v_forward_prepare_workspace_size(n, ctypes.byref(nbytes)),
+                       "g2v_forward_prepare_workspace_size")
         ws1 = _workspace(nbytes.value, dev)
         if timing:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record(stream)
         m = ctypes.c_int64()
-        _lib.check(lib.g2v_forward_prepare(_ptr(means3D), _ptr(covariances), n, _lib.f3(size_h), _lib.f6(range_h),
-                                           _ptr(cov_inv), _ptr(lb), _ptr(ub), _ptr(nvox), _ptr(g2t_offsets),
-                                           _ptr(ws1), ws1.numel(), sptr, ctypes.byref(m)), "g2v_forward_prepare")
+        mb = ctypes.c_int64()
+        if plan:  # prepare + the backward's block-pair count, one synchronisation
+            _lib.check(lib.g2v_forward_prepare_plan(_ptr(means3D), _ptr(covariances), n, _lib.f3(size_h),
+                                                    _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub), _ptr(nvox),
+                                                    _ptr(g2t_offsets), c, _ptr(ws1), ws1.numel(), sptr,
+                                                    ctypes.byref(m), ctypes.byref(mb)), "g2v_forward_prepare_plan")
+        else:
+            _lib.check(lib.g2v_forward_prepare(_ptr(means3D), _ptr(covariances), n, _lib.f3(size_h),
+                                               _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub), _ptr(nvox),
+                                               _ptr(g2t_offsets), _ptr(ws1), ws1.numel(), sptr, ctypes.byref(m)),
+                       "g2v_forward_prepare")
         m = int(m.value)
         g2t_tile_ids = torch.empty((m,), **i32)
         density = torch.empty((X, Y, Z), **f32)
@@ -140,6 +154,8 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
             ev1.synchronize()
             sec = ev0.elapsed_time(ev1) / 1000.0
         out = (density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, sec)
+        if plan:
+            return out, int(mb.value)
         if keep_t2g:
             tiles = _lib.grid_shape(size_h, range_h)[1]
             nt = tiles[0] * tiles[1] * tiles[2]

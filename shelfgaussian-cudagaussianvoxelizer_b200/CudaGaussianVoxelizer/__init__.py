@@ -14,7 +14,7 @@ import torch
 import torch.nn as nn
 
 from . import _C, _lib
-from ._C import gaussian_voxelizer_backward, gaussian_voxelizer_forward
+from ._C import _forward_impl, gaussian_voxelizer_backward, gaussian_voxelizer_forward
 
 _lib.load()  # fail loudly at import when the native library is missing
 
@@ -27,14 +27,16 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, means3D, opacity, covariances, voxel_size, voxel_range, features, timing=True):
-        (density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids,
-         fwd_sec) = gaussian_voxelizer_forward(means3D, opacity, covariances, voxel_size, voxel_range, features,
-                                               timing=timing)
+        # the forward also counts the backward's (Gaussian, block) pairs in its one synchronisation
+        ((density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, fwd_sec),
+         num_block_pairs) = _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing,
+                                          plan=True)
         stats = torch.zeros(2, dtype=torch.float32, device="cpu")
         stats[0] = fwd_sec
         ctx.save_for_backward(means3D, opacity, voxel_size, voxel_range, cov_inv, lb, ub, nvox, g2t_offsets,
                               g2t_tile_ids, density, grid_feats, features, stats)
         ctx.timing = timing
+        ctx.num_block_pairs = num_block_pairs
         ctx.mark_non_differentiable(stats)
         return density, grid_feats, stats
 
@@ -49,7 +51,7 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
             gfeat = grad_feats_output
         grad_means, grad_cov, grad_op, grad_feats, bwd_sec = gaussian_voxelizer_backward(
             gout, gfeat, means3D, opacity, cov_inv, voxel_size, voxel_range, lb, ub, nvox, g2t_offsets,
-            g2t_tile_ids, density, grid_feats, features, timing=ctx.timing)
+            g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs)
         stats[1] = bwd_sec
         return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None)
 

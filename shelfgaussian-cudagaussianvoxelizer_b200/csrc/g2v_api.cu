@@ -37,8 +37,8 @@ int launch_splat_simt(const float* means, const float* opacity, const float* cov
                       const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
                       float* grid_feats, cudaStream_t s);
 int launch_splat_tc(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
-                    const int32_t* ub, const float* features, int64_t n, int C, const int32_t* tile_offsets,
-                    const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
+                    const int32_t* ub, const float* features, int64_t n, int C, const int32_t* unit_offsets,
+                    const int32_t* unit_lists, int tile_x_begin, int tile_x_end, const Grid& G, float* density,
                     float* grid_feats, void* split, int* err, cudaStream_t s);
 size_t splat_tc_split_bytes(int64_t n, int64_t C);
 int launch_spass(const float* grad_density, const float* grad_feats, const float* means, const float* opacity,
@@ -353,8 +353,9 @@ int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, c
     }
     const int64_t ntiles = (int64_t)((dims[0] + 3) / 4) * ((dims[1] + 3) / 4) * ((dims[2] + 3) / 4);
     Carver c(nullptr);
-    T2GWs w;
+    T2GWs w, wu;
     carve_t2g(c, ntiles, num_pairs, w);
+    carve_t2g(c, ntiles, num_pairs, wu);  // the tensor-core path's unit lists (z pairs of tiles)
     c.take<char>(splat_tc_split_bytes(num_gaussians, channels));
     *bytes = c.bytes();
     return G2V_SUCCESS;
@@ -382,9 +383,10 @@ int g2v_forward_splat(const float* means3d, const float* opacity, const float* f
     g2v_forward_splat_workspace_size(num_gaussians, num_pairs, G.dims, channels, &need);
     if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
     Carver c(workspace);
-    T2GWs w;
+    T2GWs w, wu;
     const int64_t ntiles_all = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
     carve_t2g(c, ntiles_all, num_pairs, w);
+    carve_t2g(c, ntiles_all, num_pairs, wu);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int one[3] = {1, 1, 1};
     if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
@@ -394,11 +396,19 @@ int g2v_forward_splat(const float* means3d, const float* opacity, const float* f
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
     if (features != nullptr && C > 0 && use_tensor_cores()) {
+        // unit lists: z pairs of tiles, Gaussian ids ascending (at most M entries over fewer cells)
+        int cell[3], ncells[3];
+        spass_tc_unit_shape(G, cell, ncells);
+        if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
+                                   tile_x_end, g2t_offsets, nullptr, 0, nullptr, wu.counts, wu.tile_offsets,
+                                   wu.unsorted, wu.lists, wu.scan, wu.total, s)))
+            return rc;
         void* split = c.take<char>(splat_tc_split_bytes(num_gaussians, C));
         int* err = nullptr;
         if ((rc = device_error_ptr(&err))) return rc;
         return launch_splat_tc(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, num_gaussians, C,
-                               w.tile_offsets, w.lists, first_tile, nt, G, density, grid_feats, split, err, s);
+                               wu.tile_offsets, wu.lists, tile_x_begin, tile_x_end, G, density, grid_feats, split,
+                               err, s);
     }
     return launch_splat_simt(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, C, w.tile_offsets,
                              w.lists, first_tile, nt, G, density, grid_feats, s);
@@ -489,6 +499,74 @@ int g2v_backward_plan(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_
         set_error("%lld (Gaussian, block) pairs exceed the int32 range", (long long)mb);
         return G2V_ERROR_SIZE_LIMIT;
     }
+    *num_block_pairs = mb;
+    return G2V_SUCCESS;
+}
+
+int g2v_forward_prepare_plan_workspace_size(int64_t num_gaussians, size_t* bytes) {
+    if (!bytes || num_gaussians < 0) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    Carver c(nullptr);
+    PrepareWs wp;
+    PlanWs wb;
+    c.take<char>(carve_prepare(nullptr, num_gaussians, wp));
+    c.take<char>(carve_plan(nullptr, num_gaussians, wb));
+    *bytes = c.bytes();
+    return G2V_SUCCESS;
+}
+
+int g2v_forward_prepare_plan(const float* means3d, const float* covariances, int64_t num_gaussians,
+                             const float voxel_size[3], const float voxel_range[6], float* cov_inv,
+                             int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
+                             int32_t* g2t_offsets, int64_t channels, void* workspace, size_t workspace_bytes,
+                             void* stream, int64_t* num_pairs, int64_t* num_block_pairs) {
+    g_msg[0] = 0;
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if (num_gaussians < 0 || num_gaussians > INT32_MAX - 1 || channels < 0 || !g2t_offsets || !num_pairs ||
+        !num_block_pairs ||
+        (num_gaussians > 0 && (!means3d || !covariances || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
+                               !num_voxels))) {
+        set_error("g2v_forward_prepare_plan: invalid pointer or count");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    size_t need = 0;
+    g2v_forward_prepare_plan_workspace_size(num_gaussians, &need);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    Carver c(workspace);
+    PrepareWs wp;
+    PlanWs wb;
+    carve_prepare(c.take<char>(carve_prepare(nullptr, num_gaussians, wp)), num_gaussians, wp);
+    carve_plan(c.take<char>(carve_plan(nullptr, num_gaussians, wb)), num_gaussians, wb);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((rc = launch_prepare_boxes(means3d, covariances, num_gaussians, G, cov_inv, valid_voxel_lb, valid_voxel_ub,
+                                   num_voxels, wp.ntiles, s)))
+        return rc;
+    if ((rc = launch_exclusive_scan(wp.ntiles, num_gaussians, g2t_offsets, wp.total, wp.scan, s))) return rc;
+    const bool blocks = channels > 0 && num_gaussians > 0;
+    if (blocks) {
+        int B[3], nb[3];
+        block_shape(G, B, nb);
+        if ((rc = count_gaussian_cells(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, B, wb.counts, wb.dummy, s)))
+            return rc;
+        if ((rc = launch_exclusive_scan(wb.counts, num_gaussians, wb.offsets, wb.total, wb.scan, s))) return rc;
+    }
+    int64_t m = 0, mb = 0;
+    int word = 0;
+    G2V_CUDA(cudaMemcpyAsync(&m, wp.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    if (blocks) G2V_CUDA(cudaMemcpyAsync(&mb, wb.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    if ((rc = queue_error_read(s, &word))) return rc;
+    G2V_CUDA(cudaStreamSynchronize(s));
+    if ((rc = report_device_error(word, s))) return rc;
+    if (m > INT32_MAX || mb > INT32_MAX) {
+        set_error("%lld tile pairs / %lld block pairs exceed the int32 range of the CSR maps", (long long)m,
+                  (long long)mb);
+        return G2V_ERROR_SIZE_LIMIT;
+    }
+    *num_pairs = m;
     *num_block_pairs = mb;
     return G2V_SUCCESS;
 }

@@ -1,24 +1,33 @@
 // g2v_splat_tc.cu -- forward splat on the 5th-generation tensor cores (tcgen05, kind::f16).
 //
-// Per tile (64 voxels) and group of 512 channels, the feature sum is the contraction
-//     S[c][v] = sum_k F[g_k][c] * w[v][k]       (C x K) . (K x 64)
-// computed as D^T in TMEM: M = 128 channels per MMA (4 M-blocks, 256 TMEM columns), N = 64 voxels,
-// K = 16 Gaussians per step.  fp32-level accuracy comes from splitting both operands into a half
-// pair, x = hi + lo (~22 bits), and accumulating hi*hi + hi*lo + lo*hi in fp32 (the dropped lo*lo
-// term is ~2^-22 relative).  Range: features are scaled per channel by a power of two so that a
-// channel's max |f| lies in [2^14, 2^15); weights by a per-tile power of two from the tile's max
-// |opacity| (w <= |opacity|).  The epilogue undoes both exactly and divides by max(D_v, 1e-6).
+// grid_feats[v][c] = sum_g w_gv f_gc / max(D_v, 1e-6), D_v = sum_g w_gv (reference TileGaussianVoxelizer
+// forward, src/cuda_gaussian_voxelizer.cu:857-926), as the contraction over the Gaussians of
+//     S[c][v] = sum_k F[g_k][c] * w[v][k]       (C x K) . (K x 128)
+// computed as D^T in TMEM: M = 128 channels per MMA (two M-blocks = 256 channels per job), N = the 128
+// voxels of a unit, K = 16 Gaussians per step.  fp32-level accuracy comes from splitting both operands
+// into a half pair, x = hi + lo (~22 bits), and accumulating hi*hi + hi*lo + lo*hi in fp32 (the dropped
+// lo*lo term is ~2^-22 relative).  Range: features are scaled per channel by a power of two so that a
+// channel's max |f| lies in [2^14, 2^15); weights by a per-unit power of two from the unit's max
+// |opacity| (w <= |opacity|), folded into the weight's base-2 exponent.  The epilogue undoes both
+// exactly and divides by max(D_v, 1e-6).
 //
-// Operands in shared memory:
-//   A = F^T slice (128 channels x 16 Gaussians) MN-major, 128-byte swizzle: 64-channel x 8-Gaussian
-//       atoms of 1 KB (LBO = 1 KB between the two channel halves, SBO = 2 KB between Gaussian octets),
-//       gathered row by row from the split features with cp.async (16 B = 8 channels).
-//   B = w slice (64 voxels x 16 Gaussians) K-major, no swizzle: 8x8 core matrices of 128 B
-//       (LBO = 128 B between Gaussian octets, SBO = 256 B between voxel octets), written by the
-//       threads that evaluate the weights.
-// Roles (256 threads): threads 0-127 evaluate weights (voxel = t % 64, Gaussian octet = t / 64) and
-// accumulate the density; threads 128-255 issue the feature gathers one step ahead; thread 0 issues
-// the 12 MMAs of a step and commits them to the stage's mbarrier.  Three stages; every wait is bounded.
+// Unit of work: a pair of z-adjacent tiles (4 x 4 x 8 voxels) with the union of their Gaussian lists
+// (ascending ids): each feature row gathered serves 128 voxels.  Persistent CTAs (one per SM) walk the
+// units with a fixed stride; a job is (unit, 256-channel group) and its accumulator takes half of TMEM,
+// so the epilogue of one job overlaps the main loop of the next.
+//
+// Operands in shared memory (per stage):
+//   A = F^T slice (256 channels x 16 Gaussians) MN-major, 128-byte swizzle: 64-channel x 8-Gaussian
+//       atoms of 1 KB (LBO = 1 KB between channel atoms, SBO = 2 KB between Gaussian octets), gathered
+//       row by row from the split features with 16-byte cp.async (L2 evict_last);
+//   B = w slice (128 voxels x 16 Gaussians) MN-major, 128-byte swizzle, same atom geometry: one thread
+//       writes the 8 z-voxels of a line for one Gaussian as one 16-byte store (conflict-free).
+// Roles (544 threads): warps 0-3 gather feature rows and stage the step's Gaussian records; warps 4-7
+// evaluate the weights (thread = z-line of 8 voxels x Gaussian pair; along z the exponent is a
+// quadratic, so each weight is two FMAs and one exp2) and, in a unit's first job, the density; warp 8
+// (one thread) issues the 6 MMAs of a step; warps 9-16 run the epilogue (thread = channel, streaming
+// stores).
+// Eight stages; every mbarrier wait is bounded.
 #include <cstddef>
 
 #include "g2v_internal.cuh"
@@ -27,41 +36,45 @@
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 288;          // 4 producer warps, 4 weight warps, 1 MMA warp
-constexpr int kKStep = 16;
-constexpr int kMB = 4;                   // M-blocks of 128 channels per CTA
-constexpr int kChGroup = kMB * 128;      // channels per CTA
-constexpr int kStages = 3;
-constexpr int kABytes = kMB * 4096;      // one operand half (hi or lo), one stage
-constexpr int kWBytes = 2048;
-constexpr int kStageBytes = 2 * kABytes + 2 * kWBytes;
-constexpr uint32_t kTmemCols = kMB * 64;
-constexpr uint32_t kIdesc = tc::idesc_f16_f32(128, 64, /*a MN-major*/ 1, /*b K-major*/ 0);
+constexpr int kThreads = 544;             // 17 warps
+constexpr int kKStep = 16;                // Gaussians per pipeline step
+constexpr int kCG = 256;                  // channels per job (two M-blocks)
+constexpr int kUV = 128;                  // voxels per unit
+constexpr int kStages = 8;
+constexpr int kAHalf = 2 * 4096;          // 256 channels x 16 Gaussians, one half (hi or lo)
+constexpr int kBHalf = 4096;              // 128 voxels x 16 Gaussians, one half
+constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kBufCols = 256;             // one job: 2 M-blocks x 128 voxel columns
+constexpr int kWarpW0 = 4;                // first weight warp (4 of them)
+constexpr int kNWW = 4;
+constexpr int kMmaWarp = 8;
+constexpr int kEpiWarp0 = 9;
+constexpr uint32_t kIdesc = tc::idesc_f16_f32(128, kUV, /*A MN-major*/ 1, /*B MN-major*/ 1);
 
-// The producer threads stage the GParams records of the 16 Gaussians of a step one step ahead.
+// The Gaussian records of the 16 Gaussians of a step, staged with the step's features.
 struct StepParams {
     GParams g[kKStep];
 };
 
 struct TcMisc {
-    uint64_t full_a[kStages];   // the stage's A operand and Gaussian parameters landed (128 producer threads)
+    uint64_t full_a[kStages];   // the stage's features and Gaussian records landed (128 producer threads)
     uint64_t full_w[kStages];   // the stage's weights written (4 weight warps)
     uint64_t empty[kStages];    // the MMAs reading the stage completed
-    uint64_t mma_done;
+    uint64_t tfull[2];          // a job's accumulator is complete in TMEM buffer b
+    uint64_t tempty[2];         // the epilogue has read buffer b (8 warps)
+    uint64_t dready[2];         // a unit's vscale is written (128 weight threads)
+    uint64_t dfree[2];          // the epilogue is done with a unit's vscale (8 warps)
     uint32_t tmem_base;
-    int fail;
-    alignas(16) float vscale[kVoxPerTile];  // 1 / (max(D_v, eps) * weight scale); read as float4
-    float red[(kThreads + 31) / 32];
-    StepParams prm[kStages];
+    float red[8];
+    alignas(16) float vscale[2][kUV];  // per unit: 2^-kt / max(D_v, eps)
+    alignas(16) float dpart[kKStep / 2][kUV];  // density partials [Gaussian pair][voxel], scaled by 2^kt
+    alignas(16) StepParams prm[kStages];
 };
-// Two CTAs per SM: 3 stages (108 KB) + TcMisc (4.3 KB) per CTA.  The 128-byte swizzle atoms need the
-// dynamic shared memory to start on a 1024-byte boundary; the kernel checks that at run time.
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(TcMisc);
+static_assert(kSmemBytes <= 227 * 1024, "splat_tc_kernel shared memory");
 static_assert(offsetof(TcMisc, vscale) % 16 == 0 && offsetof(TcMisc, prm) % 16 == 0,
               "vector-accessed shared fields must be 16-byte aligned");
-static_assert((kStages * kStageBytes) % 1024 == 0, "TcMisc must start 1024-byte aligned");
-// 228 KB per SM, 1 KB of it reserved per resident CTA: two CTAs need <= 113 KB of dynamic smem each
-static_assert(kSmemBytes <= (228 * 1024) / 2 - 1024, "splat_tc_kernel no longer fits two CTAs per SM");
 
 __device__ __forceinline__ int pow2_exponent(float m) {
     // floor(log2(m)) for a finite m > 0
@@ -128,293 +141,333 @@ __global__ void __launch_bounds__(256) pack_params_kernel(const float* __restric
     out[g] = r;
 }
 
-__device__ __forceinline__ float block_max(float v, float* red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float m = 0.0f;
-#pragma unroll
-    for (int w = 0; w < (kThreads + 31) / 32; ++w) m = fmaxf(m, red[w]);
-    __syncthreads();
-    return m;
+// Named barrier of the 4 weight warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void weight_barrier() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+struct UnitGeom {
+    int tx, ty, tzp;
+};
+__device__ __forceinline__ UnitGeom unit_geom(int u, int ty_n, int tzp_n, int tx_begin) {
+    UnitGeom g;
+    const int yz = ty_n * tzp_n;
+    g.tx = tx_begin + u / yz;
+    const int r = u - (u / yz) * yz;
+    g.ty = r / tzp_n;
+    g.tzp = r - g.ty * tzp_n;
+    return g;
 }
 
-// Roles: warp 0 stages step i+1 (TMA gathers of the split features into the swizzled A layout, 4-byte
-// cp.async of the Gaussian parameters); warp 1 (one thread) issues the 12 MMAs of a step once its A and
-// w are ready and commits them to the stage's "empty" barrier; warps 2-5 evaluate the weights of a
-// step.  No CTA-wide barrier in the main loop: stages hand over through mbarriers.
 __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C, int Cp,
-    const GParams* __restrict__ gparams,
-    const float* __restrict__ opacity, const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ tile_lists,
-    int first_tile, int ngroups, Grid G, float* __restrict__ density, float* __restrict__ grid_feats,
-    int* __restrict__ err) {
+    const GParams* __restrict__ gparams, const int32_t* __restrict__ unit_offsets,
+    const int32_t* __restrict__ unit_lists, int num_units, int tx_begin, Grid G, float* __restrict__ density,
+    float* __restrict__ grid_feats, int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
     TcMisc& ms = *reinterpret_cast<TcMisc*>(base + kStages * kStageBytes);
-    if ((tc::smem_u32(smem_raw) & 1023u) != 0) {  // never expected; fail loudly instead of mis-swizzling
+    if ((tc::smem_u32(smem_raw) & 1023u) != 0) {  // the swizzle atoms need 1 KB alignment; never expected
         if (threadIdx.x == 0) atomicOr(err, 2);
         return;
     }
-
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tl = blockIdx.x / ngroups, grp = blockIdx.x - tl * ngroups;
-    int tx, ty, tz;
-    decode_tile(first_tile + tl, G, tx, ty, tz);
-    const int x0 = tx * kTile, y0 = ty * kTile, z0 = tz * kTile;
-    const int s = tile_offsets[tl], K = tile_offsets[tl + 1] - s;
-    const int32_t* list = tile_lists + s;
-    const int c0 = grp * kChGroup;
-    const int nx = min(kTile, G.dims[0] - x0), ny = min(kTile, G.dims[1] - y0), nz = min(kTile, G.dims[2] - z0);
-    const int64_t row0 = ((int64_t)x0 * G.dims[1] + y0) * G.dims[2] + z0;
-    const int64_t sx = (int64_t)G.dims[1] * G.dims[2], sy = G.dims[2];
-
-    if (K == 0) {  // no Gaussian reaches the tile: zeros
-        for (int i = tid; i < kVoxPerTile * kChGroup; i += kThreads) {
-            const int v = i / kChGroup, c = c0 + (i - v * kChGroup);
-            int lx, ly, lz;
-            local_voxel(v, lx, ly, lz);
-            if (c < C && lx < nx && ly < ny && lz < nz) grid_feats[(row0 + lx * sx + ly * sy + lz) * C + c] = 0.0f;
-        }
-        if (grp == 0 && tid < kVoxPerTile) {
-            int lx, ly, lz;
-            local_voxel(tid, lx, ly, lz);
-            if (lx < nx && ly < ny && lz < nz) density[row0 + lx * sx + ly * sy + lz] = 0.0f;
-        }
-        return;
-    }
-
-    // per-tile weight scale: |w| <= |opacity|
-    float om = 0.0f;
-    for (int k = tid; k < K; k += kThreads) om = fmaxf(om, fabsf(opacity[list[k]]));
-    om = block_max(om, ms.red);
-    const int kt = (om > 0.0f) ? max(-100, min(100, 14 - pow2_exponent(om))) : 0;
-    const float wscale = ldexpf(1.0f, kt);
+    const int tzp_n = (G.tiles[2] + 1) / 2;
+    const int ngroups = (C + kCG - 1) / kCG;
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(&ms.full_a[i], 128);
-            tc::mbar_init(&ms.full_w[i], 4);
+            tc::mbar_init(&ms.full_w[i], kNWW);
             tc::mbar_init(&ms.empty[i], 1);
         }
-        tc::mbar_init(&ms.mma_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&ms.tfull[i], 1);
+            tc::mbar_init(&ms.tempty[i], 8);
+            tc::mbar_init(&ms.dready[i], kNWW * 32);
+            tc::mbar_init(&ms.dfree[i], 8);
+        }
         tc::mbar_fence_init();
-        ms.fail = 0;
     }
     if (warp == 0) tc::tmem_alloc(&ms.tmem_base, kTmemCols);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = ms.tmem_base;
-    const int nsteps = (K + kKStep - 1) / kKStep;
     bool ok = true;
-    float dsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // weight threads: density partials of their z-line
-    int dline = 0, dkp = 0;
-
-    auto a_stage = [&](int st, int hl) -> uint32_t {
-        return tc::smem_u32(base + st * kStageBytes + hl * kABytes);
-    };
-    auto w_stage = [&](int st, int hl) -> unsigned char* {
-        return base + st * kStageBytes + 2 * kABytes + hl * kWBytes;
+    auto a_stage = [&](int st, int hl) -> uint32_t { return tc::smem_u32(base + st * kStageBytes + hl * kAHalf); };
+    auto b_stage = [&](int st, int hl) -> uint32_t {
+        return tc::smem_u32(base + st * kStageBytes + 2 * kAHalf + hl * kBHalf);
     };
 
     if (warp < 4) {
-        // ---------------- producer warps: thread = (operand half, 8-channel chunk) ----------------
-        const int hl = tid >> 6, ch16 = tid & 63;
-        const int mb = ch16 >> 4, a = (ch16 >> 3) & 1, j = ch16 & 7;
-        const int c = c0 + ch16 * 8;
-        const bool cin = c < Cp;
-        const char* fbase = reinterpret_cast<const char*>(hl ? Flo : Fhi) + (int64_t)(cin ? c : 0) * 2;
+        // ============ producers: feature rows (thread = half hl, row octet kh, 8-channel chunk jc) ============
+        const int hl = tid >> 6, kh = (tid >> 5) & 1, jc = lane;
+        const int mb = jc >> 4, a = (jc >> 3) & 1, j = jc & 7;
+        const char* fbase = reinterpret_cast<const char*>(hl ? Flo : Fhi);
         const int64_t pitch = (int64_t)Cp * 2;
-        // lanes 0..15 of each producer warp hold the Gaussian ids of a step; step i+1's ids load early
-        int next_row = (lane < kKStep && lane < K) ? list[lane] : 0;
-        for (int i = 0; i < nsteps && ok; ++i) {
-            const int st = i % kStages;
-            const int k0 = i * kKStep;
-            const int my_row = next_row;
-            next_row = (lane < kKStep && k0 + kKStep + lane < K) ? list[k0 + kKStep + lane] : 0;
-            if (i >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((i / kStages) + 1) & 1, err);
-            if (!ok) break;
-            const uint32_t dbase = a_stage(st, hl) + mb * 4096 + a * 1024;
+        const uint64_t pol = tc::l2_policy_evict_last();
+        int it = 0;
+        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+            const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            if (K == 0) continue;
+            const int32_t* list = unit_lists + s0;
+            const int nsteps = (K + kKStep - 1) / kKStep;
+            for (int cg = 0; cg < ngroups && ok; ++cg) {
+                const int c = cg * kCG + jc * 8;
+                const bool cin = c < Cp;
+                const char* fcol = fbase + (int64_t)(cin ? c : 0) * 2;
+                // lanes 0..15 hold the Gaussian ids of a step; step i+1's ids load early
+                int next_row = (lane < kKStep && lane < K) ? list[lane] : 0;
+                for (int i = 0; i < nsteps && ok; ++i, ++it) {
+                    const int st = it % kStages;
+                    const int k0 = i * kKStep;
+                    const int my_row = next_row;
+                    next_row = (lane < kKStep && k0 + kKStep + lane < K) ? list[k0 + kKStep + lane] : 0;
+                    if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
+                    if (!ok) break;
+                    const uint32_t dbase = a_stage(st, hl) + mb * 4096 + a * 1024 + kh * 2048;
 #pragma unroll
-            for (int k = 0; k < kKStep; ++k) {
-                const int row = __shfl_sync(0xffffffffu, my_row, k);
-                const bool valid = cin && (k0 + k < K);
-                const uint32_t dst = dbase + (k >> 3) * 2048 + (k & 7) * 128 + ((j ^ (k & 7)) << 4);
-                tc::cp_async16(dst, fbase + (valid ? (int64_t)row * pitch : 0), valid ? 16u : 0u);
-            }
-            // Gaussian parameters: 16 records of 5 x 16 bytes (zero fill for padding)
-            {
-                const int k = min(tid / 5, kKStep - 1), wq = tid - (tid / 5) * 5;
-                const int row = __shfl_sync(0xffffffffu, my_row, k);  // whole warp takes part
-                if (tid < kKStep * 5) {
-                    const bool valid = k0 + k < K;
-                    tc::cp_async16(tc::smem_u32(ms.prm[st].g) + tid * 16, &gparams[valid ? row : 0].w[wq],
-                                   valid ? 16u : 0u);
+                    for (int r = 0; r < 8; ++r) {
+                        const int k = kh * 8 + r;
+                        const int row = __shfl_sync(0xffffffffu, my_row, k);
+                        const bool valid = cin && (k0 + k < K);
+                        tc::cp_async16_hint(dbase + r * 128 + ((j ^ r) << 4), fcol + (valid ? (int64_t)row * pitch : 0),
+                                            valid ? 16u : 0u, pol);
+                    }
+                    // Gaussian records: 16 records of 5 x 16 bytes (zero fill for padding)
+                    {
+                        const int k = min(tid / 5, kKStep - 1), wq = tid - (tid / 5) * 5;
+                        const int row = __shfl_sync(0xffffffffu, my_row, k);  // whole warp takes part
+                        if (tid < kKStep * 5) {
+                            const bool valid = k0 + k < K;
+                            tc::cp_async16(tc::smem_u32(&ms.prm[st].g[k].w[wq]), &gparams[valid ? row : 0].w[wq],
+                                           valid ? 16u : 0u);
+                        }
+                    }
+                    tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
                 }
             }
-            tc::cp_async_mbar_arrive_noinc(&ms.full_a[st]);
         }
-    } else if (warp == 8) {
-        // ---------------- MMA warp (one thread) ----------------
-        if (lane == 0) {
-            for (int i = 0; i < nsteps && ok; ++i) {
-                const int st = i % kStages;
-                const uint32_t par = (i / kStages) & 1;
-                ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
-                if (!ok) break;
-                // the A operand was written by cp.async (generic proxy); the MMA reads it through the async proxy
-                tc::fence_async_smem();
-                tc::tc_fence_after();
-                const uint64_t bh = tc::smem_desc(tc::smem_u32(w_stage(st, 0)), 128, 256, tc::kLayoutNone);
-                const uint64_t bl = tc::smem_desc(tc::smem_u32(w_stage(st, 1)), 128, 256, tc::kLayoutNone);
-#pragma unroll
-                for (int mb = 0; mb < kMB; ++mb) {
-                    const uint64_t ah = tc::smem_desc(a_stage(st, 0) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
-                    const uint64_t al = tc::smem_desc(a_stage(st, 1) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
-                    const uint32_t d = tmem + mb * 64;
-                    tc::mma_f16_ss(d, ah, bh, kIdesc, i > 0);
-                    tc::mma_f16_ss(d, ah, bl, kIdesc, true);
-                    tc::mma_f16_ss(d, al, bh, kIdesc, true);
-                }
-                tc::mma_commit(tc::smem_u32(&ms.empty[st]));
-            }
-            tc::mma_commit(tc::smem_u32(&ms.mma_done));
-        }
-        __syncwarp();
-    } else {
-        // ---------------- weight warps (4..7): thread = (z-line (lx, ly), Gaussian pair) ----------------
-        const int t = tid - 128;
-        const int line = t >> 3, kp = t & 7;  // 16 lines x 8 pairs
-        const int lx = line >> 2, ly = line & 3;
-        const int vx = x0 + lx, vy = y0 + ly;
-        const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz0 = voxel_centre(G, 2, z0);
+        tc::cp_async_wait<0>();  // no copy in flight when the shared memory is released
+    } else if (warp < kMmaWarp) {
+        // ============ weight warps: thread = (z-line o of 8 voxels, Gaussian pair kp of the step) ============
+        const int t = tid - kWarpW0 * 32;
+        const int o = t & 15, kp = t >> 4;
+        const int lx = o >> 2, ly = o & 3;
+        const float k2 = tc::kNegHalfLog2e;
         const float hz = G.h[2];
-        dline = line;
-        dkp = kp;
-        for (int i = 0; i < nsteps && ok; ++i) {
-            const int st = i % kStages;
-            if (i >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((i / kStages) + 1) & 1, err);
-            ok = ok && tc::mbar_wait(&ms.full_a[st], (i / kStages) & 1, err);
-            if (!ok) break;
-            float w[2][4];
+        // The named barriers below are reached the same number of times by every weight thread whatever
+        // `ok` says (a wait that gave up only skips work), so a failed wait cannot split the barrier.
+        int it = 0, nu = 0;
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+            const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            if (K == 0) continue;
+            const int32_t* list = unit_lists + s0;
+            const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+            const int x0 = ug.tx * kTile, y0 = ug.ty * kTile, z0 = ug.tzp * 8;
+            const int vx = x0 + lx, vy = y0 + ly;
+            const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz0 = voxel_centre(G, 2, z0);
+            // unit weight scale 2^kt from the largest |opacity| (w <= |opacity|)
+            float om = 0.0f;
+            for (int i = t; i < K; i += kNWW * 32) om = fmaxf(om, fabsf(gparams[list[i]].w[0].w));
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int k = 2 * kp + u;
-                const GParams& gp = ms.prm[st].g[k];
-                const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
+            for (int off = 16; off > 0; off >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, off));
+            if (lane == 0) ms.red[warp - kWarpW0] = om;
+            weight_barrier();
+            om = 0.0f;
 #pragma unroll
-                for (int zz = 0; zz < 4; ++zz) w[u][zz] = 0.0f;
-                const int zlo = max(__float_as_int(d.w) - z0, 0), zhi = min(__float_as_int(e4.z) - z0, 3);
-                if (i * kKStep + k < K && vx >= __float_as_int(d.y) && vx <= __float_as_int(e4.x) &&
-                    vy >= __float_as_int(d.z) && vy <= __float_as_int(e4.y) && zlo <= zhi) {
-                    // maha(z0 + t) = A + t B + t^2 Q for the voxel centres of this z-line
-                    const float dx = cx - a.x, dy = cy - a.y, dz = cz0 - a.z;
-                    const float qx = b.x * dx + b.y * dy + b.z * dz;   // (P d)
-                    const float qy = b.w * dx + c.x * dy + c.y * dz;
-                    const float qz = c.z * dx + c.w * dy + d.x * dz;
-                    const float A = dx * qx + dy * qy + dz * qz;
-                    const float ptz = b.z * dx + c.y * dy + d.x * dz;  // (P^T d)_z
-                    const float B = hz * (qz + ptz), Q = hz * hz * d.x;
+            for (int w8 = 0; w8 < kNWW; ++w8) om = fmaxf(om, ms.red[w8]);
+            weight_barrier();
+            int kt = 0;
+            if (om > 0.0f) {
+                int e2;
+                frexpf(om, &e2);
+                kt = max(-100, min(100, 15 - e2));  // max scaled weight in [2^14, 2^15)
+            }
+            const float fkt = (float)kt;
+            const int nsteps = (K + kKStep - 1) / kKStep;
+            float dsum[8];
 #pragma unroll
-                    for (int zz = 0; zz < 4; ++zz) {
-                        const float m = fmaf(fmaf(Q, (float)zz, B), (float)zz, A);
-                        const float ex = __expf(-0.5f * m);
-                        w[u][zz] = (zz >= zlo && zz <= zhi) ? a.w * ex : 0.0f;
+            for (int i = 0; i < 8; ++i) dsum[i] = 0.0f;
+            for (int cg = 0; cg < ngroups; ++cg) {
+                for (int i = 0; i < nsteps && ok; ++i, ++it) {
+                    const int st = it % kStages;
+                    if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
+                    ok = ok && tc::mbar_wait(&ms.full_a[st], (it / kStages) & 1, err);
+                    if (!ok) break;
+                    const int k0 = i * kKStep;
+#pragma unroll
+                    for (int u2 = 0; u2 < 2; ++u2) {
+                        const int k = 2 * kp + u2;
+                        const GParams& gp = ms.prm[st].g[k];
+                        const float4 A = gp.w[0], P0 = gp.w[1], P1 = gp.w[2], P2 = gp.w[3], U = gp.w[4];
+                        const bool live = k0 + k < K && vx >= __float_as_int(P2.y) && vx <= __float_as_int(U.x) &&
+                                          vy >= __float_as_int(P2.z) && vy <= __float_as_int(U.y);
+                        const int zlo = __float_as_int(P2.w) - z0, zhi = __float_as_int(U.z) - z0;
+                        const float dx = cx - A.x, dy = cy - A.y, dz = cz0 - A.z;
+                        const float qx = fmaf(P0.z, dz, fmaf(P0.y, dy, P0.x * dx));
+                        const float qy = fmaf(P1.y, dz, fmaf(P1.x, dy, P0.w * dx));
+                        const float qz = fmaf(P2.x, dz, fmaf(P1.w, dy, P1.z * dx));
+                        const float ptz = fmaf(P2.x, dz, fmaf(P1.y, dy, P0.z * dx));  // (P' d)_z
+                        // base-2 exponent along the line: k2 (a + b lz + P8 hz^2 lz^2) + kt; -inf outside the box
+                        const float a0 = live ? fmaf(k2, dx * qx + dy * qy + dz * qz, fkt) : -INFINITY;
+                        const float b0 = k2 * hz * (qz + ptz), qq = k2 * hz * hz * P2.x;
+                        float w[8];
+#pragma unroll
+                        for (int lz = 0; lz < 8; ++lz) {
+                            const float mzl = (lz >= zlo && lz <= zhi) ? 0.0f : -INFINITY;
+                            const float m = fmaf(fmaf(qq, (float)lz, b0), (float)lz, a0) + mzl;
+                            w[lz] = A.w * tc::exp2_approx(m);
+                            if (cg == 0) dsum[lz] += w[lz];
+                        }
+                        uint4 h, l;
+                        tc::split_half2(w[0], w[1], h.x, l.x);
+                        tc::split_half2(w[2], w[3], h.y, l.y);
+                        tc::split_half2(w[4], w[5], h.z, l.z);
+                        tc::split_half2(w[6], w[7], h.w, l.w);
+                        const int r = k & 7;
+                        const uint32_t off = (k >> 3) * 2048 + (o >> 3) * 1024 + r * 128 + (((o & 7) ^ r) << 4);
+                        *reinterpret_cast<uint4*>(base + st * kStageBytes + 2 * kAHalf + off) = h;
+                        *reinterpret_cast<uint4*>(base + st * kStageBytes + 2 * kAHalf + kBHalf + off) = l;
+                    }
+                    tc::fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
+                }
+                if (cg == 0) {
+                    // density of the unit: sum over the 8 Gaussian pairs; vscale for the epilogue
+#pragma unroll
+                    for (int lz = 0; lz < 8; ++lz) ms.dpart[kp][o * 8 + lz] = dsum[lz];
+                    weight_barrier();
+                    const int b = nu & 1;
+                    if (nu >= 2 && ok) ok = tc::mbar_wait(&ms.dfree[b], ((nu / 2) + 1) & 1, err);
+                    if (t < kUV) {
+                        const int v = t;  // voxel of the unit: (v >> 5, (v >> 3) & 3, v & 7)
+                        float Ds = 0.0f;
+#pragma unroll
+                        for (int q = 0; q < kKStep / 2; ++q) Ds += ms.dpart[q][v];
+                        const float D = ldexpf(Ds, -kt);
+                        ms.vscale[b][v] = ldexpf(1.0f, -kt) / fmaxf(D, kEps);
+                        const int x = x0 + (v >> 5), y = y0 + ((v >> 3) & 3), z = z0 + (v & 7);
+                        if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
+                            density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z] = D;
+                    }
+                    tc::mbar_arrive(&ms.dready[b]);
+                    weight_barrier();  // dpart is reused by the next unit
+                }
+            }
+            ++nu;
+        }
+    } else if (warp == kMmaWarp) {
+        // ============ MMA thread ============
+        if (lane == 0) {
+            int it = 0, job = 0;
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const int K = unit_offsets[u + 1] - unit_offsets[u];
+                if (K == 0) continue;
+                const int nsteps = (K + kKStep - 1) / kKStep;
+                for (int cg = 0; cg < ngroups && ok; ++cg, ++job) {
+                    const int buf = job & 1;
+                    if (job >= 2) ok = tc::mbar_wait(&ms.tempty[buf], ((job / 2) + 1) & 1, err);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    for (int i = 0; i < nsteps && ok; ++i, ++it) {
+                        const int st = it % kStages;
+                        const uint32_t par = (it / kStages) & 1;
+                        ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
+                        if (!ok) break;
+                        // the A operand was written by cp.async (generic proxy); the MMA reads it through the async proxy
+                        tc::fence_async_smem();
+                        tc::tc_fence_after();
+                        const uint64_t bh = tc::smem_desc(b_stage(st, 0), 1024, 2048, tc::kLayoutSw128);
+                        const uint64_t bl = tc::smem_desc(b_stage(st, 1), 1024, 2048, tc::kLayoutSw128);
+#pragma unroll
+                        for (int mb = 0; mb < 2; ++mb) {
+                            const uint64_t ah = tc::smem_desc(a_stage(st, 0) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                            const uint64_t al = tc::smem_desc(a_stage(st, 1) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                            const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
+                            tc::mma_f16_ss(d, ah, bh, kIdesc, i > 0);
+                            tc::mma_f16_ss(d, ah, bl, kIdesc, true);
+                            tc::mma_f16_ss(d, al, bh, kIdesc, true);
+                        }
+                        tc::mma_commit(tc::smem_u32(&ms.empty[st]));
+                    }
+                    tc::mma_commit(tc::smem_u32(&ms.tfull[buf]));
+                }
+            }
+        }
+    } else {
+        // ============ epilogue warps: thread = channel (TMEM lane), streaming stores of grid_feats ============
+        const int et = tid - kEpiWarp0 * 32;  // 0..255
+        const int q = warp & 3;               // TMEM lane quarter of this warp
+        const int mb = (warp - kEpiWarp0) >> 2;
+        const int64_t sx = (int64_t)G.dims[1] * G.dims[2], sy = G.dims[2];
+        int job = 0, nu = 0;
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+            const int K = unit_offsets[u + 1] - unit_offsets[u];
+            const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+            const int x0 = ug.tx * kTile, y0 = ug.ty * kTile, z0 = ug.tzp * 8;
+            const int nx = min(kTile, G.dims[0] - x0), ny = min(kTile, G.dims[1] - y0), nz = min(8, G.dims[2] - z0);
+            const int64_t row0 = ((int64_t)x0 * G.dims[1] + y0) * G.dims[2] + z0;
+            if (K == 0) {  // no Gaussian reaches the unit: zeros
+                for (int v = 0; v < kUV; ++v) {
+                    const int lx = v >> 5, ly = (v >> 3) & 3, lz = v & 7;
+                    if (lx >= nx || ly >= ny || lz >= nz) continue;
+                    const int64_t row = row0 + lx * sx + ly * sy + lz;
+                    for (int c = et; c < C; c += 256) __stcs(&grid_feats[row * C + c], 0.0f);
+                    if (et == 0) density[row] = 0.0f;
+                }
+                continue;
+            }
+            const int b = nu & 1;
+            bool good = ok && tc::mbar_wait(&ms.dready[b], (nu / 2) & 1, err);
+            for (int cg = 0; cg < ngroups; ++cg, ++job) {
+                const int buf = job & 1;
+                good = good && ok && tc::mbar_wait(&ms.tfull[buf], (job / 2) & 1, err);
+                if (!good) ok = false;
+                tc::tc_fence_after();
+                const int c = cg * kCG + mb * 128 + q * 32 + lane;
+                const bool cok = c < C;
+                const float us = cok ? unscale[c] : 0.0f;
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kBufCols + mb * kUV);
+                if (good) {
+#pragma unroll 1
+                    for (int ch = 0; ch < 8; ++ch) {  // 16 columns: x-slice lx = ch / 2, ly = 2 (ch % 2) + (e / 8)
+                        float vals[16];
+                        tc::tmem_ld16(taddr + ch * 16, vals);
+                        const int lx = ch >> 1;
+                        const float4* vs4 = reinterpret_cast<const float4*>(&ms.vscale[b][ch * 16]);
+                        float vs[16];
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            const float4 r4 = vs4[e4];
+                            vs[4 * e4] = r4.x;
+                            vs[4 * e4 + 1] = r4.y;
+                            vs[4 * e4 + 2] = r4.z;
+                            vs[4 * e4 + 3] = r4.w;
+                        }
+                        if (cok && lx < nx) {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                const int ly = (ch & 1) * 2 + (e >> 3), lz = e & 7;
+                                if (ly < ny && lz < nz)
+                                    __stcs(&grid_feats[(row0 + lx * sx + ly * sy + lz) * C + c], vals[e] * (us * vs[e]));
+                            }
+                        }
                     }
                 }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&ms.tempty[buf]);
             }
-            // store the 8 weights (4 voxels x 2 Gaussians) as half2 pairs, hi and lo, in the K-major core matrices
-#pragma unroll
-            for (int zz = 0; zz < 4; ++zz) {
-                dsum[zz] += w[0][zz] + w[1][zz];
-                __half h0, l0, h1, l1;
-                tc::split_half(w[0][zz] * wscale, h0, l0);
-                tc::split_half(w[1][zz] * wscale, h1, l1);
-                const int v = (lx * 4 + ly) * 4 + zz, k = 2 * kp;
-                const int off = (v >> 3) * 256 + (k >> 3) * 128 + (v & 7) * 16 + (k & 7) * 2;
-                *reinterpret_cast<__half2*>(w_stage(st, 0) + off) = __halves2half2(h0, h1);
-                *reinterpret_cast<__half2*>(w_stage(st, 1) + off) = __halves2half2(l0, l1);
-            }
-            tc::fence_async_smem();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
+            if (lane == 0) tc::mbar_arrive(&ms.dfree[b]);
+            ++nu;
         }
     }
-    // all MMAs are complete once mma_done has arrived
-    ok = tc::mbar_wait_drain(&ms.mma_done, 0, err) && ok;
-    if (!ok) ms.fail = 1;  // benign race: every writer stores 1
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
-    // the stage buffers are free now: density partials [pair slot][voxel] go there
-    float* dpartk = reinterpret_cast<float*>(base);
-    if (warp >= 4 && warp < 8) {
-#pragma unroll
-        for (int zz = 0; zz < 4; ++zz) dpartk[dkp * kVoxPerTile + dline * 4 + zz] = dsum[zz];
-    }
-    __syncthreads();
-    if (tid < kVoxPerTile) {
-        float D = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) D += dpartk[q * kVoxPerTile + tid];
-        ms.vscale[tid] = 1.0f / (fmaxf(D, kEps) * wscale);
-        int lx, ly, lz;
-        local_voxel(tid, lx, ly, lz);
-        if (grp == 0 && lx < nx && ly < ny && lz < nz) density[row0 + lx * sx + ly * sy + lz] = D;
-    }
-    __syncthreads();
-
-    // epilogue: warp w reads TMEM lanes 32*(w%4).. (channels) of M-blocks (w/4) and (w/4)+2; lane = channel,
-    // the 16 columns of one load are the voxels (lx, 0..3, 0..3) of x-slice lx = j
-    const bool good = !ms.fail;
-    const bool full = nx == kTile && ny == kTile && nz == kTile;
-    const int q = warp & 3, hh = (warp >> 2) & 1;
-    int64_t off[16];  // element offsets of the 16 voxels (ly, lz) of an x-slice, relative to the slice
-#pragma unroll
-    for (int e = 0; e < 16; ++e) off[e] = ((int64_t)(e >> 2) * sy + (e & 3)) * C;
-#pragma unroll
-    for (int t = 0; t < 2 && warp < 8; ++t) {
-        const int mb = hh + 2 * t;
-        const int c = c0 + mb * 128 + q * 32 + lane;
-        const bool cok = c < C;
-        const float us = cok ? unscale[c] : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float vals[16];
-            if (good) {
-                tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + mb * 64 + j * 16, vals);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) vals[e] = 0.0f;
-            }
-            float* slice = grid_feats + (row0 + j * sx) * C + c;
-            const float4* vs4 = reinterpret_cast<const float4*>(&ms.vscale[j * 16]);
-            if (full) {
-                if (cok) {
-#pragma unroll
-                    for (int e4 = 0; e4 < 4; ++e4) {
-                        const float4 r = vs4[e4];
-                        slice[off[4 * e4 + 0]] = vals[4 * e4 + 0] * (us * r.x);
-                        slice[off[4 * e4 + 1]] = vals[4 * e4 + 1] * (us * r.y);
-                        slice[off[4 * e4 + 2]] = vals[4 * e4 + 2] * (us * r.z);
-                        slice[off[4 * e4 + 3]] = vals[4 * e4 + 3] * (us * r.w);
-                    }
-                }
-            } else if (cok && j < nx) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    if ((e >> 2) < ny && (e & 3) < nz) slice[off[e]] = vals[e] * (us * ms.vscale[j * 16 + e]);
-            }
-        }
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, kTmemCols);
-    }
+    if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 }  // namespace
 
@@ -434,12 +487,13 @@ size_t splat_tc_split_bytes(int64_t n, int64_t C) {
 }
 
 // Splits the features (per-channel power-of-two scale) into `split` (splat_tc_split_bytes) and runs the
-// tensor-core splat over the tiles [first_tile, first_tile + num_tiles).
+// tensor-core splat over the units (z pairs of tiles) of the slab [tile_x_begin, tile_x_end).
 int launch_splat_tc(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
-                    const int32_t* ub, const float* features, int64_t n, int C, const int32_t* tile_offsets,
-                    const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
+                    const int32_t* ub, const float* features, int64_t n, int C, const int32_t* unit_offsets,
+                    const int32_t* unit_lists, int tile_x_begin, int tile_x_end, const Grid& G, float* density,
                     float* grid_feats, void* split, int* err, cudaStream_t s) {
-    if (num_tiles <= 0) return 0;
+    const int num_units = (tile_x_end - tile_x_begin) * G.tiles[1] * ((G.tiles[2] + 1) / 2);
+    if (num_units <= 0) return 0;
     const int Cp = (C + 7) / 8 * 8;
     Carver cv(split);
     __half* hi = cv.take<__half>((size_t)n * Cp);
@@ -458,17 +512,18 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
                                                                                     lo, unscale));
         G2V_LAUNCH_CHECK("feature_split_kernel");
     }
-    const int ngroups = (C + kChGroup - 1) / kChGroup;
     GParams* gp = cv.take<GParams>((size_t)(n > 0 ? n : 1));
     int rc = launch_pack_params(means, opacity, cov_inv, lb, ub, n, gp, s);
     if (rc) return rc;
     G2V_CUDA(cudaFuncSetAttribute(splat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    const int64_t grid = (int64_t)num_tiles * ngroups;
+    int dev = 0, sms = 148;
+    G2V_CUDA(cudaGetDevice(&dev));
+    G2V_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = num_units < sms ? num_units : sms;
     G2V_TIMED("splat_tc_kernel", s,
-              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(hi, lo, unscale, C, Cp, gp, opacity,
-                                                                            tile_offsets, tile_lists,
-                                                                            first_tile, ngroups, G, density,
-                                                                            grid_feats, err));
+              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(hi, lo, unscale, C, Cp, gp, unit_offsets,
+                                                                            unit_lists, num_units, tile_x_begin, G,
+                                                                            density, grid_feats, err));
     G2V_LAUNCH_CHECK("splat_tc_kernel");
     return 0;
 }

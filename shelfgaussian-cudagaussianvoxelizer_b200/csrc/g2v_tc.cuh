@@ -7,6 +7,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <cstring>
+
 namespace g2v {
 namespace tc {
 
@@ -179,6 +181,15 @@ __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, u
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
     const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(x1 - h1), "f"(x0 - h0));
+}
+
+// Two floats -> packed f16x2 hi / lo words (x0 in the low half) with x ~= hi + lo as in split_half.
+__device__ __forceinline__ void split_half2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+    __half2 h2;
+    memcpy(&h2, &hi, 4);
+    const float2 hf = __half22float2(h2);
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(x1 - hf.y), "f"(x0 - hf.x));
 }
 
 // 2^x with the hardware approximation (ex2.approx.ftz).
