@@ -118,6 +118,19 @@ G2V_API int g2v_forward_splat(const float* means3d, const float* opacity, const 
                       size_t workspace_bytes, void* stream);
 
 /*
+ * g2v_forward_splat for one x-slab of a scene sharded across devices: the same arguments, but density
+ * and grid_feats hold only the slab's voxel x rows, [4 * tile_x_begin, min(4 * tile_x_end, X)), as
+ * (rows, Y, Z) and (rows, Y, Z, C) arrays.  Each rank of a single-scene split calls it for its slab;
+ * the slabs' outputs are disjoint.  No reference counterpart (the reference is single-device).
+ */
+G2V_API int g2v_forward_splat_local(const float* means3d, const float* opacity, const float* features,
+                                    int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                                    const float voxel_range[6], const float* cov_inv, const int32_t* valid_voxel_lb,
+                                    const int32_t* valid_voxel_ub, const int32_t* g2t_offsets, int64_t num_pairs,
+                                    int32_t* g2t_tile_ids, float* density, float* grid_feats, int tile_x_begin,
+                                    int tile_x_end, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Backward planning: counts the (Gaussian, tile block) pairs that the feature-gradient pass needs and
  * reads the count back to *num_block_pairs (one stream synchronisation).  Needed only to size the
  * backward workspace; the Python layer obtains it once per forward.
@@ -169,6 +182,22 @@ G2V_API int g2v_backward(const float* grad_density, const float* grad_grid_feats
                  const float* grid_feats, float* grad_means3d, float* grad_covariances, float* grad_opacity,
                  float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
                  size_t workspace_bytes, void* stream);
+
+/*
+ * g2v_backward for one x-slab with slab-local volume arrays (grad_density, grad_grid_feats, density,
+ * grid_feats hold the slab's voxel x rows only, as in g2v_forward_splat_local).  The outputs are the
+ * slab's partial per-Gaussian gradients; summed over the slabs of a split (one all-reduce) they equal
+ * the whole-grid gradients.  No reference counterpart.
+ */
+G2V_API int g2v_backward_local(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                               const float* opacity, const float* cov_inv, const float* features,
+                               int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                               const float voxel_range[6], const int dims[3], const int32_t* valid_voxel_lb,
+                               const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                               const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                               const float* density, const float* grid_feats, float* grad_means3d,
+                               float* grad_covariances, float* grad_opacity, float* grad_features, int tile_x_begin,
+                               int tile_x_end, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Debug / parity hook: the Tile->Gaussian CSR built by g2v_forward_splat for the whole grid, copied

@@ -139,6 +139,8 @@ int make_grid(const float size[3], const float range[6], Grid& G) {
         G.dims[a] = static_cast<int>(q);
         G.tiles[a] = (G.dims[a] + kTile - 1) / kTile;
     }
+    G.xoff = 0;
+    G.xlen = G.dims[0];
     const int64_t ntiles = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
     const int64_t nvox = (int64_t)G.dims[0] * G.dims[1] * G.dims[2];
     if (ntiles > INT32_MAX / 2 || nvox > ((int64_t)1 << 40)) {
@@ -155,6 +157,12 @@ int check_slab(const Grid& G, int& tx_begin, int& tx_end) {
         return G2V_ERROR_INVALID_VALUE;
     }
     return 0;
+}
+
+// Slab-local volume arrays: they hold the voxel x rows of the tiles [tx_begin, tx_end) only.
+void set_slab_local(Grid& G, int tx_begin, int tx_end) {
+    G.xoff = tx_begin * kTile;
+    G.xlen = (tx_end * kTile < G.dims[0] ? tx_end * kTile : G.dims[0]) - G.xoff;
 }
 
 // Blocks of tiles used by the feature-gradient pass.
@@ -361,17 +369,18 @@ int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, c
     return G2V_SUCCESS;
 }
 
-int g2v_forward_splat(const float* means3d, const float* opacity, const float* features, int64_t num_gaussians,
-                      int64_t channels, const float voxel_size[3], const float voxel_range[6],
-                      const float* cov_inv, const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub,
-                      const int32_t* g2t_offsets, int64_t num_pairs, int32_t* g2t_tile_ids, float* density,
-                      float* grid_feats, int tile_x_begin, int tile_x_end, void* workspace,
-                      size_t workspace_bytes, void* stream) {
+static int forward_splat_impl(const float* means3d, const float* opacity, const float* features,
+                              int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                              const float voxel_range[6], const float* cov_inv, const int32_t* valid_voxel_lb,
+                              const int32_t* valid_voxel_ub, const int32_t* g2t_offsets, int64_t num_pairs,
+                              int32_t* g2t_tile_ids, float* density, float* grid_feats, int tile_x_begin,
+                              int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local) {
     g_msg[0] = 0;
     Grid G;
     int rc = make_grid(voxel_size, voxel_range, G);
     if (rc) return rc;
     if ((rc = check_slab(G, tile_x_begin, tile_x_end))) return rc;
+    if (local) set_slab_local(G, tile_x_begin, tile_x_end);
     const int C = features ? (int)channels : 0;
     if (num_gaussians < 0 || num_pairs < 0 || channels < 0 || channels > INT32_MAX / 2 || !density ||
         !g2t_offsets || (num_pairs > 0 && !g2t_tile_ids) || (features && channels > 0 && !grid_feats) ||
@@ -412,6 +421,28 @@ int g2v_forward_splat(const float* means3d, const float* opacity, const float* f
     }
     return launch_splat_simt(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, C, w.tile_offsets,
                              w.lists, first_tile, nt, G, density, grid_feats, s);
+}
+
+int g2v_forward_splat(const float* means3d, const float* opacity, const float* features, int64_t num_gaussians,
+                      int64_t channels, const float voxel_size[3], const float voxel_range[6],
+                      const float* cov_inv, const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub,
+                      const int32_t* g2t_offsets, int64_t num_pairs, int32_t* g2t_tile_ids, float* density,
+                      float* grid_feats, int tile_x_begin, int tile_x_end, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    return forward_splat_impl(means3d, opacity, features, num_gaussians, channels, voxel_size, voxel_range, cov_inv,
+                              valid_voxel_lb, valid_voxel_ub, g2t_offsets, num_pairs, g2t_tile_ids, density,
+                              grid_feats, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream, false);
+}
+
+int g2v_forward_splat_local(const float* means3d, const float* opacity, const float* features,
+                            int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                            const float voxel_range[6], const float* cov_inv, const int32_t* valid_voxel_lb,
+                            const int32_t* valid_voxel_ub, const int32_t* g2t_offsets, int64_t num_pairs,
+                            int32_t* g2t_tile_ids, float* density, float* grid_feats, int tile_x_begin,
+                            int tile_x_end, void* workspace, size_t workspace_bytes, void* stream) {
+    return forward_splat_impl(means3d, opacity, features, num_gaussians, channels, voxel_size, voxel_range, cov_inv,
+                              valid_voxel_lb, valid_voxel_ub, g2t_offsets, num_pairs, g2t_tile_ids, density,
+                              grid_feats, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream, true);
 }
 
 int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs, const int dims[3],
@@ -587,14 +618,14 @@ int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs, int64_
     return G2V_SUCCESS;
 }
 
-int g2v_backward(const float* grad_density, const float* grad_grid_feats, const float* means3d,
-                 const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
-                 int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
-                 const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
-                 const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs, const float* density,
-                 const float* grid_feats, float* grad_means3d, float* grad_covariances, float* grad_opacity,
-                 float* grad_features, int tile_x_begin, int tile_x_end, void* workspace, size_t workspace_bytes,
-                 void* stream) {
+static int backward_impl(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                         const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
+                         int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                         const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                         const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                         const float* density, const float* grid_feats, float* grad_means3d,
+                         float* grad_covariances, float* grad_opacity, float* grad_features, int tile_x_begin,
+                         int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local) {
     (void)grid_feats;
     g_msg[0] = 0;
     Grid G;
@@ -605,6 +636,7 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
         return G2V_ERROR_INVALID_VALUE;
     }
     if ((rc = check_slab(G, tile_x_begin, tile_x_end))) return rc;
+    if (local) set_slab_local(G, tile_x_begin, tile_x_end);
     const int C = features ? (int)channels : 0;
     if (num_gaussians < 0 || num_pairs < 0 || channels < 0 || channels > INT32_MAX / 2 || num_block_pairs < 0 ||
         !grad_density || !density || !g2t_offsets || (num_pairs > 0 && !g2t_tile_ids) ||
@@ -676,6 +708,36 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
             return rc;
     }
     return G2V_SUCCESS;
+}
+
+int g2v_backward(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                 const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
+                 int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                 const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                 const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs, const float* density,
+                 const float* grid_feats, float* grad_means3d, float* grad_covariances, float* grad_opacity,
+                 float* grad_features, int tile_x_begin, int tile_x_end, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+    return backward_impl(grad_density, grad_grid_feats, means3d, opacity, cov_inv, features, num_gaussians, channels,
+                         voxel_size, voxel_range, dims, valid_voxel_lb, valid_voxel_ub, g2t_offsets, g2t_tile_ids,
+                         num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_covariances,
+                         grad_opacity, grad_features, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream,
+                         false);
+}
+
+int g2v_backward_local(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                       const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
+                       int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                       const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                       const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                       const float* density, const float* grid_feats, float* grad_means3d, float* grad_covariances,
+                       float* grad_opacity, float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+    return backward_impl(grad_density, grad_grid_feats, means3d, opacity, cov_inv, features, num_gaussians, channels,
+                         voxel_size, voxel_range, dims, valid_voxel_lb, valid_voxel_ub, g2t_offsets, g2t_tile_ids,
+                         num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_covariances,
+                         grad_opacity, grad_features, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream,
+                         true);
 }
 
 }  // extern "C"

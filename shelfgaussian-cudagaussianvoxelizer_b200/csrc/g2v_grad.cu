@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) spass_kernel(
         local_voxel(tid, lx, ly, lz);
         const int x = x0 + lx, y = y0 + ly, z = z0 + lz;
         const bool ok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
-        const int64_t row = ok ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : 0;
+        const int64_t row = ok ? grid_row(G, x, y, z) : 0;
         sm.vox_ok[tid] = ok;
         sm.vrow[tid] = row;
         const float D = ok ? density[row] : 0.0f;
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kThreads) fpass_kernel(
                         local_voxel(tid, lx, ly, lz);
                         const int x = x0 + lx, y = y0 + ly, z = z0 + lz;
                         const bool ok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
-                        const int64_t row = ok ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : -1;
+                        const int64_t row = ok ? grid_row(G, x, y, z) : -1;
                         vrow[tid] = row;
                         rden[tid] = ok ? 1.0f / fmaxf(density[row], kEps) : 0.0f;
                     }

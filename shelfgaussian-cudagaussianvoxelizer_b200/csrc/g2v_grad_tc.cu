@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         const int x = (txa + txi) * kTile + lx, y = (tya + tyi) * kTile + ly, z = (tza + tzi) * kTile + lz;
         float r = -INFINITY;
         if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
-            r = -log2f(fmaxf(density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z], kEps));
+            r = -log2f(fmaxf(density[grid_row(G, x, y, z)], kEps));
         ms.lrd[i] = r;
     }
     for (int t = tid; t < ntiles; t += kThreads) {
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                         const int x = x0 + ks, y = y0 + (r >> 2), z = z0 + (r & 3);
                         const bool vok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
                         const int c = c0 + jc * 8;
-                        const float* src = grad_feats + (((int64_t)x * G.dims[1] + y) * G.dims[2] + z) * C + c;
+                        const float* src = grad_feats + grid_row(G, x, y, z) * C + c;
                         if (vok && c + 7 < C && vec) {
                             const float4 u = *reinterpret_cast<const float4*>(src);
                             const float4 w4 = *reinterpret_cast<const float4*>(src + 4);
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 if (it >= kGS) ok = tc::mbar_wait(&ms.gempty[gs], ((it / kGS) + 1) & 1, err);
                 if (!ok) break;
                 tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
-                tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, c0, z0, y0, x0 + ks, &ms.gfull[gs]);
+                tc::tma_load_4d(tc::smem_u32(gstage + gs * kGBytes), &gmap, c0, z0, y0, x0 + ks - G.xoff, &ms.gfull[gs]);
                 issued = it + 1;
             }
         } else if (warp == 16 && lane == 0) {
@@ -405,7 +405,8 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
     }
     CUtensorMap gmap;
     memset(&gmap, 0, sizeof(gmap));
-    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kCG, kTile, kTile, 1);
+    const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, ldims, C, kCG, kTile, kTile, 1);
     auto kern = tma ? fpass_tc_kernel<true> : fpass_tc_kernel<false>;
     G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int64_t grid = nblocks * ngroups;

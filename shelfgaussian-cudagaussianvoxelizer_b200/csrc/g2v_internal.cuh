@@ -20,7 +20,14 @@ struct Grid {
     float h[3];      // voxel size
     int dims[3];     // X, Y, Z voxels
     int tiles[3];    // Tx, Ty, Tz tiles
+    int xoff;        // voxel x of the first row of the volume arrays (0: the arrays cover the whole grid)
+    int xlen;        // voxel x rows held by the volume arrays (dims[0] for whole-grid arrays)
 };
+
+// Row (voxel index) of voxel (x, y, z) in the volume arrays (density, grid_feats and their gradients).
+__host__ __device__ __forceinline__ int64_t grid_row(const Grid& G, int x, int y, int z) {
+    return ((int64_t)(x - G.xoff) * G.dims[1] + y) * G.dims[2] + z;
+}
 
 // Voxel centre along one axis: origin + (i + 1/2) * h (reference cu:825-828).
 __device__ __forceinline__ float voxel_centre(const Grid& G, int a, int i) {

@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
             const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
             const int x = ug.tx * kTile + (v >> 5), y = ug.ty * kTile + ((v >> 3) & 3), z = ug.tzp * 8 + (v & 7);
             const bool vin = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
-            const int64_t vrow = vin ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : -1;
+            const int64_t vrow = vin ? grid_row(G, x, y, z) : -1;
             const int npass = (K + kSlots - 1) / kSlots;
             const int njobs = npass == 1 ? 1 : 2 * npass;
             for (int jb = 0; jb < njobs && ok; ++jb) {
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                         if (!ok) break;
                         tc::mbar_arrive_expect_tx(&ms.gfull[gs], kGBytes);
                         tc::tma_load_4d_hint(tc::smem_u32(gstage + gs * kGBytes), &gmap, j * kKC, ug.tzp * 8,
-                                             ug.ty * kTile, ug.tx * kTile, &ms.gfull[gs], pol);
+                                             ug.ty * kTile, ug.tx * kTile - G.xoff, &ms.gfull[gs], pol);
                         issued = it + 1;
                     }
                 }
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
             if (et < kUV) {
                 const int x = x0 + (et >> 5), y = y0 + ((et >> 3) & 3), z = z0 + (et & 7);
                 const bool in = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
-                const int64_t row = in ? ((int64_t)x * G.dims[1] + y) * G.dims[2] + z : 0;
+                const int64_t row = in ? grid_row(G, x, y, z) : 0;
                 const float D = in ? density[row] : 0.0f;
                 const float den = fmaxf(D, kEps);
                 ms.lrd[et] = in ? -log2f(den) : -INFINITY;
@@ -635,7 +635,8 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
     }
     CUtensorMap gmap;
     memset(&gmap, 0, sizeof(gmap));
-    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, G.dims, C, kKC, 8, kTile, kTile, /*swizzle128*/ true);
+    const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, ldims, C, kKC, 8, kTile, kTile, /*swizzle128*/ true);
     auto kern = tma ? spass_tc_kernel<true> : spass_tc_kernel<false>;
     G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     int dev = 0, sms = 148;

@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) splat_tile_kernel(
             }
             if (c < C) {
                 const int64_t sz = C, sy = (int64_t)G.dims[2] * C, sx = (int64_t)G.dims[1] * sy;
-                float* base = grid_feats + (((int64_t)x0 * G.dims[1] + y0) * G.dims[2] + z0) * C + c;
+                float* base = grid_feats + grid_row(G, x0, y0, z0) * C + c;
                 const int nx = min(kTile, G.dims[0] - x0), ny = min(kTile, G.dims[1] - y0),
                           nz = min(kTile, G.dims[2] - z0);
 #pragma unroll
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) splat_tile_kernel(
         local_voxel(tid, lx, ly, lz);
         const int x = x0 + lx, y = y0 + ly, z = z0 + lz;
         if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
-            density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z] = zero_density ? 0.0f : sm.D[tid];
+            density[grid_row(G, x, y, z)] = zero_density ? 0.0f : sm.D[tid];
     }
 }
 }  // namespace

@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
                         ms.vscale[b][v] = ldexpf(1.0f, -kt) / fmaxf(D, kEps);
                         const int x = x0 + (v >> 5), y = y0 + ((v >> 3) & 3), z = z0 + (v & 7);
                         if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
-                            density[((int64_t)x * G.dims[1] + y) * G.dims[2] + z] = D;
+                            density[grid_row(G, x, y, z)] = D;
                     }
                     tc::mbar_arrive(&ms.dready[b]);
                     weight_barrier();  // dpart is reused by the next unit
@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
             const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
             const int x0 = ug.tx * kTile, y0 = ug.ty * kTile, z0 = ug.tzp * 8;
             const int nx = min(kTile, G.dims[0] - x0), ny = min(kTile, G.dims[1] - y0), nz = min(8, G.dims[2] - z0);
-            const int64_t row0 = ((int64_t)x0 * G.dims[1] + y0) * G.dims[2] + z0;
+            const int64_t row0 = grid_row(G, x0, y0, z0);
             if (K == 0) {  // no Gaussian reaches the unit: zeros
                 for (int v = 0; v < kUV; ++v) {
                     const int lx = v >> 5, ly = (v >> 3) & 3, lz = v & 7;

@@ -214,7 +214,7 @@ namespace g2v {
 namespace tc {
 
 // ---------------------------------------------------------------------------------------------
-// TMA and mbarrier transaction helpers (single CTA; no cluster multicast anywhere in this library).
+// TMA and mbarrier transaction helpers (single CTA, this CTA's own shared memory only).
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");

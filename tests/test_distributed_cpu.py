@@ -1,0 +1,88 @@
+"""Host logic of the single-scene split (CudaGaussianVoxelizer.distributed) on CPU: the slab partition,
+the gradient packing, and -- with two gloo ranks -- that the slab-partial gradients combined by
+allreduce_grads equal the whole-grid gradients (per-slab compute by the float64 oracle)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from CudaGaussianVoxelizer import distributed as D
+from oracle import oracle
+
+
+@pytest.mark.parametrize("tiles,world", [(50, 1), (50, 2), (50, 8), (100, 8), (7, 3), (3, 8)])
+def test_slab_tiles_partition(tiles, world):
+    ranges = [D.slab_tiles(tiles, r, world) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == tiles
+    for (b0, e0), (b1, e1) in zip(ranges, ranges[1:]):
+        assert e0 == b1 and b0 <= e0
+    sizes = [e - b for b, e in ranges]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_slab_voxel_rows_clip_the_last_tile():
+    assert D.slab_voxel_rows(10, (0, 2)) == (0, 8)
+    assert D.slab_voxel_rows(10, (2, 3)) == (8, 10)  # the last tile holds 2 voxel rows
+
+
+def test_pack_unpack_roundtrip():
+    g = torch.Generator().manual_seed(3)
+    n, c = 17, 5
+    parts = (torch.randn(n, 3, generator=g), torch.randn(n, 9, generator=g), torch.randn(n, generator=g),
+             torch.randn(n, c, generator=g))
+    buf = D.pack_grads(*parts)
+    assert buf.shape == (n, 13 + c)
+    for a, b in zip(D.unpack_grads(buf, c), parts):
+        assert torch.equal(a, b)
+    m, cv, o, f = D.unpack_grads(D.pack_grads(parts[0], parts[1], parts[2], None), 0)
+    assert f.shape == (n, 0) and torch.equal(o, parts[2])
+
+
+def _scene():
+    size, rng = [0.4] * 3, [-4.0, -4.0, -1.0, 4.0, 4.0, 2.2]
+    m, o, cv, f = oracle.generate_inputs(120, 6, rng, seed=5, num_outside=6)
+    m, o, cv, f = m.numpy(), o.numpy(), cv.numpy(), f.numpy()
+    bx = oracle.boxes(m, cv, size, rng)
+    dims = bx.dims
+    g = torch.Generator().manual_seed(11)
+    gD = torch.randn(*dims, generator=g).numpy()
+    gF = torch.randn(*dims, f.shape[1], generator=g).numpy()
+    dref, fref = oracle.forward(m, o, cv, f, bx.lb, bx.ub, size, rng, dims)
+    return size, rng, m, o, cv, f, bx, dims, gD, gF, dref, fref
+
+
+def _rank_main(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        size, rng, m, o, cv, f, bx, dims, gD, gF, dref, fref = _scene()
+        tiles_x = (dims[0] + 3) // 4
+        tr = D.slab_tiles(tiles_x, rank, world)
+        xr = D.slab_voxel_rows(dims[0], tr)
+        gm, gc, go, gf = oracle.backward(m, o, cv, f, bx.lb, bx.ub, size, rng, dims, gD, gF, dref, fref, x_range=xr)
+        tm, tcv, to, tf = D.allreduce_grads(*(torch.from_numpy(np.ascontiguousarray(a)) for a in (gm, gc, go, gf)))
+        if rank == 0:
+            np.savez(out_path, m=tm.numpy(), c=tcv.numpy(), o=to.numpy(), f=tf.numpy())
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_slab_gradients_sum_to_whole_grid(tmp_path, world):
+    out = str(tmp_path / "grads.npz")
+    mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
+    size, rng, m, o, cv, f, bx, dims, gD, gF, dref, fref = _scene()
+    rm, rc, ro, rf = oracle.backward(m, o, cv, f, bx.lb, bx.ub, size, rng, dims, gD, gF, dref, fref)
+    with np.load(out) as z:
+        for key, ref in (("m", rm), ("c", rc), ("o", ro), ("f", rf)):
+            np.testing.assert_allclose(z[key], ref, rtol=1e-9, atol=1e-12)
