@@ -17,6 +17,8 @@
 //           in the Gaussian->Tile CSR.
 //   F-pass  one CTA per (block of tiles, 64 channels): df partial rows of every (Gaussian, block) pair.
 //   reduce  per Gaussian, in CSR order: sums of the pair partials -> the output gradients.
+#include <algorithm>
+
 #include "g2v_internal.cuh"
 
 namespace g2v {
@@ -392,7 +394,11 @@ __global__ void __launch_bounds__(256) reduce10_kernel(const float* __restrict__
     }
 }
 
-// CTA per Gaussian: sums its block partial rows (blocks with x in the slab's block range).
+// CTA per Gaussian: sums its block partial rows (blocks with x in the slab's block range).  The rows of
+// one block-x column are contiguous, so each thread streams a run of rows for its 4 channels with
+// 16-byte loads and four independent accumulators (several loads in flight per thread); the sum is taken
+// in row order, so results do not depend on the launch shape.
+template <bool kVec>
 __global__ void __launch_bounds__(256) reduce_feats_kernel(const float* __restrict__ partialF,
                                                            const int32_t* __restrict__ g2b_offsets,
                                                            const int32_t* __restrict__ lb,
@@ -412,17 +418,46 @@ __global__ void __launch_bounds__(256) reduce_feats_kernel(const float* __restri
         }
     }
     const int64_t base = g2b_offsets[g];
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float acc = 0.0f;
-        if (ok) {
-            for (int lx = 0; lx < ext[0]; ++lx) {
-                const int bx = blo[0] + lx;
-                if (bx < bx_begin || bx >= bx_end) continue;
-                const int64_t r0 = base + (int64_t)lx * ext[1] * ext[2];
-                for (int j = 0; j < ext[1] * ext[2]; ++j) acc += partialF[(r0 + j) * C + c];
+    const int run = ext[1] * ext[2];  // rows of one block-x column
+    if (kVec) {
+        const int C4 = C >> 2;
+        for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ok) {
+                for (int lx = 0; lx < ext[0]; ++lx) {
+                    const int bx = blo[0] + lx;
+                    if (bx < bx_begin || bx >= bx_end) continue;
+                    const float4* p = reinterpret_cast<const float4*>(partialF + (base + (int64_t)lx * run) * C) + c4;
+                    int j = 0;
+                    for (; j + 4 <= run; j += 4) {
+                        const float4 a0 = __ldg(p + (int64_t)(j + 0) * C4), a1 = __ldg(p + (int64_t)(j + 1) * C4);
+                        const float4 a2 = __ldg(p + (int64_t)(j + 2) * C4), a3 = __ldg(p + (int64_t)(j + 3) * C4);
+                        acc.x += a0.x; acc.y += a0.y; acc.z += a0.z; acc.w += a0.w;
+                        acc.x += a1.x; acc.y += a1.y; acc.z += a1.z; acc.w += a1.w;
+                        acc.x += a2.x; acc.y += a2.y; acc.z += a2.z; acc.w += a2.w;
+                        acc.x += a3.x; acc.y += a3.y; acc.z += a3.z; acc.w += a3.w;
+                    }
+                    for (; j < run; ++j) {
+                        const float4 a0 = __ldg(p + (int64_t)j * C4);
+                        acc.x += a0.x; acc.y += a0.y; acc.z += a0.z; acc.w += a0.w;
+                    }
+                }
             }
+            reinterpret_cast<float4*>(grad_features + g * C)[c4] = acc;
         }
-        grad_features[g * C + c] = acc;
+    } else {
+        for (int c = threadIdx.x; c < C; c += blockDim.x) {
+            float acc = 0.0f;
+            if (ok) {
+                for (int lx = 0; lx < ext[0]; ++lx) {
+                    const int bx = blo[0] + lx;
+                    if (bx < bx_begin || bx >= bx_end) continue;
+                    const int64_t r0 = base + (int64_t)lx * run;
+                    for (int j = 0; j < run; ++j) acc += partialF[(r0 + j) * C + c];
+                }
+            }
+            grad_features[g * C + c] = acc;
+        }
     }
 }
 }  // namespace
@@ -487,8 +522,20 @@ int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const
                         int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
                         cudaStream_t s) {
     if (n == 0 || C == 0) return 0;
-    G2V_TIMED("reduce_feats_kernel", s, reduce_feats_kernel<<<(unsigned)n, 256, 0, s>>>(partialF, g2b_offsets, lb, ub, C, B[0], B[1], B[2], bx_begin,
-                                                    bx_end, grad_features));
+    // 16-byte rows: C % 4 == 0 and 16-byte aligned bases (the partial rows live in the library's workspace)
+    const bool vec = C % 4 == 0 && (reinterpret_cast<uintptr_t>(partialF) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(grad_features) & 15) == 0;
+    const int threads = vec ? std::min(256, std::max(32, ((C / 4 + 31) / 32) * 32)) : 256;
+    if (vec)
+        G2V_TIMED("reduce_feats_kernel", s,
+                  reduce_feats_kernel<true><<<(unsigned)n, threads, 0, s>>>(partialF, g2b_offsets, lb, ub, C, B[0],
+                                                                            B[1], B[2], bx_begin, bx_end,
+                                                                            grad_features));
+    else
+        G2V_TIMED("reduce_feats_kernel", s,
+                  reduce_feats_kernel<false><<<(unsigned)n, threads, 0, s>>>(partialF, g2b_offsets, lb, ub, C, B[0],
+                                                                             B[1], B[2], bx_begin, bx_end,
+                                                                             grad_features));
     G2V_LAUNCH_CHECK("reduce_feats_kernel");
     return 0;
 }
