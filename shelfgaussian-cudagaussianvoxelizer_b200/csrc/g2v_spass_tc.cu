@@ -12,7 +12,8 @@
 // lists (ascending ids).  Pairing halves the feature-row gathers and doubles the MMA's N against the
 // per-tile shape, at the price of the Gaussians that reach only one of the two tiles.
 // MMA: M = 128 Gaussians (two M-blocks = 256 slots per pass), N = the unit's 128 voxels, K = 32
-// channels per pipeline step; both operands K-major without swizzle (8-row x 16-byte core matrices).
+// channels per pipeline step; both operands K-major with 64-byte swizzle (a row = the step's 32
+// channels; atoms of 8 rows x 64 bytes, 16-byte chunk c of row r stored at chunk c ^ ((r / 2) % 4)).
 // A rows are the features, pre-split once into bf16 hi/lo rows padded to Cp channels and gathered with
 // 16-byte cp.async; B rows are the upstream gradient of the unit's voxels, brought in by one tiled TMA
 // load of the 4-D tensor map {C, Z, Y, X} per step and converted fp32 -> bf16 hi/lo in shared memory
@@ -52,7 +53,13 @@ constexpr int kAStage = 2 * kAHalf;               // hi + lo
 constexpr int kBStage = 2 * kBHalf;
 constexpr int kGBytes = kUV * kKC * 4;            // 16 KB: [x][y][z8][32 channels], 128-byte swizzle
 static_assert(kKC * 4 == 128, "the staging rows are one 128-byte swizzle span");
-constexpr int kRowGroupBytes = (kKC / 8) * 128;   // 8 rows x kKC channels: 4 core matrices along K
+constexpr int kRowGroupBytes = 8 * kKC * 2;       // 8 rows x kKC bf16: one 64-byte-swizzle atom
+static_assert(kKC * 2 == 64, "a K-major row of the step is one 64-byte swizzle span");
+
+// Byte offset of 16-byte chunk c of row r in a K-major 64-byte-swizzled operand.
+__device__ __forceinline__ uint32_t sw64_off(int r, int c) {
+    return (uint32_t)((r >> 3) * kRowGroupBytes + (r & 7) * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
 constexpr int kMBlockBytes = 16 * kRowGroupBytes; // 128 rows
 constexpr uint32_t kTmemCols = 512;
 constexpr int kBufCols = 256;                     // one job: 2 M-blocks x 128 voxel columns
@@ -208,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                     for (int q = 0; q < 8; ++q) {
                         const int slot = q * 32 + warp * 8 + rs;
                         if (slot < nrows) {
-                            const uint32_t aoff = (slot >> 3) * kRowGroupBytes + kc * 128 + (slot & 7) * 16;
+                            const uint32_t aoff = sw64_off(slot, kc);
                             const int64_t src = goff[q] >= 0 ? goff[q] + (int64_t)(c0 + kc * 8) * 2 : 0;
                             const uint32_t nb = goff[q] >= 0 ? 16u : 0u;
                             tc::cp_async16_hint(a_half(sa, 0) + aoff, reinterpret_cast<const char*>(Fh) + src, nb, pol);
@@ -223,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
     } else if (warp < 8) {
         // ============ gradient-row converters: staged fp32 -> bf16 hi / lo; thread = voxel row v ============
         const int v = tid - 128;
-        const int boff0 = (v >> 3) * kRowGroupBytes + (v & 7) * 16;
+        unsigned char* const bbase = bring;
         int it = 0;
         for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
             const int K = unit_offsets[u + 1] - unit_offsets[u];
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                     if (it >= kSB) ok = tc::mbar_wait(&ms.empty_b[sb], ((it / kSB) + 1) & 1, err);
                     if (kTma && ok) ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
                     if (!ok) break;
-                    unsigned char* bst = bring + sb * kBStage + boff0;
+                    unsigned char* bst = bbase + sb * kBStage;
                     // 128-byte swizzled staging row: logical chunk c sits at chunk c ^ (v % 8)
                     const unsigned char* row = gstage + gs * kGBytes + v * (kKC * 4);
 #pragma unroll
@@ -271,10 +278,11 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                         tc::split_bf16x2(f[10], f[11], h1.y, l1.y);
                         tc::split_bf16x2(f[12], f[13], h1.z, l1.z);
                         tc::split_bf16x2(f[14], f[15], h1.w, l1.w);
-                        *reinterpret_cast<uint4*>(bst + hv * 256) = h0;
-                        *reinterpret_cast<uint4*>(bst + hv * 256 + 128) = h1;
-                        *reinterpret_cast<uint4*>(bst + kBHalf + hv * 256) = l0;
-                        *reinterpret_cast<uint4*>(bst + kBHalf + hv * 256 + 128) = l1;
+                        const uint32_t o0 = sw64_off(v, 2 * hv), o1 = sw64_off(v, 2 * hv + 1);
+                        *reinterpret_cast<uint4*>(bst + o0) = h0;
+                        *reinterpret_cast<uint4*>(bst + o1) = h1;
+                        *reinterpret_cast<uint4*>(bst + kBHalf + o0) = l0;
+                        *reinterpret_cast<uint4*>(bst + kBHalf + o1) = l1;
                     }
                     tc::fence_async_smem();
                     __syncwarp();
@@ -310,16 +318,17 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                         tc::tc_fence_after();
 #pragma unroll
                         for (int ks = 0; ks < kKC / 16; ++ks) {
+                            // K step ks = channels 16 ks .. 16 ks + 15: 32 bytes into each swizzled row
                             const uint64_t bh =
-                                tc::smem_desc(b_half(sb, 0) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
+                                tc::smem_desc(b_half(sb, 0) + ks * 32, 16, kRowGroupBytes, tc::kLayoutSw64);
                             const uint64_t bl =
-                                tc::smem_desc(b_half(sb, 1) + ks * 256, 128, kRowGroupBytes, tc::kLayoutNone);
+                                tc::smem_desc(b_half(sb, 1) + ks * 32, 16, kRowGroupBytes, tc::kLayoutSw64);
                             for (int mb = 0; mb < nmb; ++mb) {
-                                const uint32_t ao = mb * kMBlockBytes + ks * 256;
+                                const uint32_t ao = mb * kMBlockBytes + ks * 32;
                                 const uint64_t ah =
-                                    tc::smem_desc(a_half(sa, 0) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
+                                    tc::smem_desc(a_half(sa, 0) + ao, 16, kRowGroupBytes, tc::kLayoutSw64);
                                 const uint64_t al =
-                                    tc::smem_desc(a_half(sa, 1) + ao, 128, kRowGroupBytes, tc::kLayoutNone);
+                                    tc::smem_desc(a_half(sa, 1) + ao, 16, kRowGroupBytes, tc::kLayoutSw64);
                                 const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
                                 tc::mma_f16_ss(d, ah, bh, kIdesc, j > 0 || ks > 0);
                                 tc::mma_f16_ss(d, ah, bl, kIdesc, true);

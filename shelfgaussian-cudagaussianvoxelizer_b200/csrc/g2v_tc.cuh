@@ -24,9 +24,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 // ---------------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05): start address, leading / stride byte offsets (16-byte
-// units), version 1, layout type in bits 61-63 (0 = no swizzle, 2 = 128-byte swizzle).
+// units), version 1, layout type in bits 61-63 (0 = no swizzle, 2 = 128-byte, 4 = 64-byte, 6 = 32-byte
+// swizzle).  In a swizzled layout the 16-byte chunk index of an address (bits 4..) is XORed with its
+// 128-byte row index (bits 7..): 3 bits for 128-byte, 2 for 64-byte, 1 for 32-byte swizzle, repeating
+// every 1024 / 512 / 256 bytes, so atoms start on those boundaries.
 constexpr int kLayoutNone = 0;
 constexpr int kLayoutSw128 = 2;
+constexpr int kLayoutSw64 = 4;
+constexpr int kLayoutSw32 = 6;
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, int layout) {
     uint64_t d = 0;
