@@ -10,7 +10,7 @@
 // Operands in shared memory (per stage):
 //   A = gF^T slice (256 channels x 16 voxels) MN-major, 128-byte swizzle (64-channel x 8-voxel atoms),
 //       converted from the fp32 gradient rows by the producer warps;
-//   B = weights (256 slots x 16 voxels) K-major, no swizzle (8x8 core matrices), evaluated by the weight
+//   B = weights (256 slots x 16 voxels) K-major, 32-byte swizzle (a row = one slot's 16 voxels), evaluated by the weight
 //       warps from the slot's parameters: over the 4x4 voxels of an x-slice the Mahalanobis distance is a
 //       quadratic in (ly, lz), so each weight costs a few FMAs and one exp.
 // The fp32 gradient rows of a step (16 voxels x 256 channels, 16 KB) arrive in a staging ring through
@@ -307,11 +307,13 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 tc::split_bf16x2(w[10], w[11], h1.y, l1.y);
                 tc::split_bf16x2(w[12], w[13], h1.z, l1.z);
                 tc::split_bf16x2(w[14], w[15], h1.w, l1.w);
-                const int off = (t >> 3) * 256 + (t & 7) * 16;
-                *reinterpret_cast<uint4*>(b_stage(st, 0) + off) = h0;
-                *reinterpret_cast<uint4*>(b_stage(st, 0) + off + 128) = h1;
-                *reinterpret_cast<uint4*>(b_stage(st, 1) + off) = l0;
-                *reinterpret_cast<uint4*>(b_stage(st, 1) + off + 128) = l1;
+                // K-major, 32-byte swizzle: row t = the slot's 16 voxels (32 bytes), chunk c at c ^ ((t / 4) % 2)
+                const int sw = (t >> 2) & 1;
+                const int off0 = (t >> 3) * 256 + (t & 7) * 32 + (sw << 4), off1 = off0 ^ 16;
+                *reinterpret_cast<uint4*>(b_stage(st, 0) + off0) = h0;
+                *reinterpret_cast<uint4*>(b_stage(st, 0) + off1) = h1;
+                *reinterpret_cast<uint4*>(b_stage(st, 1) + off0) = l0;
+                *reinterpret_cast<uint4*>(b_stage(st, 1) + off1) = l1;
                 }
                 tc::fence_async_smem();
                 __syncwarp();
@@ -337,8 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
                 if (!ok) break;
                 tc::tc_fence_after();
-                const uint64_t bh = tc::smem_desc(tc::smem_u32(b_stage(st, 0)), 128, 256, tc::kLayoutNone);
-                const uint64_t blo = tc::smem_desc(tc::smem_u32(b_stage(st, 1)), 128, 256, tc::kLayoutNone);
+                const uint64_t bh = tc::smem_desc(tc::smem_u32(b_stage(st, 0)), 16, 256, tc::kLayoutSw32);
+                const uint64_t blo = tc::smem_desc(tc::smem_u32(b_stage(st, 1)), 16, 256, tc::kLayoutSw32);
 #pragma unroll
                 for (int mb = 0; mb < kMB; ++mb) {
                     const uint64_t ah = tc::smem_desc(tc::smem_u32(a_stage(st, 0)) + mb * 4096, 1024, 2048,
