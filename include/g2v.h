@@ -217,6 +217,14 @@ G2V_API int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussian
 G2V_API int g2v_device_error(void* stream, int* word);
 
 /*
+ * Self-test of the failure path (no reference counterpart): launches one CTA that waits on an mbarrier
+ * nothing arrives at, with the library's bounded wait (about 2 s), and synchronises `stream`.  On return
+ * *gave_up is 1 when the wait gave up as designed, and the device error word holds its timeout bit
+ * (read and clear it with g2v_device_error).  The context stays usable.
+ */
+G2V_API int g2v_debug_wait_timeout(void* stream, int* gave_up);
+
+/*
  * Profiling hook (no reference counterpart): when enabled, every kernel launch of the library is
  * bracketed by CUDA events on its launch stream.  g2v_profile_enable(1) clears the records and starts
  * recording, g2v_profile_enable(0) stops.  g2v_profile_read(i, ...) waits for the recorded events,

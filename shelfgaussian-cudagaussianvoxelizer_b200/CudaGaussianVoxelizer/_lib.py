@@ -44,6 +44,7 @@ SIGNATURES = {
                            P, SZ, P]),
     "g2v_debug_copy_t2g": (I32, [P, I64, I64, I3, P, P, P]),
     "g2v_device_error": (I32, [P, ctypes.POINTER(I32)]),
+    "g2v_debug_wait_timeout": (I32, [P, ctypes.POINTER(I32)]),
     "g2v_profile_enable": (I32, [I32]),
     "g2v_profile_read": (I32, [I32, ctypes.c_char_p, SZ, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(I64)]),
 }

@@ -35,6 +35,7 @@ SOURCES = {
     "g2v_splat_tc.cu": [],
     "g2v_grad_tc.cu": [],
     "g2v_spass_tc.cu": [],
+    "g2v_selftest.cu": [],
 }
 HEADERS_TC = ["g2v_tc.cuh"]
 HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(HERE, "g2v_tc.cuh"), os.path.join(INCLUDE, "g2v.h")]

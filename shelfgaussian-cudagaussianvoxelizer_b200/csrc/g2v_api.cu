@@ -61,6 +61,7 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
                     const float* density, const GParams* gparams, const int32_t* g2t_offsets,
                     const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
                     const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s);
+int launch_wait_timeout(int* err, cudaStream_t s, int* gave_up_host);
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
                     const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
                     float* grad_opacity, cudaStream_t s);
@@ -463,6 +464,18 @@ int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64
         G2V_CUDA(cudaMemcpyAsync(t2g_gaussians, w.lists, sizeof(int32_t) * (size_t)num_pairs,
                                  cudaMemcpyDeviceToDevice, s));
     return G2V_SUCCESS;
+}
+
+int g2v_debug_wait_timeout(void* stream, int* gave_up) {
+    g_msg[0] = 0;
+    if (!gave_up) {
+        set_error("gave_up must not be NULL");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    int* err = nullptr;
+    int rc = device_error_ptr(&err);
+    if (rc) return rc;
+    return launch_wait_timeout(err, static_cast<cudaStream_t>(stream), gave_up);
 }
 
 int g2v_device_error(void* stream, int* word) {
