@@ -405,6 +405,90 @@ def run_reference(args, rank, world, dev):
     return line
 
 
+def run_single_scene(args, rank, world, dev):
+    """One scene split into x-slabs over the ranks (CudaGaussianVoxelizer.distributed): every rank holds
+    the same Gaussians, splats its slab, and one NCCL all-reduce sums the gradients.  Strong scaling:
+    the total work is fixed as N grows; `value` is the max-over-ranks device time of a step."""
+    import torch
+    import torch.distributed as dist
+    from CudaGaussianVoxelizer import _C, _lib
+    from CudaGaussianVoxelizer.distributed import SlabGaussianVoxelizer
+
+    cfg = CONFIGS[args.config]
+    size, rng, m_h, o_h, c_h, f_h = make_inputs(cfg, seed=args.seed)  # the same scene on every rank
+    (X, Y, Z), tiles = _C.grid_shape(size, rng)
+    n, c = cfg["n"], cfg["c"]
+    vox = SlabGaussianVoxelizer(voxel_size=size, voxel_range=rng, rank=rank, world=world)
+    x0, x1 = vox.rows
+    g = torch.Generator(device=dev).manual_seed(1000)
+    gD = torch.randn((X, Y, Z), device=dev, generator=g)[x0:x1].contiguous()
+    gF = torch.randn((X, Y, Z, c), device=dev, generator=g)[x0:x1].contiguous()
+    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
+
+    def step():
+        density, grid_feats, _ = vox(*leaves)
+        return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    sampler = ClockSampler(gpu_id_for(dev.index))
+    ms = timed(step)
+    clocks = sampler.stop()
+    host = [t.pin_memory() for t in (m_h, o_h, c_h, f_h)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+
+    def e2e_step():
+        ls = [t.to(dev, non_blocking=True).requires_grad_() for t in host]
+        density, grid_feats, _ = vox(*ls)
+        grads = torch.autograd.grad([density, grid_feats], ls, [gD, gF])
+        return grads[0].reshape(-1)[:1].to("cpu").item()
+
+    e2e_ms = timed(e2e_step)
+    _lib.profile_enable(True)
+    step()
+    torch.cuda.synchronize()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    tot = sum(v[0] for v in prof.values()) or 1.0
+    return {
+        "metric": METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference distributions)",
+        "config": {"workload": f"{args.config}: one scene, N={n} Gaussians, C={c}, {X}x{Y}x{Z} voxels, split into "
+                               f"{world} x-slabs of tiles (rank 0: tiles {vox.tile_range}), one NCCL all-reduce of "
+                               f"the packed gradients per step", "global_batch": 1,
+                   "parallelism": f"x-slab split over {world} GPUs",
+                   "l2": "inputs larger than L2 (grid_feats 4*V*C bytes)"},
+        "rank0_kernel_share": {k: round(v[0] / tot, 4) for k, v in prof.items()},
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(sum(v[1] for v in prof.values())),
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -416,6 +500,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-cuda", action="store_true")
     ap.add_argument("--forward-only", action="store_true", help="profiling mode: forward passes only")
+    ap.add_argument("--single-scene", action="store_true",
+                    help="one scene split into x-slabs over the ranks (strong scaling) instead of one scene per rank")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -441,7 +527,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     try:
-        line = run_ours(args, rank, world, dev)
+        line = (run_single_scene if args.single_scene else run_ours)(args, rank, world, dev)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
