@@ -25,13 +25,18 @@
 // Roles (544 threads): warps 0-3 gather feature rows and stage the step's Gaussian records; warps 4-7
 // evaluate the weights (thread = z-line of 8 voxels x Gaussian pair; along z the exponent is a
 // quadratic, so each weight is two FMAs and one exp2) and, in a unit's first job, the density; warp 8
-// (one thread) issues the 6 MMAs of a step; warps 9-16 run the epilogue (thread = channel, streaming
-// stores).
-// Eight stages; every mbarrier wait is bounded.
+// (one thread) issues the 6 MMAs of a step; warps 9-16 run the epilogue (thread = channel): the scaled
+// values of 16 voxels x 256 channels go to a shared-memory tile that one tiled TMA store writes out
+// (L2 evict_first; the store clips the grid edges), double-buffered, or -- when the tensor map cannot be
+// built (C % 4 != 0, unaligned output) -- straight to global memory with streaming stores.
+// Seven stages; every mbarrier wait is bounded.
 #include <cstddef>
+
+#include <cstring>
 
 #include "g2v_internal.cuh"
 #include "g2v_tc.cuh"
+#include "g2v_tmap.cuh"
 
 namespace g2v {
 
@@ -40,7 +45,8 @@ constexpr int kThreads = 544;             // 17 warps
 constexpr int kKStep = 16;                // Gaussians per pipeline step
 constexpr int kCG = 256;                  // channels per job (two M-blocks)
 constexpr int kUV = 128;                  // voxels per unit
-constexpr int kStages = 8;
+constexpr int kStages = 7;
+constexpr int kOutBytes = 16 * kCG * 4;  // epilogue staging tile: 16 voxels x 256 channels fp32
 constexpr int kAHalf = 2 * 4096;          // 256 channels x 16 Gaussians, one half (hi or lo)
 constexpr int kBHalf = 4096;              // 128 voxels x 16 Gaussians, one half
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
@@ -71,7 +77,7 @@ struct TcMisc {
     alignas(16) float dpart[kKStep / 2][kUV];  // density partials [Gaussian pair][voxel], scaled by 2^kt
     alignas(16) StepParams prm[kStages];
 };
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(TcMisc);
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 2 * (size_t)kOutBytes + sizeof(TcMisc);
 static_assert(kSmemBytes <= 227 * 1024, "splat_tc_kernel shared memory");
 static_assert(offsetof(TcMisc, vscale) % 16 == 0 && offsetof(TcMisc, prm) % 16 == 0,
               "vector-accessed shared fields must be 16-byte aligned");
@@ -157,14 +163,19 @@ __device__ __forceinline__ UnitGeom unit_geom(int u, int ty_n, int tzp_n, int tx
     return g;
 }
 
+// Named barrier of the 8 epilogue warps.
+__device__ __forceinline__ void epi_barrier() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+template <bool kTmaStore>
 __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
-    const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C, int Cp,
+    const __grid_constant__ CUtensorMap omap, const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C, int Cp,
     const GParams* __restrict__ gparams, const int32_t* __restrict__ unit_offsets,
     const int32_t* __restrict__ unit_lists, int num_units, int tx_begin, Grid G, float* __restrict__ density,
     float* __restrict__ grid_feats, int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
-    TcMisc& ms = *reinterpret_cast<TcMisc*>(base + kStages * kStageBytes);
+    unsigned char* ostage = base + kStages * kStageBytes;  // 2 epilogue staging tiles
+    TcMisc& ms = *reinterpret_cast<TcMisc*>(ostage + 2 * kOutBytes);
     if ((tc::smem_u32(smem_raw) & 1023u) != 0) {  // the swizzle atoms need 1 KB alignment; never expected
         if (threadIdx.x == 0) atomicOr(err, 2);
         return;
@@ -401,7 +412,8 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
         const int q = warp & 3;               // TMEM lane quarter of this warp
         const int mb = (warp - kEpiWarp0) >> 2;
         const int64_t sx = (int64_t)G.dims[1] * G.dims[2], sy = G.dims[2];
-        int job = 0, nu = 0;
+        const uint64_t opol = tc::l2_policy_evict_first();  // grid_feats is written once
+        int job = 0, nu = 0, ochunk = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
             const int K = unit_offsets[u + 1] - unit_offsets[u];
             const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
@@ -429,7 +441,40 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
                 const bool cok = c < C;
                 const float us = cok ? unscale[c] : 0.0f;
                 const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kBufCols + mb * kUV);
-                if (good) {
+                if (kTmaStore) {
+                    // all 8 warps take part in every chunk (the staging tile spans the job's 256 channels)
+                    const int cl = mb * 128 + q * 32 + lane;  // channel within the job
+#pragma unroll 1
+                    for (int ch = 0; ch < 8; ++ch, ++ochunk) {  // x-slice lx = ch / 2, ly = 2 (ch % 2) + e / 8
+                        float vals[16];
+                        if (good) {
+                            tc::tmem_ld16(taddr + ch * 16, vals);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) vals[e] = 0.0f;
+                        }
+                        const float4* vs4 = reinterpret_cast<const float4*>(&ms.vscale[b][ch * 16]);
+                        const int sb = ochunk & 1;
+                        float* st = reinterpret_cast<float*>(ostage + sb * kOutBytes);
+                        if (et == 0) tc::bulk_wait_group_read<1>();  // the store that last read tile sb is done
+                        epi_barrier();
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            const float4 r4 = vs4[e4];
+                            st[(4 * e4 + 0) * kCG + cl] = vals[4 * e4 + 0] * (us * r4.x);
+                            st[(4 * e4 + 1) * kCG + cl] = vals[4 * e4 + 1] * (us * r4.y);
+                            st[(4 * e4 + 2) * kCG + cl] = vals[4 * e4 + 2] * (us * r4.z);
+                            st[(4 * e4 + 3) * kCG + cl] = vals[4 * e4 + 3] * (us * r4.w);
+                        }
+                        tc::fence_async_smem();
+                        epi_barrier();
+                        if (et == 0 && good) {
+                            tc::tma_store_4d_hint(&omap, tc::smem_u32(st), cg * kCG, z0, y0 + 2 * (ch & 1),
+                                                  x0 + (ch >> 1) - G.xoff, opol);
+                            tc::bulk_commit_group();
+                        }
+                    }
+                } else if (good) {
 #pragma unroll 1
                     for (int ch = 0; ch < 8; ++ch) {  // 16 columns: x-slice lx = ch / 2, ly = 2 (ch % 2) + (e / 8)
                         float vals[16];
@@ -463,6 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
             if (lane == 0) tc::mbar_arrive(&ms.dfree[b]);
             ++nu;
         }
+        if (kTmaStore && et == 0) tc::bulk_wait_group_all();  // the output is written before the CTA exits
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -515,13 +561,18 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
     GParams* gp = cv.take<GParams>((size_t)(n > 0 ? n : 1));
     int rc = launch_pack_params(means, opacity, cov_inv, lb, ub, n, gp, s);
     if (rc) return rc;
-    G2V_CUDA(cudaFuncSetAttribute(splat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    CUtensorMap omap;
+    memset(&omap, 0, sizeof(omap));
+    const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
+    const bool tma = C > 0 && encode_grid_rows_f32(&omap, grid_feats, ldims, C, kCG, 8, 2, 1);
+    auto kern = tma ? splat_tc_kernel<true> : splat_tc_kernel<false>;
+    G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     int dev = 0, sms = 148;
     G2V_CUDA(cudaGetDevice(&dev));
     G2V_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int grid = num_units < sms ? num_units : sms;
     G2V_TIMED("splat_tc_kernel", s,
-              splat_tc_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(hi, lo, unscale, C, Cp, gp, unit_offsets,
+              kern<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(omap, hi, lo, unscale, C, Cp, gp, unit_offsets,
                                                                             unit_lists, num_units, tile_x_begin, G,
                                                                             density, grid_feats, err));
     G2V_LAUNCH_CHECK("splat_tc_kernel");

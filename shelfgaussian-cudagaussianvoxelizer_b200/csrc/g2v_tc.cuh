@@ -287,6 +287,26 @@ __device__ __forceinline__ void tma_load_4d_hint(uint32_t dst_saddr, const void*
         : "memory");
 }
 
+// Tiled 4-D store of a box from shared memory to global memory (bulk-group completion) with an L2
+// cache policy.  c0 * element size must be a multiple of 16 bytes and no coordinate may be negative;
+// the parts of the box beyond the tensor are not written.
+__device__ __forceinline__ void tma_store_4d_hint(const void* tmap, uint32_t src_saddr, int c0, int c1, int c2, int c3,
+                                                  uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group.L2::cache_hint"
+        " [%0, {%2, %3, %4, %5}], [%1], %6;" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+        "r"(src_saddr), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N bulk groups of this thread still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until all bulk groups of this thread have completed (writes visible).
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 }  // namespace tc
 }  // namespace g2v
 
