@@ -325,8 +325,7 @@ def cpu_baseline(cfg, seed, threads, steps=1, slab_vox=16):
 
 def reference_cuda(cfg, seed, dev, steps=2):
     """Time the reference's own CUDA build (oracle/_ref, compiled from its sources) on this GPU."""
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import build_ref
+    from oracle import build_ref
     ext = build_ref.load()
     if ext is None:
         return {"unavailable": "oracle/_ref has no reference build"}
@@ -489,6 +488,213 @@ def run_single_scene(args, rank, world, dev):
     }
 
 
+LOSS_METRIC = "feature cosine loss fwd+bwd ms/step over the voxel grid and % HBM roofline"
+
+
+def loss_bytes(kernel, V, C, nvalid):
+    """Algorithmic HBM bytes of one cosine-loss launch: label + mask of every voxel (5 B), prediction and
+    target rows of the valid voxels (8 C B), and for the backward the gradient of every voxel (4 C B)."""
+    if kernel == "cosine_loss_fwd_kernel":
+        return 5 * V + 8 * C * nvalid
+    if kernel == "cosine_loss_bwd_kernel":
+        return 5 * V + 8 * C * nvalid + 4 * C * V
+    return None
+
+
+def run_loss(args, rank, world, dev):
+    """Feature cosine loss (PyCudaFeatsCosineLoss) forward + backward on a resident grid.
+
+    Workload: the voxelizer's grid at --config (200x200x16 at cfg3) with --loss-channels channels (default
+    the config's C), labels and masks drawn as in the reference's loss tests (25% labelled x 70% visible),
+    target = prediction + 0.1 noise.  Every rank runs its own grid (weak scaling, no collective).  An L2
+    flush (a 256 MB write) separates the timed steps; only the steps are inside the events."""
+    import torch
+    import torch.distributed as dist
+    from CudaGaussianVoxelizer import PyCudaFeatsCosineLoss, _C, _lib
+
+    cfg = CONFIGS[args.config]
+    size = [cfg["size"]] * 3
+    (X, Y, Z), _ = _C.grid_shape(size, cfg["range"])
+    C = args.loss_channels or cfg["c"]
+    V = X * Y * Z
+    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    p = torch.randn((X, Y, Z, C), device=dev, generator=gen)
+    g = p + 0.1 * torch.randn((X, Y, Z, C), device=dev, generator=gen)
+    label = (torch.rand((X, Y, Z), device=dev, generator=gen) < 0.25).float()
+    mask = torch.rand((X, Y, Z), device=dev, generator=gen) < 0.7
+    nvalid = int((label.bool() & mask).sum().item())
+    p.requires_grad_(True)
+    crit = PyCudaFeatsCosineLoss(voxel_size=size, voxel_range=cfg["range"], timing=False)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        loss, _ = crit(label, mask, p, g)
+        return torch.autograd.grad(loss, p)[0]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        evs = []
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        barrier()
+        t = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    sampler = ClockSampler(gpu_id_for(dev.index))
+    ms = timed(step)
+    clocks = sampler.stop()
+
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        flush.fill_(1)
+        step()
+    torch.cuda.synchronize()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    peak, peak_kind = load_peaks()
+    kern = {}
+    for k, (kms, cnt) in prof.items():
+        b = loss_bytes(k, V, C, nvalid)
+        avg = kms / cnt
+        kern[k] = {"avg_launch_ms": avg, "algorithmic_bytes_per_launch": b,
+                   "achieved_gbs": b / (avg * 1e-3) / 1e9 if b else None,
+                   "frac": b / (avg * 1e-3) / 1e9 / peak if b else None}
+    top = "cosine_loss_bwd_kernel"
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as fh:
+            traffic = json.load(fh).get(f"loss_{args.config}_c{C}", {}).get(top)
+    roofline = {"bound": "hbm", "kernel": top, "achieved": kern[top]["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                "frac": kern[top]["frac"], "traffic": traffic,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_launch": kern[top]["algorithmic_bytes_per_launch"],
+                "avg_launch_ms": kern[top]["avg_launch_ms"], "kernels": kern}
+
+    # end to end: pinned host inputs copied every step, loss value read back
+    host = [t.detach().cpu().pin_memory() for t in (label, mask, p, g)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    crit_e2e = PyCudaFeatsCosineLoss(voxel_size=size, voxel_range=cfg["range"], timing=False)
+
+    def e2e_step():
+        lab, msk, pp, gg = [t.to(dev, non_blocking=True) for t in host]
+        pp.requires_grad_(True)
+        loss, _ = crit_e2e(lab, msk, pp, gg)
+        grad = torch.autograd.grad(loss, pp)[0]
+        return loss.item(), grad
+
+    e2e_ms = timed(e2e_step)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = loss_cpu_baseline(X, Y, Z, C)
+    return {
+        "metric": LOSS_METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; reference loss-test distributions)",
+        "config": {"workload": f"loss on {args.config}'s grid: {X}x{Y}x{Z} voxels, C={C}, {nvalid} valid voxels "
+                               f"(25% labelled x 70% visible), fwd+bwd via PyCudaFeatsCosineLoss + autograd",
+                   "global_batch": world, "l2": "256 MB L2 flush between timed steps (outside the events)",
+                   "parallelism": f"dp{world} (independent grids)"},
+        "roofline": roofline, "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(sum(v[1] for v in prof.values())),
+        "clocks": clocks,
+    }
+
+
+def loss_cpu_baseline(X, Y, Z, C, rows=None):
+    """The float64 oracle of the loss (numpy) on an x-slab of the grid, scaled to the whole grid."""
+    import numpy as np
+    from oracle import oracle
+    rows = rows or max(1, min(X, int(2e7 // max(1, Y * Z * max(C, 1)))))
+    label, mask, p, g = oracle.generate_loss_inputs((rows, Y, Z), C, "noise", seed=0)
+    label, mask, p, g = label.numpy(), mask.numpy(), p.numpy(), g.numpy()
+    ts = []
+    for _ in range(2):  # the first pass also pays the first touch of its float64 buffers
+        t0 = time.perf_counter()
+        _, count = oracle.cosine_loss_forward(label, mask, p, g)
+        oracle.cosine_loss_backward(1.0, count, label, mask, p, g)
+        ts.append(time.perf_counter() - t0)
+    t = ts[-1]
+    return {"value": round(t * 1e3 * X / rows, 1), "unit": "ms", "cores": 1, "kind": "port",
+            "sample": f"x-slab of {rows} of {X} voxel rows ({rows * Y * Z} voxels, C={C}), numpy float64, scaled "
+                      f"x{X / rows:.1f} to the full grid; {t:.2f} s per sample"}
+
+
+def reference_loss_cuda(X, Y, Z, C, dev, steps=3):
+    """The reference's own loss kernels (oracle/_ref build of src/cuda_feats_loss.cu) on the same grid."""
+    from oracle import build_ref
+    ext = build_ref.load()
+    if ext is None:
+        return {"unavailable": "oracle/_ref has no reference build"}
+    import torch
+    gen = torch.Generator(device=dev).manual_seed(2000)
+    p = torch.randn((X, Y, Z, C), device=dev, generator=gen)
+    g = p + 0.1 * torch.randn((X, Y, Z, C), device=dev, generator=gen)
+    label = (torch.rand((X, Y, Z), device=dev, generator=gen) < 0.25).float()
+    mask = torch.rand((X, Y, Z), device=dev, generator=gen) < 0.7
+    one = torch.ones((), device=dev)
+    ts = []
+    for i in range(steps + 1):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        loss, count, _ = ext.CudaFeatsCosinelossForward(label, mask, p, g)
+        ext.CudaFeatsCosinelossBackward(one, label, mask, p, g, count)
+        torch.cuda.synchronize()
+        if i:
+            ts.append((time.perf_counter() - t0) * 1e3)
+    return {"value": round(statistics.median(ts), 3), "unit": "ms",
+            "what": "reference CUDA build of src/cuda_feats_loss.cu (oracle/_ref), forward + backward, wall clock "
+                    "with its own host synchronisations"}
+
+
+def run_loss_reference(args, rank, world, dev):
+    cfg = CONFIGS[args.config]
+    from CudaGaussianVoxelizer import _C
+    (X, Y, Z), _ = _C.grid_shape([cfg["size"]] * 3, cfg["range"])
+    C = args.loss_channels or cfg["c"]
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = loss_cpu_baseline(X, Y, Z, C)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    value = statistics.median(vals)
+    cpu = dict(r)
+    cpu["value"] = value
+    line = {"metric": LOSS_METRIC, "value": value, "unit": "ms", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+            "config": {"workload": f"loss on {args.config}'s grid {X}x{Y}x{Z}, C={C}, CPU x-slab sample",
+                       "global_batch": 1},
+            "cpu_baseline": cpu, "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0}}
+    if dev is not None and not args.no_reference_cuda:
+        try:
+            line["reference_cuda"] = reference_loss_cuda(X, Y, Z, C, dev)
+        except Exception as exc:
+            line["reference_cuda"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -500,6 +706,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-cuda", action="store_true")
     ap.add_argument("--forward-only", action="store_true", help="profiling mode: forward passes only")
+    ap.add_argument("--path", default="voxelizer", choices=["voxelizer", "loss"],
+                    help="voxelizer: the G2V fwd+bwd step (default); loss: the feature cosine loss fwd+bwd")
+    ap.add_argument("--loss-channels", type=int, default=0, help="channels of the loss workload (default: config C)")
     ap.add_argument("--single-scene", action="store_true",
                     help="one scene split into x-slabs over the ranks (strong scaling) instead of one scene per rank")
     args = ap.parse_args()
@@ -513,7 +722,8 @@ def main():
             return
         import torch
         dev = torch.device("cuda", local) if torch.cuda.is_available() else None
-        print(json.dumps(run_reference(args, rank, world, dev)), flush=True)
+        run = run_loss_reference if args.path == "loss" else run_reference
+        print(json.dumps(run(args, rank, world, dev)), flush=True)
         return
 
     import torch
@@ -527,7 +737,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     try:
-        line = (run_single_scene if args.single_scene else run_ours)(args, rank, world, dev)
+        run = run_loss if args.path == "loss" else (run_single_scene if args.single_scene else run_ours)
+        line = run(args, rank, world, dev)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -200,6 +200,36 @@ G2V_API int g2v_backward_local(const float* grad_density, const float* grad_grid
                                int tile_x_end, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Feature cosine loss over the voxel grid (the consumer of grid_feats in training).  All arrays are
+ * device, contiguous, row-major over V = X*Y*Z voxels: voxel_label [V] f32, occ_mask [V] bool/u8,
+ * grid_feats and gt_feats [V, channels] f32.  A voxel is valid when occ_mask != 0 and label > 0;
+ * loss_v = 1 - p.g / (sqrt(max(|p|^2, 1e-6)) sqrt(max(|g|^2, 1e-6)) + 1e-6).
+ *
+ * g2v_cosine_loss_forward writes *loss (device f32: the mean of loss_v over valid voxels, 0 when there
+ * are none) and *count (device int32: the number of valid voxels).  Stream-ordered, no synchronisation,
+ * deterministic (fixed summation order).  Replaces CudaFeatsCosinelossForward, src/cuda_feats_loss.cu:146-225
+ * (VoxelCosineLossKernel :45-101 + ReduceLossAndCountKernel :104-143), which returns the count to the
+ * host.  The workspace is a fixed 16 KiB (g2v_cosine_loss_workspace_size).
+ */
+G2V_API int g2v_cosine_loss_workspace_size(int64_t num_voxels, size_t* bytes);
+G2V_API int g2v_cosine_loss_forward(const float* voxel_label, const uint8_t* occ_mask, const float* grid_feats,
+                                    const float* gt_feats, int64_t num_voxels, int64_t channels, float* loss,
+                                    int32_t* count, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Gradient of the cosine loss with respect to grid_feats: grad_grid_feats [V, channels] f32 (every
+ * voxel written; invalid voxels get 0).  grad_loss is the upstream gradient (device f32 scalar); the
+ * valid-voxel count comes from `count` (device int32, e.g. the forward's output) or, when count is
+ * NULL, from count_host.  Stream-ordered, no synchronisation.  Replaces CudaFeatsCosinelossBackward,
+ * src/cuda_feats_loss.cu:311-366 (CosineLossBackwardKernel :228-289), which reads grad_output and the
+ * count on the host.
+ */
+G2V_API int g2v_cosine_loss_backward(const float* grad_loss, const int32_t* count, int32_t count_host,
+                                     const float* voxel_label, const uint8_t* occ_mask, const float* grid_feats,
+                                     const float* gt_feats, int64_t num_voxels, int64_t channels,
+                                     float* grad_grid_feats, void* stream);
+
+/*
  * Debug / parity hook: the Tile->Gaussian CSR built by g2v_forward_splat for the whole grid, copied
  * out of the splat workspace after the call: tile_offsets (num_tiles+1, int32) and t2g_gaussians
  * (M, int32).  No reference counterpart (the reference keeps this map internal, cu:1675-1772).

@@ -242,3 +242,91 @@ def generate_inputs(num_gaussians, feat_dim, voxel_range, num_outside=0, seed=0,
     feats = torch.randn(n, feat_dim, generator=g) if feat_dim is not None else None
     return means.contiguous(), opacity.contiguous(), cov.contiguous(), (
         feats.contiguous() if feats is not None else None)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Feature cosine loss (src/cuda_feats_loss.cu), float64 numpy restatement.
+
+LOSS_EPS = 1e-6  # include/utils.cuh:80 (`eps`), shared by the norm clamps and the denominator
+
+
+def _loss_rows(voxel_label, occ_mask, grid_feats, gt_feats):
+    """(valid mask [V], prediction rows, target rows) -- the rows of the valid voxels only, in float64."""
+    c = np.shape(grid_feats)[-1]
+    label = np.asarray(voxel_label, np.float32).reshape(-1)
+    mask = np.asarray(occ_mask).reshape(-1).astype(bool)
+    valid = mask & (label > 0)  # cuda_feats_loss.cu:70-71 (and :138, :251)
+    pv = np.asarray(grid_feats).reshape(-1, c)[valid].astype(np.float64)
+    gv = np.asarray(gt_feats).reshape(-1, c)[valid].astype(np.float64)
+    return valid, pv, gv
+
+
+def _row_sums(pv, gv):
+    return (np.einsum("ij,ij->i", pv, gv), np.einsum("ij,ij->i", pv, pv), np.einsum("ij,ij->i", gv, gv))
+
+
+def cosine_loss_forward(voxel_label, occ_mask, grid_feats, gt_feats):
+    """(mean loss, valid count) of CudaFeatsCosinelossForward (cuda_feats_loss.cu:146-225).
+
+    Per valid voxel (VoxelCosineLossKernel, :80-99): dot, |p|^2, |g|^2 over the channels, then
+    1 - dot / (sqrt(max(|p|^2, eps)) sqrt(max(|g|^2, eps)) + eps); invalid voxels contribute 0.
+    The sum and the count (ReduceLossAndCountKernel, :104-143) give mean = sum / count, or 0 when
+    count is 0 (:196-198).
+    """
+    valid, pv, gv = _loss_rows(voxel_label, occ_mask, grid_feats, gt_feats)
+    dot, pp, gg = _row_sums(pv, gv)
+    pn = np.sqrt(np.maximum(pp, LOSS_EPS))
+    gn = np.sqrt(np.maximum(gg, LOSS_EPS))
+    loss_v = 1.0 - dot / (pn * gn + LOSS_EPS)
+    count = int(valid.sum())
+    return (float(loss_v.sum()) / count if count > 0 else 0.0), count
+
+
+def cosine_loss_backward(grad_output, num_valid_voxel, voxel_label, occ_mask, grid_feats, gt_feats,
+                         return_terms=False):
+    """d loss / d grid_feats of CudaFeatsCosinelossBackward (cuda_feats_loss.cu:311-366).
+
+    inv_count = 1/count or 0 (:319); per valid voxel (CosineLossBackwardKernel, :262-287) with
+    a = sqrt(max(|p|^2, eps)), b = sqrt(max(|g|^2, eps)), D = a b + eps:
+    grad = grad_out inv_count (-g / D + [|p|^2 > eps] dot b / (a D^2) p); invalid voxels get 0.
+    ``return_terms`` also returns |grad_out inv_count| (|g / D| + |c2 p|) per element: the size of the
+    two terms whose difference is the gradient, the scale of float32 rounding when they cancel.
+    """
+    valid, pv, gv = _loss_rows(voxel_label, occ_mask, grid_feats, gt_feats)
+    inv_count = 1.0 / num_valid_voxel if num_valid_voxel > 0 else 0.0
+    dot, pp, gg = _row_sums(pv, gv)
+    a = np.sqrt(np.maximum(pp, LOSS_EPS))
+    b = np.sqrt(np.maximum(gg, LOSS_EPS))
+    D = a * b + LOSS_EPS
+    c1 = -1.0 / D
+    c2 = np.where(pp > LOSS_EPS, dot * b / (a * D * D), 0.0)
+    scale = float(grad_output) * inv_count
+    grad = np.zeros((valid.size, pv.shape[1]), np.float64)
+    grad[valid] = scale * (c1[:, None] * gv + c2[:, None] * pv)
+    if not return_terms:
+        return grad.reshape(np.shape(grid_feats))
+    terms = np.zeros_like(grad)
+    terms[valid] = abs(scale) * (np.abs(c1[:, None] * gv) + np.abs(c2[:, None] * pv))
+    return grad.reshape(np.shape(grid_feats)), terms.reshape(np.shape(grid_feats))
+
+
+def generate_loss_inputs(dims, channels, case="noise", p_label=0.25, p_mask=0.7, noise=0.1, seed=0):
+    """Seeded inputs shaped like the reference's loss tests (test/test_feats_loss_backward.py:58-64,
+    :151-180): label = (U < p_label) as float, mask = U < p_mask, grid_feats ~ randn(X,Y,Z,C) and a
+    target that is the prediction ("same"), its negation ("neg") or the prediction plus
+    ``noise`` x randn ("noise")."""
+    import torch
+    gen = torch.Generator().manual_seed(seed)
+    X, Y, Z = dims
+    feats = torch.randn(X, Y, Z, channels, generator=gen)
+    label = (torch.rand(X, Y, Z, generator=gen) < p_label).float()
+    mask = torch.rand(X, Y, Z, generator=gen) < p_mask
+    if case == "same":
+        gt = feats.clone()
+    elif case == "neg":
+        gt = -feats
+    elif case == "noise":
+        gt = feats + noise * torch.randn(X, Y, Z, channels, generator=gen)
+    else:
+        raise ValueError(case)
+    return label.contiguous(), mask.contiguous(), feats.contiguous(), gt.contiguous()

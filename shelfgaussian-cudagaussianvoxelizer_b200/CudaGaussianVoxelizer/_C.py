@@ -1,7 +1,8 @@
-"""Drop-in replacement of the reference's ``CudaGaussianVoxelizer._C`` voxelizer functions.
+"""Drop-in replacement of the reference's ``CudaGaussianVoxelizer._C`` functions.
 
 Same names, argument names, argument meaning and return tuples as the reference's pybind module
-(src/bindings.cpp:8-64), implemented over the C ABI of libg2v.so.  Outputs are allocated from the
+(src/bindings.cpp:8-100: the voxelizer forward/backward and the feature cosine loss forward/backward),
+implemented over the C ABI of libg2v.so.  Outputs are allocated from the
 torch caching allocator on ``means3D.device``; the library itself never allocates: every call passes
 it a workspace tensor.  Failures raise ``RuntimeError`` (never exit the process).
 """
@@ -14,7 +15,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["gaussian_voxelizer_forward", "gaussian_voxelizer_backward", "grid_shape", "t2g_maps"]
+__all__ = ["gaussian_voxelizer_forward", "gaussian_voxelizer_backward", "grid_shape", "t2g_maps",
+           "CudaFeatsCosinelossForward", "CudaFeatsCosinelossBackward"]
 
 # id(tensor) -> (weakref to the tensor, its _version, host values).  The weak reference makes sure a
 # hit is the same live tensor object (an address or id can be reused after a tensor is freed).
@@ -268,3 +270,109 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
             ev1.synchronize()
             sec = ev0.elapsed_time(ev1) / 1000.0
     return grad_means, grad_cov, grad_op, grad_feats, sec
+
+
+def _loss_inputs(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt):
+    """Checks of the reference (cuda_feats_loss.cu:150-153: dtype, contiguous, CUDA) plus the shape
+    agreement the reference assumes: label and mask (X,Y,Z), features and targets (X,Y,Z,C)."""
+    dev = d_grid_feats.device if isinstance(d_grid_feats, torch.Tensor) else None
+    _need_contig(voxel_label, "voxel_label", torch.float32, dev)
+    if not isinstance(occ_gt_mask_camera, torch.Tensor) or occ_gt_mask_camera.dtype not in (torch.bool, torch.uint8):
+        raise RuntimeError("occ_gt_mask_camera must be a bool tensor")
+    _need_contig(occ_gt_mask_camera, "occ_gt_mask_camera", occ_gt_mask_camera.dtype, dev)
+    _need_contig(d_grid_feats, "d_grid_feats", torch.float32, dev)
+    _need_contig(pseudo_dino_gt, "pseudo_dino_gt", torch.float32, dev)
+    if d_grid_feats.dim() != 4:
+        raise RuntimeError(f"d_grid_feats must be (X,Y,Z,C), got {tuple(d_grid_feats.shape)}")
+    dims = tuple(d_grid_feats.shape[:3])
+    if tuple(pseudo_dino_gt.shape) != tuple(d_grid_feats.shape):
+        raise RuntimeError(f"pseudo_dino_gt {tuple(pseudo_dino_gt.shape)} must match d_grid_feats "
+                           f"{tuple(d_grid_feats.shape)}")
+    if tuple(voxel_label.shape) != dims or tuple(occ_gt_mask_camera.shape) != dims:
+        raise RuntimeError(f"voxel_label {tuple(voxel_label.shape)} and occ_gt_mask_camera "
+                           f"{tuple(occ_gt_mask_camera.shape)} must be {dims}")
+    return dev, dims[0] * dims[1] * dims[2], int(d_grid_feats.shape[3])
+
+
+def _cosine_loss_forward_impl(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt, timing):
+    """(loss 0-dim f32, count (1,) int32, sec) on the device; no synchronisation unless ``timing``."""
+    lib = _lib.load()
+    dev, nv, c = _loss_inputs(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        sptr = ctypes.c_void_p(stream.cuda_stream)
+        nbytes = ctypes.c_size_t()
+        _lib.check(lib.g2v_cosine_loss_workspace_size(nv, ctypes.byref(nbytes)), "g2v_cosine_loss_workspace_size")
+        ws = _workspace(nbytes.value, dev)
+        loss = torch.empty((), dtype=torch.float32, device=dev)
+        count = torch.empty((1,), dtype=torch.int32, device=dev)
+        if timing:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+        _lib.check(lib.g2v_cosine_loss_forward(_ptr(voxel_label), _ptr(occ_gt_mask_camera), _ptr(d_grid_feats),
+                                               _ptr(pseudo_dino_gt), nv, c, _ptr(loss), _ptr(count), _ptr(ws),
+                                               ws.numel(), sptr), "g2v_cosine_loss_forward")
+        sec = 0.0
+        if timing:
+            ev1.record(stream)
+            ev1.synchronize()
+            sec = ev0.elapsed_time(ev1) / 1000.0
+    return loss, count, sec
+
+
+def CudaFeatsCosinelossForward(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt, *,
+                               timing: bool = True):
+    """Mean cosine loss over the valid voxels (reference src/bindings.cpp:67-80, cuda_feats_loss.cu:146-225).
+
+    A voxel is valid when ``occ_gt_mask_camera`` and ``voxel_label > 0``.  Returns ``(loss (0-dim f32
+    CUDA tensor), num_valid_voxel (int), fwd_sec)``; the int needs one synchronisation, as in the
+    reference.  ``fwd_sec`` is the device time (CUDA events; 0.0 with ``timing=False``).
+    """
+    loss, count, sec = _cosine_loss_forward_impl(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt,
+                                                 timing)
+    return loss, int(count.item()), sec
+
+
+def CudaFeatsCosinelossBackward(grad_output, voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt,
+                                num_valid_voxel, *, timing: bool = True):
+    """Gradient of the loss with respect to ``d_grid_feats`` (reference src/bindings.cpp:82-100,
+    cuda_feats_loss.cu:311-366).  Returns ``(grad_p (X,Y,Z,C), bwd_sec)``; invalid voxels get 0.
+
+    ``grad_output`` is the upstream gradient (one element; read on the device, no synchronisation when
+    it is a CUDA tensor).  ``num_valid_voxel`` is the forward's count: an int as in the reference, or a
+    one-element int32 CUDA tensor (the count left on the device by the autograd path).
+    """
+    lib = _lib.load()
+    dev, nv, c = _loss_inputs(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt)
+    if isinstance(grad_output, torch.Tensor):
+        if grad_output.numel() != 1:
+            raise RuntimeError(f"grad_output must have one element, got {grad_output.numel()}")
+        gout = grad_output.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    else:
+        gout = torch.full((1,), float(grad_output), dtype=torch.float32, device=dev)
+    count_dev, count_host = None, 0
+    if isinstance(num_valid_voxel, torch.Tensor):
+        if num_valid_voxel.numel() != 1:
+            raise RuntimeError("num_valid_voxel must have one element")
+        count_dev = num_valid_voxel.detach().to(device=dev, dtype=torch.int32).reshape(1).contiguous()
+    else:
+        count_host = int(num_valid_voxel)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        sptr = ctypes.c_void_p(stream.cuda_stream)
+        grad_p = torch.empty_like(d_grid_feats)
+        if timing:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+        _lib.check(lib.g2v_cosine_loss_backward(_ptr(gout), _ptr(count_dev) if count_dev is not None else None,
+                                                count_host, _ptr(voxel_label), _ptr(occ_gt_mask_camera),
+                                                _ptr(d_grid_feats), _ptr(pseudo_dino_gt), nv, c, _ptr(grad_p), sptr),
+                   "g2v_cosine_loss_backward")
+        sec = 0.0
+        if timing:
+            ev1.record(stream)
+            ev1.synchronize()
+            sec = ev0.elapsed_time(ev1) / 1000.0
+    return grad_p, sec

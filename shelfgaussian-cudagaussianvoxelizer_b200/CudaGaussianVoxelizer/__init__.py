@@ -1,11 +1,12 @@
 """B200 Gaussian-to-voxel splatting, drop-in for the reference ``CudaGaussianVoxelizer`` package.
 
-    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer
+    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer, PyCudaFeatsCosineLoss
     voxelizer = PyCudaGaussianVoxelizer(voxel_size=[0.4] * 3, voxel_range=[-40, -40, -1, 40, 40, 5.4])
     density, grid_feats, stats = voxelizer(means3D, opacity, covariances, features)
+    loss, loss_stats = PyCudaFeatsCosineLoss()(voxel_label, occ_mask, grid_feats, target_feats)
 
-Same module, autograd function, argument meaning, outputs and ``stats`` semantics as the reference's
-``CudaGaussianVoxelizer/__init__.py:10-47, 69-82``; the compute runs in libg2v.so (hand-written sm_100a
+Same modules, autograd functions, argument meaning, outputs and ``stats`` semantics as the reference's
+``CudaGaussianVoxelizer/__init__.py:10-95``; the compute runs in libg2v.so (hand-written sm_100a
 kernels behind a C ABI, include/g2v.h).
 """
 from __future__ import annotations
@@ -14,12 +15,14 @@ import torch
 import torch.nn as nn
 
 from . import _C, _lib
-from ._C import _forward_impl, gaussian_voxelizer_backward, gaussian_voxelizer_forward
+from ._C import (CudaFeatsCosinelossBackward, CudaFeatsCosinelossForward, _cosine_loss_forward_impl, _forward_impl,
+                 gaussian_voxelizer_backward, gaussian_voxelizer_forward)
 
 _lib.load()  # fail loudly at import when the native library is missing
 
 __all__ = ["PyCudaGaussianVoxelizer", "_CudaGaussianVoxelizeFunction", "gaussian_voxelizer_forward",
-           "gaussian_voxelizer_backward", "_C"]
+           "gaussian_voxelizer_backward", "PyCudaFeatsCosineLoss", "_CudaFeatsCosinelossFunction",
+           "CudaFeatsCosinelossForward", "CudaFeatsCosinelossBackward", "_C"]
 
 
 class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
@@ -78,3 +81,52 @@ class PyCudaGaussianVoxelizer(nn.Module):
     def forward(self, means3D, opacity, covariances, features=None):
         return _CudaGaussianVoxelizeFunction.apply(means3D, opacity, covariances, self.voxel_size, self.voxel_range,
                                                    features, self.timing)
+
+
+class _CudaFeatsCosinelossFunction(torch.autograd.Function):
+    """Autograd function of the feature cosine loss (reference CudaGaussianVoxelizer/__init__.py:49-70).
+
+    Unlike the reference, the valid-voxel count stays on the device between forward and backward and
+    the upstream gradient is read on the device, so with ``timing=False`` neither pass synchronises.
+    """
+
+    @staticmethod
+    def forward(ctx, voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt, timing=True):
+        loss, count, fwd_sec = _cosine_loss_forward_impl(voxel_label, occ_gt_mask_camera, d_grid_feats,
+                                                         pseudo_dino_gt, timing)
+        stats = torch.zeros(2, dtype=torch.float32, device="cpu")
+        stats[0] = fwd_sec
+        ctx.save_for_backward(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt, count, stats)
+        ctx.timing = timing
+        ctx.mark_non_differentiable(stats)
+        return loss, stats
+
+    @staticmethod
+    def backward(ctx, grad_output, grad_stats):
+        voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt, count, stats = ctx.saved_tensors
+        grad_p, bwd_sec = CudaFeatsCosinelossBackward(grad_output, voxel_label, occ_gt_mask_camera, d_grid_feats,
+                                                      pseudo_dino_gt, count, timing=ctx.timing)
+        stats[1] = bwd_sec
+        return None, None, grad_p, None, None
+
+
+class PyCudaFeatsCosineLoss(nn.Module):
+    """Mean cosine distance between voxel features and target features over the valid voxels.
+
+    forward(voxel_label (X,Y,Z) f32, occ_gt_mask_camera (X,Y,Z) bool, d_grid_feats (X,Y,Z,C) f32,
+            pseudo_dino_gt (X,Y,Z,C) f32) -> (loss (0-dim), stats (2,) CPU float32)
+    A voxel is valid when the mask is set and its label is > 0; the loss is 0 when none is.  ``stats``
+    holds the forward and backward device seconds, as for the voxelizer (``timing=False`` leaves them
+    0 and skips the synchronisations).  ``voxel_size`` / ``voxel_range`` are kept for signature parity;
+    the loss does not use them.  Reference: CudaGaussianVoxelizer/__init__.py:84-95.
+    """
+
+    def __init__(self, voxel_size=[0.4, 0.4, 0.4], voxel_range=[-40, -40, -1, 40, 40, 5.4], timing: bool = True):
+        super().__init__()
+        self.voxel_size = torch.tensor(voxel_size, dtype=torch.float32, device="cuda")
+        self.voxel_range = torch.tensor(voxel_range, dtype=torch.float32, device="cuda")
+        self.timing = timing
+
+    def forward(self, voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt):
+        return _CudaFeatsCosinelossFunction.apply(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt,
+                                                  self.timing)

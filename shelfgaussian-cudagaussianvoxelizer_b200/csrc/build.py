@@ -36,6 +36,7 @@ SOURCES = {
     "g2v_grad_tc.cu": [],
     "g2v_spass_tc.cu": [],
     "g2v_selftest.cu": [],
+    "g2v_loss.cu": [],
 }
 HEADERS_TC = ["g2v_tc.cuh"]
 HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(HERE, "g2v_tc.cuh"), os.path.join(INCLUDE, "g2v.h")]

@@ -68,6 +68,12 @@ int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const in
 int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const int32_t* lb, const int32_t* ub,
                         int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
                         cudaStream_t s);
+size_t cosine_loss_workspace_bytes();
+int launch_cosine_loss_fwd(const float* label, const uint8_t* mask, const float* p, const float* g, int64_t V, int C,
+                           float* loss, int* count, void* ws, cudaStream_t s);
+int launch_cosine_loss_bwd(const float* grad_out, const int* count_dev, int count_host, const float* label,
+                           const uint8_t* mask, const float* p, const float* g, int64_t V, int C, float* gp,
+                           cudaStream_t s);
 
 // Device error word: kernels with bounded waits set bits here when a wait gives up.  It is read (and
 // cleared) at the synchronisation points the API already has (g2v_forward_prepare, g2v_backward_plan)
@@ -751,6 +757,46 @@ int g2v_backward_local(const float* grad_density, const float* grad_grid_feats, 
                          num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_covariances,
                          grad_opacity, grad_features, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream,
                          true);
+}
+
+int g2v_cosine_loss_workspace_size(int64_t num_voxels, size_t* bytes) {
+    if (!bytes || num_voxels < 0) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    *bytes = cosine_loss_workspace_bytes();
+    return G2V_SUCCESS;
+}
+
+int g2v_cosine_loss_forward(const float* voxel_label, const uint8_t* occ_mask, const float* grid_feats,
+                            const float* gt_feats, int64_t num_voxels, int64_t channels, float* loss, int32_t* count,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    g_msg[0] = 0;
+    if (num_voxels < 0 || channels < 0 || channels > INT32_MAX || num_voxels > INT32_MAX || !loss || !count ||
+        (num_voxels > 0 && (!voxel_label || !occ_mask)) ||
+        (num_voxels > 0 && channels > 0 && (!grid_feats || !gt_feats))) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    int rc = need_ws(cosine_loss_workspace_bytes(), workspace_bytes, workspace);
+    if (rc) return rc;
+    return launch_cosine_loss_fwd(voxel_label, occ_mask, grid_feats, gt_feats, num_voxels, (int)channels, loss,
+                                  reinterpret_cast<int*>(count), workspace, static_cast<cudaStream_t>(stream));
+}
+
+int g2v_cosine_loss_backward(const float* grad_loss, const int32_t* count, int32_t count_host,
+                             const float* voxel_label, const uint8_t* occ_mask, const float* grid_feats,
+                             const float* gt_feats, int64_t num_voxels, int64_t channels, float* grad_grid_feats,
+                             void* stream) {
+    g_msg[0] = 0;
+    if (num_voxels < 0 || channels < 0 || channels > INT32_MAX || num_voxels > INT32_MAX || !grad_loss ||
+        (num_voxels > 0 && channels > 0 && (!voxel_label || !occ_mask || !grid_feats || !gt_feats || !grad_grid_feats))) {
+        set_error("invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return launch_cosine_loss_bwd(grad_loss, reinterpret_cast<const int*>(count), count_host, voxel_label, occ_mask,
+                                  grid_feats, gt_feats, num_voxels, (int)channels, grad_grid_feats,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -8,21 +8,15 @@ oracle/build_ref.py compiles the reference's src/cuda_gaussian_voxelizer.cu with
   * density, grid_feats and all gradients agree within the parity tolerance.
 Skipped when oracle/_ref has no build (it is produced in the build container and travels with the repo).
 """
-import os
-import sys
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import REPO
 from gpu_util import assert_close, dev
-from oracle import oracle
+from oracle import build_ref, oracle
 
 pytestmark = pytest.mark.gpu
-
-sys.path.insert(0, os.path.join(REPO, "oracle"))
-import build_ref  # noqa: E402
 
 REF = build_ref.load()
 needs_ref = pytest.mark.skipif(REF is None, reason="oracle/_ref has no reference build")
