@@ -603,6 +603,20 @@ def run_loss(args, rank, world, dev):
 
     e2e_ms = timed(e2e_step)
 
+    # the drop-in _C calls timed exactly like the reference build's (reference_loss_cuda): wall clock of
+    # forward (count returned to the host, as the reference's signature requires) + backward, synchronised
+    pd = p.detach()
+    one = torch.ones((), device=dev)
+    walls = []
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        _, count, _ = _C.CudaFeatsCosinelossForward(label, mask, pd, g, timing=False)
+        _C.CudaFeatsCosinelossBackward(one, label, mask, pd, g, count, timing=False)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            walls.append((time.perf_counter() - t0) * 1e3)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = loss_cpu_baseline(X, Y, Z, C)
@@ -616,6 +630,9 @@ def run_loss(args, rank, world, dev):
                    "parallelism": f"dp{world} (independent grids)"},
         "roofline": roofline, "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "dropin_wall": {"value": round(statistics.median(walls), 4), "unit": "ms",
+                        "what": "_C.CudaFeatsCosinelossForward + Backward, wall clock with host synchronisation, "
+                                "timed like the reference build's arm"},
         "gpu_launches": int(sum(v[1] for v in prof.values())),
         "clocks": clocks,
     }

@@ -256,8 +256,8 @@ def _loss_rows(voxel_label, occ_mask, grid_feats, gt_feats):
     label = np.asarray(voxel_label, np.float32).reshape(-1)
     mask = np.asarray(occ_mask).reshape(-1).astype(bool)
     valid = mask & (label > 0)  # cuda_feats_loss.cu:70-71 (and :138, :251)
-    pv = np.asarray(grid_feats).reshape(-1, c)[valid].astype(np.float64)
-    gv = np.asarray(gt_feats).reshape(-1, c)[valid].astype(np.float64)
+    pv = np.asarray(grid_feats).reshape(label.size, c)[valid].astype(np.float64)
+    gv = np.asarray(gt_feats).reshape(label.size, c)[valid].astype(np.float64)
     return valid, pv, gv
 
 

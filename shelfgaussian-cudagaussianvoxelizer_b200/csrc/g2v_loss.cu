@@ -64,50 +64,126 @@ __device__ __forceinline__ void group_sum3(float& d, float& a, float& b, int G) 
     }
 }
 
+// Valid flag of voxel v; both loads are issued unconditionally (no dependent branch between them).
 __device__ __forceinline__ bool voxel_valid(const float* label, const uint8_t* mask, int64_t v, int64_t V) {
-    return v < V && mask[v] != 0 && label[v] > 0.f;
+    if (v >= V) return false;
+    const uint8_t m = __ldg(mask + v);
+    const float l = __ldg(label + v);
+    return m != 0 && l > 0.f;
 }
 
-// Forward: per-CTA partial (sum of loss_v, count) of the voxels the CTA visits.
-// gl2 = log2(G); n = row length in elements of Row<kVec>::E.
-template <bool kVec>
+// Per-warp list of a window's voxels (offsets 0..31): the valid ones in order, then the other in-range
+// ones.  Returns the number of valid voxels; *ninv receives the number of the others.
+__device__ __forceinline__ int window_list(int* list, bool valid, bool inrange, int lane, int* ninv) {
+    const unsigned bal = __ballot_sync(0xffffffffu, valid);
+    const unsigned inr = __ballot_sync(0xffffffffu, inrange);
+    const unsigned below = (1u << lane) - 1u;
+    const int nv = __popc(bal);
+    __syncwarp();  // the previous window's list has been read
+    if (valid) list[__popc(bal & below)] = lane;
+    else if (inrange) list[nv + __popc(inr & ~bal & below)] = lane;
+    __syncwarp();
+    *ninv = __popc(inr & ~bal);
+    return nv;
+}
+
+// Row slot of a lane: the voxel window of a warp is 32 consecutive voxels; the valid ones are dealt to
+// the warp's S = 32 / G lane groups in order, S per round.  kK > 0: a lane holds kK
+// elements of the row (element l + k G), all loads of a round issued before the sums; kK == 0: any
+// row length, a strided loop.
+template <bool kVec, int kK>
+struct RowIO {
+    using R = Row<kVec>;
+    using E = typename R::E;
+    static constexpr int kRegs = kK > 0 ? kK : 1;
+    E x[kRegs], y[kRegs];
+
+    __device__ __forceinline__ void sums(const E* pr, const E* gr, bool act, int l, int G, int n, float& d, float& a,
+                                         float& b) {
+        d = a = b = 0.f;
+        if (kK > 0) {
+#pragma unroll
+            for (int k = 0; k < kRegs; ++k) {
+                const int c = l + k * G;
+                const bool in = act && c < n;
+                x[k] = in ? __ldg(pr + c) : R::zero();
+                y[k] = in ? __ldg(gr + c) : R::zero();
+            }
+#pragma unroll
+            for (int k = 0; k < kRegs; ++k) R::acc(x[k], y[k], d, a, b);
+        } else if (act) {
+#pragma unroll 4
+            for (int c = l; c < n; c += G) R::acc(__ldg(pr + c), __ldg(gr + c), d, a, b);
+        }
+    }
+
+    __device__ __forceinline__ void write_grad(E* out, const E* pr, const E* gr, int l, int G, int n, float c1,
+                                               float c2) {
+        if (kK > 0) {
+#pragma unroll
+            for (int k = 0; k < kRegs; ++k) {
+                const int c = l + k * G;
+                if (c < n) out[c] = R::grad(c1, y[k], c2, x[k]);
+            }
+        } else {
+            for (int c = l; c < n; c += G) out[c] = R::grad(c1, __ldg(gr + c), c2, __ldg(pr + c));
+        }
+    }
+
+    static __device__ __forceinline__ void write_zero(E* out, int l, int G, int n) {
+        if (kK > 0) {
+#pragma unroll
+            for (int k = 0; k < kRegs; ++k) {
+                const int c = l + k * G;
+                if (c < n) out[c] = R::zero();
+            }
+        } else {
+            for (int c = l; c < n; c += G) out[c] = R::zero();
+        }
+    }
+};
+
+// Forward: per-CTA partial (sum of loss_v, count) of the voxel windows the CTA's warps visit.
+template <bool kVec, int kK>
 __global__ void __launch_bounds__(kLossThreads) cosine_loss_fwd_kernel(
     const float* __restrict__ label, const uint8_t* __restrict__ mask, const float* __restrict__ p,
     const float* __restrict__ g, int64_t V, int n, int gl2, float* __restrict__ part_loss,
     int* __restrict__ part_count) {
-    using R = Row<kVec>;
-    using E = typename R::E;
+    using E = typename Row<kVec>::E;
     __shared__ float sl[kLossWarps];
     __shared__ int sc[kLossWarps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = 1 << gl2, l = lane & (G - 1), per_warp = 32 >> gl2;
+    const int G = 1 << gl2, l = lane & (G - 1), sub = lane >> gl2, S = 32 >> gl2;
     const E* P = reinterpret_cast<const E*>(p);
     const E* Q = reinterpret_cast<const E*>(g);
+    const int64_t step = (int64_t)gridDim.x * kLossWarps * 32;
+    __shared__ int lists[kLossWarps][32];
+    int* list = lists[warp];
     float lsum = 0.f;
     int cnt = 0;
-    const int64_t stride = (int64_t)gridDim.x * kLossWarps * per_warp;
-    for (int64_t base = ((int64_t)blockIdx.x * kLossWarps + warp) * per_warp; base < V; base += stride) {
-        const int64_t v = base + (lane >> gl2);
-        const bool valid = voxel_valid(label, mask, v, V);
-        float d = 0.f, a = 0.f, b = 0.f;
-        if (valid) {
-            const E* pr = P + v * n;
-            const E* gr = Q + v * n;
-#pragma unroll 4
-            for (int c = l; c < n; c += G) R::acc(__ldg(pr + c), __ldg(gr + c), d, a, b);
-        }
-        group_sum3(d, a, b, G);
-        if (valid && l == 0) {
-            const float pn = sqrtf(fmaxf(a, kEps)), gn = sqrtf(fmaxf(b, kEps));
-            lsum += 1.f - d / (pn * gn + kEps);
-            ++cnt;
+    int64_t win = ((int64_t)blockIdx.x * kLossWarps + warp) * 32;
+    bool flag = voxel_valid(label, mask, win + lane, V);
+    RowIO<kVec, kK> io;
+    for (; win < V; win += step) {
+        int ninv;
+        const int nv = window_list(list, flag, win + lane < V, lane, &ninv);
+        flag = voxel_valid(label, mask, win + step + lane, V);  // next window, in flight meanwhile
+        cnt += nv;
+        for (int j = 0; j < nv; j += S) {
+            const int slot = j + sub;
+            const bool act = slot < nv;
+            const int64_t v = win + (act ? list[slot] : 0);
+            float d, a, b;
+            io.sums(P + v * n, Q + v * n, act, l, G, n, d, a, b);
+            group_sum3(d, a, b, G);
+            if (act && l == 0) {
+                const float pn = sqrtf(fmaxf(a, kEps)), gn = sqrtf(fmaxf(b, kEps));
+                lsum += 1.f - d / (pn * gn + kEps);
+            }
         }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-        cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-    }
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
     if (lane == 0) {
         sl[warp] = lsum;
         sc[warp] = cnt;
@@ -155,64 +231,50 @@ __global__ void __launch_bounds__(kLossThreads) cosine_loss_final_kernel(const f
     }
 }
 
-// Backward.  kK > 0: the row stays in registers (kK elements per lane, n <= kK * G); kK == 0: any n,
-// the row is read a second time for the gradient.
+// Backward: valid voxels of a window get the gradient (rows read once, kept in registers when kK > 0),
+// the other in-range voxels get zero rows (no reads).
 template <bool kVec, int kK>
 __global__ void __launch_bounds__(kLossThreads) cosine_loss_bwd_kernel(
     const float* __restrict__ grad_out, const int* __restrict__ count_dev, int count_host,
     const float* __restrict__ label, const uint8_t* __restrict__ mask, const float* __restrict__ p,
     const float* __restrict__ g, int64_t V, int n, int gl2, float* __restrict__ gp) {
-    using R = Row<kVec>;
-    using E = typename R::E;
+    using E = typename Row<kVec>::E;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = 1 << gl2, l = lane & (G - 1), per_warp = 32 >> gl2;
+    const int G = 1 << gl2, l = lane & (G - 1), sub = lane >> gl2, S = 32 >> gl2;
     const int cnt = count_dev ? *count_dev : count_host;
     const float inv_count = cnt > 0 ? 1.0f / (float)cnt : 0.0f;
     const float scale = *grad_out * inv_count;
     const E* P = reinterpret_cast<const E*>(p);
     const E* Q = reinterpret_cast<const E*>(g);
     E* O = reinterpret_cast<E*>(gp);
-    const int64_t stride = (int64_t)gridDim.x * kLossWarps * per_warp;
-    for (int64_t base = ((int64_t)blockIdx.x * kLossWarps + warp) * per_warp; base < V; base += stride) {
-        const int64_t v = base + (lane >> gl2);
-        const bool valid = voxel_valid(label, mask, v, V);
-        const E* pr = P + v * n;
-        const E* gr = Q + v * n;
-        E xs[kK > 0 ? kK : 1], ys[kK > 0 ? kK : 1];
-        float d = 0.f, a = 0.f, b = 0.f;
-        if (kK > 0) {
-#pragma unroll
-            for (int k = 0; k < (kK > 0 ? kK : 1); ++k) {
-                const int c = l + k * G;
-                const bool in = valid && c < n;
-                xs[k] = in ? __ldg(pr + c) : R::zero();
-                ys[k] = in ? __ldg(gr + c) : R::zero();
-                R::acc(xs[k], ys[k], d, a, b);
+    const int64_t step = (int64_t)gridDim.x * kLossWarps * 32;
+    __shared__ int lists[kLossWarps][32];
+    int* list = lists[warp];
+    int64_t win = ((int64_t)blockIdx.x * kLossWarps + warp) * 32;
+    bool flag = voxel_valid(label, mask, win + lane, V);
+    RowIO<kVec, kK> io;
+    for (; win < V; win += step) {
+        int ni;
+        const int nv = window_list(list, flag, win + lane < V, lane, &ni);
+        flag = voxel_valid(label, mask, win + step + lane, V);  // next window, in flight meanwhile
+        for (int j = 0; j < nv; j += S) {
+            const int slot = j + sub;
+            const bool act = slot < nv;
+            const int64_t v = win + (act ? list[slot] : 0);
+            const E* pr = P + v * n;
+            const E* gr = Q + v * n;
+            float d, a, b;
+            io.sums(pr, gr, act, l, G, n, d, a, b);
+            group_sum3(d, a, b, G);
+            if (act) {
+                const float ra = sqrtf(fmaxf(a, kEps)), rb = sqrtf(fmaxf(b, kEps));
+                const float D = ra * rb + kEps;
+                const float c1 = (-1.0f / D) * scale;                               // multiplies g
+                const float c2 = (a > kEps ? (d * rb) / (ra * D * D) : 0.0f) * scale;  // multiplies p
+                io.write_grad(O + v * n, pr, gr, l, G, n, c1, c2);
             }
-        } else if (valid) {
-#pragma unroll 4
-            for (int c = l; c < n; c += G) R::acc(__ldg(pr + c), __ldg(gr + c), d, a, b);
         }
-        group_sum3(d, a, b, G);
-        if (v >= V) continue;
-        E* out = O + v * n;
-        if (!valid) {
-            for (int c = l; c < n; c += G) out[c] = R::zero();
-            continue;
-        }
-        const float ra = sqrtf(fmaxf(a, kEps)), rb = sqrtf(fmaxf(b, kEps));
-        const float D = ra * rb + kEps;
-        const float c1 = (-1.0f / D) * scale;                               // multiplies g
-        const float c2 = (a > kEps ? (d * rb) / (ra * D * D) : 0.0f) * scale;  // multiplies p
-        if (kK > 0) {
-#pragma unroll
-            for (int k = 0; k < (kK > 0 ? kK : 1); ++k) {
-                const int c = l + k * G;
-                if (c < n) out[c] = R::grad(c1, ys[k], c2, xs[k]);
-            }
-        } else {
-            for (int c = l; c < n; c += G) out[c] = R::grad(c1, __ldg(gr + c), c2, __ldg(pr + c));
-        }
+        for (int j = sub; j < ni; j += S) RowIO<kVec, kK>::write_zero(O + (win + list[nv + j]) * n, l, G, n);
     }
 }
 
@@ -227,38 +289,83 @@ struct RowShape {
     bool vec;
     int n;    // row length in elements (float4 when vec)
     int gl2;  // log2 of the lanes per voxel
-    int grid;
+    int kk;   // elements per lane held in registers (1, 2, 4, 8) or 0 (strided loop)
 };
 
-RowShape row_shape(int64_t V, int C, const void* a, const void* b, const void* c) {
+// G = the power of two near n / 4 (at most 32), so that a lane holds about 4 elements of a row.
+RowShape row_shape(int C, const void* a, const void* b, const void* c) {
     auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     RowShape r;
     r.vec = C % 4 == 0 && al(a) && al(b) && al(c);
     r.n = r.vec ? C / 4 : C;
+    const int want = (r.n + 3) / 4;
     r.gl2 = 0;
-    while (r.gl2 < 5 && (1 << r.gl2) < r.n) ++r.gl2;
-    const int64_t per_cta = (int64_t)kLossWarps * (32 >> r.gl2);
-    const int64_t need = (V + per_cta - 1) / per_cta;
-    r.grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, std::min(sm_count() * 8, kMaxLossParts)));
+    while (r.gl2 < 5 && (1 << r.gl2) < want) ++r.gl2;
+    const int need = (r.n + (1 << r.gl2) - 1) >> r.gl2;
+    r.kk = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 0;
     return r;
 }
 
+// Enough CTAs to cover the windows, at most one resident wave (occupancy of this instance), capped.
+template <typename K>
+int loss_grid(K kernel, int64_t V) {
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLossThreads, 0) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    const int64_t need = (V + kLossWarps * 32 - 1) / (kLossWarps * 32);
+    return (int)std::max<int64_t>(1, std::min<int64_t>(need, std::min(sm_count() * per_sm, kMaxLossParts)));
+}
+
+template <bool kVec, int kK>
+int fwd_k(const float* label, const uint8_t* mask, const float* p, const float* g, int64_t V, const RowShape& r,
+          float* loss, int* count, void* ws, cudaStream_t s) {
+    float* part_loss = static_cast<float*>(ws);
+    int* part_count = reinterpret_cast<int*>(part_loss + kMaxLossParts);
+    const int grid = loss_grid(cosine_loss_fwd_kernel<kVec, kK>, V);
+    G2V_TIMED("cosine_loss_fwd_kernel", s,
+              (cosine_loss_fwd_kernel<kVec, kK><<<grid, kLossThreads, 0, s>>>(label, mask, p, g, V, r.n, r.gl2,
+                                                                              part_loss, part_count)));
+    G2V_LAUNCH_CHECK("cosine_loss_fwd_kernel");
+    G2V_TIMED("cosine_loss_final_kernel", s,
+              (cosine_loss_final_kernel<<<1, kLossThreads, 0, s>>>(part_loss, part_count, grid, loss, count)));
+    G2V_LAUNCH_CHECK("cosine_loss_final_kernel");
+    return 0;
+}
+
+template <bool kVec, int kK>
+int bwd_k(const float* grad_out, const int* count_dev, int count_host, const float* label, const uint8_t* mask,
+          const float* p, const float* g, int64_t V, const RowShape& r, float* gp, cudaStream_t s) {
+    const int grid = loss_grid(cosine_loss_bwd_kernel<kVec, kK>, V);
+    G2V_TIMED("cosine_loss_bwd_kernel", s,
+              (cosine_loss_bwd_kernel<kVec, kK><<<grid, kLossThreads, 0, s>>>(grad_out, count_dev, count_host, label,
+                                                                              mask, p, g, V, r.n, r.gl2, gp)));
+    G2V_LAUNCH_CHECK("cosine_loss_bwd_kernel");
+    return 0;
+}
+
 template <bool kVec>
-void launch_bwd_k(int kk, int grid, const float* grad_out, const int* count_dev, int count_host, const float* label,
-                  const uint8_t* mask, const float* p, const float* g, int64_t V, int n, int gl2, float* gp,
-                  cudaStream_t s) {
-#define G2V_LOSS_BWD(K)                                                                                          \
-    G2V_TIMED("cosine_loss_bwd_kernel", s,                                                                      \
-              (cosine_loss_bwd_kernel<kVec, K><<<grid, kLossThreads, 0, s>>>(grad_out, count_dev, count_host,   \
-                                                                             label, mask, p, g, V, n, gl2, gp)))
-    switch (kk) {
-        case 1: G2V_LOSS_BWD(1); break;
-        case 2: G2V_LOSS_BWD(2); break;
-        case 4: G2V_LOSS_BWD(4); break;
-        case 8: G2V_LOSS_BWD(8); break;
-        default: G2V_LOSS_BWD(0); break;
+int fwd_dispatch(const float* label, const uint8_t* mask, const float* p, const float* g, int64_t V,
+                 const RowShape& r, float* loss, int* count, void* ws, cudaStream_t s) {
+    switch (r.kk) {
+        case 1: return fwd_k<kVec, 1>(label, mask, p, g, V, r, loss, count, ws, s);
+        case 2: return fwd_k<kVec, 2>(label, mask, p, g, V, r, loss, count, ws, s);
+        case 4: return fwd_k<kVec, 4>(label, mask, p, g, V, r, loss, count, ws, s);
+        case 8: return fwd_k<kVec, 8>(label, mask, p, g, V, r, loss, count, ws, s);
+        default: return fwd_k<kVec, 0>(label, mask, p, g, V, r, loss, count, ws, s);
     }
-#undef G2V_LOSS_BWD
+}
+
+template <bool kVec>
+int bwd_dispatch(const float* grad_out, const int* count_dev, int count_host, const float* label,
+                 const uint8_t* mask, const float* p, const float* g, int64_t V, const RowShape& r, float* gp,
+                 cudaStream_t s) {
+    switch (r.kk) {
+        case 1: return bwd_k<kVec, 1>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s);
+        case 2: return bwd_k<kVec, 2>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s);
+        case 4: return bwd_k<kVec, 4>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s);
+        case 8: return bwd_k<kVec, 8>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s);
+        default: return bwd_k<kVec, 0>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s);
+    }
 }
 }  // namespace
 
@@ -266,38 +373,18 @@ size_t cosine_loss_workspace_bytes() { return (size_t)kMaxLossParts * (sizeof(fl
 
 int launch_cosine_loss_fwd(const float* label, const uint8_t* mask, const float* p, const float* g, int64_t V, int C,
                            float* loss, int* count, void* ws, cudaStream_t s) {
-    const RowShape r = row_shape(V, C, p, g, nullptr);
-    float* part_loss = static_cast<float*>(ws);
-    int* part_count = reinterpret_cast<int*>(part_loss + kMaxLossParts);
-    if (r.vec)
-        G2V_TIMED("cosine_loss_fwd_kernel", s,
-                  (cosine_loss_fwd_kernel<true><<<r.grid, kLossThreads, 0, s>>>(label, mask, p, g, V, r.n, r.gl2,
-                                                                                 part_loss, part_count)));
-    else
-        G2V_TIMED("cosine_loss_fwd_kernel", s,
-                  (cosine_loss_fwd_kernel<false><<<r.grid, kLossThreads, 0, s>>>(label, mask, p, g, V, r.n, r.gl2,
-                                                                                  part_loss, part_count)));
-    G2V_LAUNCH_CHECK("cosine_loss_fwd_kernel");
-    G2V_TIMED("cosine_loss_final_kernel", s,
-              (cosine_loss_final_kernel<<<1, kLossThreads, 0, s>>>(part_loss, part_count, r.grid, loss, count)));
-    G2V_LAUNCH_CHECK("cosine_loss_final_kernel");
-    return 0;
+    const RowShape r = row_shape(C, p, g, nullptr);
+    return r.vec ? fwd_dispatch<true>(label, mask, p, g, V, r, loss, count, ws, s)
+                 : fwd_dispatch<false>(label, mask, p, g, V, r, loss, count, ws, s);
 }
 
 int launch_cosine_loss_bwd(const float* grad_out, const int* count_dev, int count_host, const float* label,
                            const uint8_t* mask, const float* p, const float* g, int64_t V, int C, float* gp,
                            cudaStream_t s) {
     if (V <= 0 || C <= 0) return 0;
-    const RowShape r = row_shape(V, C, p, g, gp);
-    const int G = 1 << r.gl2;
-    const int need = (r.n + G - 1) / G;  // elements per lane
-    const int kk = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 0;
-    if (r.vec)
-        launch_bwd_k<true>(kk, r.grid, grad_out, count_dev, count_host, label, mask, p, g, V, r.n, r.gl2, gp, s);
-    else
-        launch_bwd_k<false>(kk, r.grid, grad_out, count_dev, count_host, label, mask, p, g, V, r.n, r.gl2, gp, s);
-    G2V_LAUNCH_CHECK("cosine_loss_bwd_kernel");
-    return 0;
+    const RowShape r = row_shape(C, p, g, gp);
+    return r.vec ? bwd_dispatch<true>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s)
+                 : bwd_dispatch<false>(grad_out, count_dev, count_host, label, mask, p, g, V, r, gp, s);
 }
 
 }  // namespace g2v

@@ -107,3 +107,14 @@ def test_terms_bound_the_gradient():
     _, count = oracle.cosine_loss_forward(label, mask, p, g)
     grad, terms = oracle.cosine_loss_backward(1.0, count, label, mask, p, g, return_terms=True)
     assert (np.abs(grad) <= terms * (1 + 1e-12)).all()
+
+
+def test_zero_channels_and_empty_grid():
+    # C = 0: every valid voxel has loss 1 - 0 / (sqrt(eps) sqrt(eps) + eps) = 1
+    label, mask, p, g = _np(*oracle.generate_loss_inputs((6, 5, 4), 0, "noise", seed=8))
+    loss, count = oracle.cosine_loss_forward(label, mask, p, g)
+    assert count > 0 and loss == 1.0
+    assert oracle.cosine_loss_backward(1.0, count, label, mask, p, g).shape == (6, 5, 4, 0)
+    label, mask, p, g = _np(*oracle.generate_loss_inputs((0, 4, 4), 8, "noise", seed=7))
+    assert oracle.cosine_loss_forward(label, mask, p, g) == (0.0, 0)
+    assert oracle.cosine_loss_backward(1.0, 0, label, mask, p, g).shape == (0, 4, 4, 8)
