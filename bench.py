@@ -169,11 +169,23 @@ def run_ours(args, rank, world, dev):
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     gD = torch.randn((X, Y, Z), device=dev, generator=g)
     gF = torch.randn((X, Y, Z, c), device=dev, generator=g)
-    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
+    sr = args.cov_input == "sr"
+    if sr:  # Gaussians given by scales and rotation quaternions (covariances formed in the kernels)
+        from oracle import oracle
+        s_h, q_h = oracle.generate_scale_rot(n, seed=args.seed + rank + 100, var_max=cfg["var_max"])
+        host_in = (m_h, o_h, s_h, q_h, f_h)
+    else:
+        host_in = (m_h, o_h, c_h, f_h)
+    leaves = [t.to(dev).requires_grad_() for t in host_in]
     vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
 
+    def call(v, ls):
+        if sr:
+            return v(ls[0], ls[1], features=ls[4], scales=ls[2], rotations=ls[3])
+        return v(*ls)
+
     def step():
-        density, grid_feats, _ = vox(*leaves)
+        density, grid_feats, _ = call(vox, leaves)
         return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
 
     def barrier():
@@ -211,8 +223,12 @@ def run_ours(args, rank, world, dev):
     launches_per_step = sum(v[1] for v in prof.values()) / args.steps
 
     # sizes for the roofline
-    out = _C.gaussian_voxelizer_forward(*[t.detach() for t in leaves[:3]], size, rng, leaves[3].detach(),
-                                        timing=False)
+    if sr:
+        out = _C._forward_impl(leaves[0].detach(), leaves[1].detach(), None, size, rng, leaves[4].detach(), False,
+                               scale_rot=(leaves[2].detach(), leaves[3].detach()))[0]
+    else:
+        out = _C.gaussian_voxelizer_forward(*[t.detach() for t in leaves[:3]], size, rng, leaves[3].detach(),
+                                            timing=False)
     M = int(out[7].numel())
     MB = _C.backward_plan(out[2], out[3], (X, Y, Z), c)
     del out
@@ -236,7 +252,7 @@ def run_ours(args, rank, world, dev):
     sb = step_bytes(n, c, V, M)
 
     # end-to-end through the public API with pinned host inputs (H2D inside the timed region)
-    host = [t.pin_memory() for t in (m_h, o_h, c_h, f_h)]
+    host = [t.pin_memory() for t in host_in]
     h2d = sum(t.numel() * t.element_size() for t in host)
     # stats timing off: the reference-style per-call timing synchronisations are optional
     vox_e2e = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
@@ -245,7 +261,7 @@ def run_ours(args, rank, world, dev):
         # H2D of the inputs, forward, backward with the same upstream gradients as the device-timed step,
         # and a D2H read of one element of the result (4 bytes)
         ls = [t.to(dev, non_blocking=True).requires_grad_() for t in host]
-        density, grid_feats, _ = vox_e2e(*ls)
+        density, grid_feats, _ = call(vox_e2e, ls)
         grads = torch.autograd.grad([density, grid_feats], ls, [gD, gF])
         return grads[0].reshape(-1)[:1].to("cpu").item()
 
@@ -274,7 +290,9 @@ def run_ours(args, rank, world, dev):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference distributions)",
         "config": {"workload": f"{args.config}: N={n} Gaussians, C={c} fp32 features, {X}x{Y}x{Z} voxels, "
-                               f"fwd+bwd with randn upstream grads", "global_batch": world,
+                               f"fwd+bwd with randn upstream grads"
+                               + (", Gaussians as scales + rotation quaternions (grads to both)" if sr else ""),
+                   "global_batch": world,
                    "scenes_per_rank": 1, "l2": "inputs larger than L2 (grid_feats 4*V*C bytes)",
                    "pairs_M": M, "block_pairs": MB, "parallelism": f"dp{world} (independent scenes)",
                    "e2e": "PyCudaGaussianVoxelizer(timing=False) + torch.autograd.grad with the upstream "
@@ -726,6 +744,8 @@ def main():
     ap.add_argument("--path", default="voxelizer", choices=["voxelizer", "loss"],
                     help="voxelizer: the G2V fwd+bwd step (default); loss: the feature cosine loss fwd+bwd")
     ap.add_argument("--loss-channels", type=int, default=0, help="channels of the loss workload (default: config C)")
+    ap.add_argument("--cov-input", default="cov", choices=["cov", "sr"],
+                    help="voxelizer inputs: covariances (default) or scales + rotation quaternions")
     ap.add_argument("--single-scene", action="store_true",
                     help="one scene split into x-slabs over the ranks (strong scaling) instead of one scene per rank")
     args = ap.parse_args()

@@ -156,8 +156,39 @@ G2V_API int g2v_forward_prepare_plan(const float* means3d, const float* covarian
                                      size_t workspace_bytes, void* stream, int64_t* num_pairs,
                                      int64_t* num_block_pairs);
 
-/* Workspace of g2v_forward_prepare_plan (N-sized). */
+/* Workspace of g2v_forward_prepare_plan (N-sized); also that of g2v_forward_prepare_plan_sr. */
 G2V_API int g2v_forward_prepare_plan_workspace_size(int64_t num_gaussians, size_t* bytes);
+
+/*
+ * Covariances from per-Gaussian scales (N,3) and rotation quaternions (N,4, (r, x, y, z), any norm):
+ * covariances (N,9) = R(q/|q|) diag(s)^2 R(q/|q|)^T, row-major.  Replaces the GaussTR front end that
+ * feeds the voxelizer, get_covariance(scales, quat_to_rotmat(rotations)) (test/gaussian_voxelizer.py:
+ * 14-37, called at :176-177).  Stream-ordered, no synchronisation.  A zero quaternion gives NaN, as
+ * the reference's division does.
+ */
+G2V_API int g2v_covariance_from_scale_rot(const float* scales, const float* rotations, int64_t num_gaussians,
+                                          float* covariances, void* stream);
+
+/*
+ * Gradient of g2v_covariance_from_scale_rot: from grad_covariances (N,9, entries independent, the layout
+ * g2v_backward writes) to grad_scales (N,3) and grad_rotations (N,4) -- what autograd through the
+ * reference front end gives.
+ */
+G2V_API int g2v_covariance_from_scale_rot_backward(const float* scales, const float* rotations,
+                                                   const float* grad_covariances, int64_t num_gaussians,
+                                                   float* grad_scales, float* grad_rotations, void* stream);
+
+/*
+ * g2v_forward_prepare_plan with the covariances formed inside the preparation kernel from scales (N,3)
+ * and rotations (N,4) (the same bits as g2v_covariance_from_scale_rot): no covariance array is read or
+ * written.  Same outputs, workspace and single synchronisation.
+ */
+G2V_API int g2v_forward_prepare_plan_sr(const float* means3d, const float* scales, const float* rotations,
+                                        int64_t num_gaussians, const float voxel_size[3],
+                                        const float voxel_range[6], float* cov_inv, int32_t* valid_voxel_lb,
+                                        int32_t* valid_voxel_ub, int32_t* num_voxels, int32_t* g2t_offsets,
+                                        int64_t channels, void* workspace, size_t workspace_bytes, void* stream,
+                                        int64_t* num_pairs, int64_t* num_block_pairs);
 
 /* Workspace of g2v_backward. */
 G2V_API int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs, int64_t num_block_pairs,
@@ -182,6 +213,24 @@ G2V_API int g2v_backward(const float* grad_density, const float* grad_grid_feats
                  const float* grid_feats, float* grad_means3d, float* grad_covariances, float* grad_opacity,
                  float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
                  size_t workspace_bytes, void* stream);
+
+/*
+ * g2v_backward for Gaussians parameterised by scales (N,3) and rotations (N,4): the same inputs plus
+ * scales/rotations, and grad_scales (N,3) / grad_rotations (N,4) in place of grad_covariances (the chain
+ * rule runs in the per-Gaussian gradient reduction, so dL/dSigma is never written).  Workspace: the
+ * g2v_backward_workspace_size of the same sizes.  Replaces autograd through get_covariance /
+ * quat_to_rotmat (test/gaussian_voxelizer.py:14-37) after the reference backward (cu:1920-2057).
+ */
+G2V_API int g2v_backward_sr(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                            const float* opacity, const float* scales, const float* rotations, const float* cov_inv,
+                            const float* features, int64_t num_gaussians, int64_t channels,
+                            const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                            const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub,
+                            const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t num_pairs,
+                            int64_t num_block_pairs, const float* density, const float* grid_feats,
+                            float* grad_means3d, float* grad_scales, float* grad_rotations, float* grad_opacity,
+                            float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /*
  * g2v_backward for one x-slab with slab-local volume arrays (grad_density, grad_grid_feats, density,

@@ -330,3 +330,66 @@ def generate_loss_inputs(dims, channels, case="noise", p_label=0.25, p_mask=0.7,
     else:
         raise ValueError(case)
     return label.contiguous(), mask.contiguous(), feats.contiguous(), gt.contiguous()
+
+
+# ---------------------------------------------------------------------------------------------------
+# Covariance from (scale, rotation quaternion): the GaussTR front end of the voxelizer
+# (test/gaussian_voxelizer.py:14-37, quat_to_rotmat and get_covariance), float64 numpy restatement.
+
+def _rotmat(q):
+    """Rotation matrices (..., 3, 3) of quaternions (..., 4) = (r, x, y, z) after normalisation (:14-29)."""
+    q = q / np.sqrt((q ** 2).sum(axis=-1, keepdims=True))
+    r, x, y, z = q[..., 0], q[..., 1], q[..., 2], q[..., 3]
+    R = np.empty(q.shape[:-1] + (3, 3))
+    R[..., 0, 0] = 1 - 2 * (y * y + z * z)
+    R[..., 0, 1] = 2 * (x * y - r * z)
+    R[..., 0, 2] = 2 * (x * z + r * y)
+    R[..., 1, 0] = 2 * (x * y + r * z)
+    R[..., 1, 1] = 1 - 2 * (x * x + z * z)
+    R[..., 1, 2] = 2 * (y * z - r * x)
+    R[..., 2, 0] = 2 * (x * z - r * y)
+    R[..., 2, 1] = 2 * (y * z + r * x)
+    R[..., 2, 2] = 1 - 2 * (x * x + y * y)
+    return q, R
+
+
+def covariance_from_scale_rot(scales, rotations):
+    """Sigma = (R diag(s)) (R diag(s))^T, (..., 3, 3), of get_covariance(s, quat_to_rotmat(q)) (:31-37)."""
+    s = np.asarray(scales, np.float64)
+    _, R = _rotmat(np.asarray(rotations, np.float64))
+    M = R * s[..., None, :]
+    return M @ np.swapaxes(M, -1, -2)
+
+
+def covariance_from_scale_rot_backward(scales, rotations, grad_cov):
+    """(dL/ds (..., 3), dL/dq (..., 4)) from dL/dSigma (..., 3, 3) with independent entries, by the chain
+    rule through Sigma = M M^T, M = R diag(s), R = R(q / |q|) -- what autograd through the reference
+    front end computes."""
+    s = np.asarray(scales, np.float64)
+    q0 = np.asarray(rotations, np.float64)
+    G = np.asarray(grad_cov, np.float64).reshape(s.shape[:-1] + (3, 3))
+    q, R = _rotmat(q0)
+    M = R * s[..., None, :]
+    gM = (G + np.swapaxes(G, -1, -2)) @ M
+    gs = (gM * R).sum(axis=-2)
+    gR = gM * s[..., None, :]
+    r, x, y, z = q[..., 0], q[..., 1], q[..., 2], q[..., 3]
+    g = [gR[..., i, j] for i in range(3) for j in range(3)]
+    gr = 2 * (-z * g[1] + y * g[2] + z * g[3] - x * g[5] - y * g[6] + x * g[7])
+    gx = 2 * (y * g[1] + z * g[2] + y * g[3] - 2 * x * g[4] - r * g[5] + z * g[6] + r * g[7] - 2 * x * g[8])
+    gy = 2 * (-2 * y * g[0] + x * g[1] + r * g[2] + x * g[3] + z * g[5] - r * g[6] + z * g[7] - 2 * y * g[8])
+    gz = 2 * (-2 * z * g[0] - r * g[1] + x * g[2] + r * g[3] - 2 * z * g[4] + y * g[5] + x * g[6] + y * g[7])
+    gqh = np.stack([gr, gx, gy, gz], axis=-1)
+    norm = np.sqrt((q0 ** 2).sum(axis=-1, keepdims=True))
+    gq = (gqh - q * (q * gqh).sum(axis=-1, keepdims=True)) / norm
+    return gs, gq
+
+
+def generate_scale_rot(n, seed=0, var_max=2.5):
+    """Seeded scales and quaternions with cfg-like spreads: s = sqrt(U(0.5, var_max)) per axis (the
+    variances of generate_inputs), q = randn(4) scaled by U(0.5, 2) (unnormalised, as networks emit)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    s = torch.sqrt(torch.rand(n, 3, generator=g) * (var_max - 0.5) + 0.5)
+    q = torch.randn(n, 4, generator=g) * (torch.rand(n, 1, generator=g) * 1.5 + 0.5)
+    return s.contiguous(), q.contiguous()

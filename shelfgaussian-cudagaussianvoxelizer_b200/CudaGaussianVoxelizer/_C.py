@@ -16,7 +16,8 @@ import torch
 from . import _lib
 
 __all__ = ["gaussian_voxelizer_forward", "gaussian_voxelizer_backward", "grid_shape", "t2g_maps",
-           "CudaFeatsCosinelossForward", "CudaFeatsCosinelossBackward"]
+           "CudaFeatsCosinelossForward", "CudaFeatsCosinelossBackward", "covariance_from_scale_rot",
+           "covariance_from_scale_rot_backward"]
 
 # id(tensor) -> (weakref to the tensor, its _version, host values).  The weak reference makes sure a
 # hit is the same live tensor object (an address or id can be reused after a tensor is freed).
@@ -84,26 +85,45 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
+def _scale_rot_inputs(scales, rotations, n, dev):
+    """(N,3) scales and (N,4) rotation quaternions, float32 contiguous on ``dev``."""
+    _need(scales, "scales", dim=2, device=dev)
+    _need(rotations, "rotations", dim=2, device=dev)
+    if tuple(scales.shape) != (n, 3) or tuple(rotations.shape) != (n, 4):
+        raise RuntimeError(f"expected scales (N,3) and rotations (N,4) for N={n}; got {tuple(scales.shape)}, "
+                           f"{tuple(rotations.shape)}")
+    return scales.contiguous(), rotations.contiguous()
+
+
 def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False,
-                  plan=False):
+                  plan=False, scale_rot=None):
+    """The forward; ``scale_rot=(scales, rotations)`` replaces ``covariances`` (then ``plan`` is implied and
+    the covariances are formed inside the preparation kernel)."""
     lib = _lib.load()
     size_h = _host_values(voxel_size, 3, "voxel_size")
     range_h = _host_values(voxel_range, 6, "voxel_range")
     _need(means3D, "means3D", dim=2)
     dev = means3D.device
     _need(opacity, "opacity", dim=1, device=dev)
-    _need(covariances, "covariances", dim=2, device=dev)
     n = means3D.shape[0]
-    if means3D.shape[1] != 3 or covariances.shape != (n, 9) or opacity.shape[0] != n:
+    if scale_rot is not None:
+        plan = True
+        scales, rotations = _scale_rot_inputs(scale_rot[0], scale_rot[1], n, dev)
+        covariances = None
+    else:
+        _need(covariances, "covariances", dim=2, device=dev)
+    if means3D.shape[1] != 3 or opacity.shape[0] != n or (covariances is not None and covariances.shape != (n, 9)):
         raise RuntimeError(f"expected means3D (N,3), opacity (N,), covariances (N,9); got {tuple(means3D.shape)}, "
-                           f"{tuple(opacity.shape)}, {tuple(covariances.shape)}")
+                           f"{tuple(opacity.shape)}, {None if covariances is None else tuple(covariances.shape)}")
     if features is not None:
         _need(features, "features", dim=2, device=dev)
         if features.shape[0] != n:
             raise RuntimeError(f"features must have {n} rows, got {features.shape[0]}")
         features = features.contiguous()
     c = 0 if features is None else int(features.shape[1])
-    means3D, opacity, covariances = means3D.contiguous(), opacity.contiguous(), covariances.contiguous()
+    means3D, opacity = means3D.contiguous(), opacity.contiguous()
+    if covariances is not None:
+        covariances = covariances.contiguous()
     (X, Y, Z), _ = _lib.grid_shape(size_h, range_h)
     i32 = dict(dtype=torch.int32, device=dev)
     f32 = dict(dtype=torch.float32, device=dev)
@@ -129,7 +149,13 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
             ev0.record(stream)
         m = ctypes.c_int64()
         mb = ctypes.c_int64()
-        if plan:  # prepare + the backward's block-pair count, one synchronisation
+        if scale_rot is not None:  # covariances formed in the preparation kernel
+            _lib.check(lib.g2v_forward_prepare_plan_sr(_ptr(means3D), _ptr(scales), _ptr(rotations), n,
+                                                       _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb),
+                                                       _ptr(ub), _ptr(nvox), _ptr(g2t_offsets), c, _ptr(ws1),
+                                                       ws1.numel(), sptr, ctypes.byref(m), ctypes.byref(mb)),
+                       "g2v_forward_prepare_plan_sr")
+        elif plan:  # prepare + the backward's block-pair count, one synchronisation
             _lib.check(lib.g2v_forward_prepare_plan(_ptr(means3D), _ptr(covariances), n, _lib.f3(size_h),
                                                     _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub), _ptr(nvox),
                                                     _ptr(g2t_offsets), c, _ptr(ws1), ws1.numel(), sptr,
@@ -205,13 +231,16 @@ def backward_plan(valid_voxel_lb, valid_voxel_ub, dims, channels) -> int:
 def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity, cov_inv, voxel_size, voxel_range,
                                 valid_voxel_lb, valid_voxel_ub, num_voxels_per_gaussian, g2t_offsets, g2t_tile_ids,
                                 density, grid_feats, features=None, *, timing: bool = True,
-                                num_block_pairs: int | None = None, tile_x_range=None):
+                                num_block_pairs: int | None = None, tile_x_range=None, scale_rot=None):
     """Backward of the G2V splat (reference src/bindings.cpp:30-64, cu:1920-2057).
 
     Returns ``(grad_means3D (N,3), grad_cov (N,9), grad_opacity (N,), grad_feats (N,C), bwd_sec)``;
     ``grad_feats`` is (N,0) when ``features`` is None.  Inputs must be contiguous CUDA tensors of the
     reference's dtypes (RuntimeError otherwise, like the reference's TORCH_CHECKs, cu:1941-1954).
     ``tile_x_range=(b, e)`` restricts the gradient to the voxels of tiles with x in [b, e).
+    ``scale_rot=(scales (N,3), rotations (N,4))``: the Gaussians' covariances came from them; the second
+    output is then the pair ``(grad_scales (N,3), grad_rotations (N,4))`` in place of grad_cov (the chain
+    rule runs inside the gradient reduction).
     """
     lib = _lib.load()
     dev = means3D.device
@@ -249,7 +278,12 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
                    "g2v_backward_workspace_size")
         ws = _workspace(nbytes.value, dev)
         grad_means = torch.empty((n, 3), **f32)
-        grad_cov = torch.empty((n, 9), **f32)
+        if scale_rot is not None:
+            scales, rotations = _scale_rot_inputs(scale_rot[0], scale_rot[1], n, dev)
+            grad_cov = torch.empty((n, 3), **f32)  # grad_scales
+            grad_rot = torch.empty((n, 4), **f32)
+        else:
+            grad_cov = torch.empty((n, 9), **f32)
         grad_op = torch.empty((n,), **f32)
         grad_feats = torch.empty((n, c), **f32)
         tb, te = (0, 0) if tile_x_range is None else (int(tile_x_range[0]), int(tile_x_range[1]))
@@ -258,18 +292,76 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record(stream)
         fptr = _features_ptr(features, grad_op if grad_op.numel() else density)
-        _lib.check(lib.g2v_backward(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None, _ptr(means3D),
-                                    _ptr(opacity), _ptr(cov_inv), fptr, n, c, _lib.f3(size_h), _lib.f6(range_h),
-                                    _lib.i3(dims), _ptr(valid_voxel_lb), _ptr(valid_voxel_ub), _ptr(g2t_offsets),
-                                    _ptr(g2t_tile_ids), m, int(num_block_pairs), _ptr(density), _ptr(grid_feats),
-                                    _ptr(grad_means), _ptr(grad_cov), _ptr(grad_op), _ptr(grad_feats), tb, te,
-                                    _ptr(ws), ws.numel(), sptr), "g2v_backward")
+        if scale_rot is not None:
+            _lib.check(lib.g2v_backward_sr(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None,
+                                           _ptr(means3D), _ptr(opacity), _ptr(scales), _ptr(rotations), _ptr(cov_inv),
+                                           fptr, n, c, _lib.f3(size_h), _lib.f6(range_h), _lib.i3(dims),
+                                           _ptr(valid_voxel_lb), _ptr(valid_voxel_ub), _ptr(g2t_offsets),
+                                           _ptr(g2t_tile_ids), m, int(num_block_pairs), _ptr(density),
+                                           _ptr(grid_feats), _ptr(grad_means), _ptr(grad_cov), _ptr(grad_rot),
+                                           _ptr(grad_op), _ptr(grad_feats), tb, te, _ptr(ws), ws.numel(), sptr),
+                       "g2v_backward_sr")
+        else:
+            _lib.check(lib.g2v_backward(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None,
+                                        _ptr(means3D), _ptr(opacity), _ptr(cov_inv), fptr, n, c, _lib.f3(size_h),
+                                        _lib.f6(range_h), _lib.i3(dims), _ptr(valid_voxel_lb), _ptr(valid_voxel_ub),
+                                        _ptr(g2t_offsets), _ptr(g2t_tile_ids), m, int(num_block_pairs),
+                                        _ptr(density), _ptr(grid_feats), _ptr(grad_means), _ptr(grad_cov),
+                                        _ptr(grad_op), _ptr(grad_feats), tb, te, _ptr(ws), ws.numel(), sptr),
+                       "g2v_backward")
         sec = 0.0
         if timing:
             ev1.record(stream)
             ev1.synchronize()
             sec = ev0.elapsed_time(ev1) / 1000.0
+    if scale_rot is not None:
+        return grad_means, (grad_cov, grad_rot), grad_op, grad_feats, sec
     return grad_means, grad_cov, grad_op, grad_feats, sec
+
+
+def covariance_from_scale_rot(scales, rotations):
+    """Covariances R(q/|q|) diag(s)^2 R(q/|q|)^T of (..., 3) scales and (..., 4) (r, x, y, z) quaternions,
+    as (..., 3, 3) -- the front end of GaussTR pipelines, get_covariance(scales, quat_to_rotmat(rotations))
+    (reference test/gaussian_voxelizer.py:14-37), on the device (no autograd; see
+    ``CudaGaussianVoxelizer.covariance_from_scale_rot`` for the differentiable one)."""
+    lib = _lib.load()
+    _need(scales, "scales")
+    dev = scales.device
+    _need(rotations, "rotations", device=dev)
+    lead = tuple(scales.shape[:-1])
+    if scales.shape[-1:] != (3,) or tuple(rotations.shape) != lead + (4,):
+        raise RuntimeError(f"expected scales (...,3) and rotations (...,4); got {tuple(scales.shape)}, "
+                           f"{tuple(rotations.shape)}")
+    s = scales.detach().reshape(-1, 3).contiguous()
+    q = rotations.detach().reshape(-1, 4).contiguous()
+    n = s.shape[0]
+    with torch.cuda.device(dev):
+        cov = torch.empty((n, 9), dtype=torch.float32, device=dev)
+        sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(lib.g2v_covariance_from_scale_rot(_ptr(s), _ptr(q), n, _ptr(cov), sptr),
+                   "g2v_covariance_from_scale_rot")
+    return cov.reshape(lead + (3, 3))
+
+
+def covariance_from_scale_rot_backward(scales, rotations, grad_covariances):
+    """(grad_scales (..., 3), grad_rotations (..., 4)) from grad_covariances (..., 3, 3) or (..., 9)."""
+    lib = _lib.load()
+    dev = scales.device
+    lead = tuple(scales.shape[:-1])
+    s = scales.detach().reshape(-1, 3).contiguous()
+    q = rotations.detach().reshape(-1, 4).contiguous()
+    n = s.shape[0]
+    _need(grad_covariances, "grad_covariances", device=dev)
+    if grad_covariances.numel() != 9 * n:
+        raise RuntimeError(f"grad_covariances must have {9 * n} elements, got {grad_covariances.numel()}")
+    g = grad_covariances.detach().reshape(n, 9).contiguous()
+    with torch.cuda.device(dev):
+        gs = torch.empty((n, 3), dtype=torch.float32, device=dev)
+        gq = torch.empty((n, 4), dtype=torch.float32, device=dev)
+        sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(lib.g2v_covariance_from_scale_rot_backward(_ptr(s), _ptr(q), _ptr(g), n, _ptr(gs), _ptr(gq), sptr),
+                   "g2v_covariance_from_scale_rot_backward")
+    return gs.reshape(lead + (3,)), gq.reshape(lead + (4,))
 
 
 def _loss_inputs(voxel_label, occ_gt_mask_camera, d_grid_feats, pseudo_dino_gt):

@@ -20,7 +20,8 @@ from ._C import (CudaFeatsCosinelossBackward, CudaFeatsCosinelossForward, _cosin
 
 _lib.load()  # fail loudly at import when the native library is missing
 
-__all__ = ["PyCudaGaussianVoxelizer", "_CudaGaussianVoxelizeFunction", "gaussian_voxelizer_forward",
+__all__ = ["PyCudaGaussianVoxelizer", "_CudaGaussianVoxelizeFunction", "_CudaGaussianVoxelizeSRFunction",
+           "covariance_from_scale_rot", "gaussian_voxelizer_forward",
            "gaussian_voxelizer_backward", "PyCudaFeatsCosineLoss", "_CudaFeatsCosinelossFunction",
            "CudaFeatsCosinelossForward", "CudaFeatsCosinelossBackward", "_C"]
 
@@ -59,11 +60,72 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
         return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None)
 
 
+class _CudaGaussianVoxelizeSRFunction(torch.autograd.Function):
+    """The splat for Gaussians given by scales (N,3) and rotation quaternions (N,4) instead of covariances:
+    the covariances are formed inside the preparation kernel and the gradient reduction applies the chain
+    rule, so neither Sigma nor dL/dSigma is materialised.  Same outputs as _CudaGaussianVoxelizeFunction;
+    gradients flow to means3D, opacity, scales, rotations and features (the composition of the reference
+    voxelizer with GaussTR's get_covariance / quat_to_rotmat, test/gaussian_voxelizer.py:14-37)."""
+
+    @staticmethod
+    def forward(ctx, means3D, opacity, scales, rotations, voxel_size, voxel_range, features, timing=True):
+        ((density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, fwd_sec),
+         num_block_pairs) = _forward_impl(means3D, opacity, None, voxel_size, voxel_range, features, timing,
+                                          scale_rot=(scales, rotations))
+        stats = torch.zeros(2, dtype=torch.float32, device="cpu")
+        stats[0] = fwd_sec
+        ctx.save_for_backward(means3D, opacity, scales, rotations, voxel_size, voxel_range, cov_inv, lb, ub, nvox,
+                              g2t_offsets, g2t_tile_ids, density, grid_feats, features, stats)
+        ctx.timing = timing
+        ctx.num_block_pairs = num_block_pairs
+        ctx.mark_non_differentiable(stats)
+        return density, grid_feats, stats
+
+    @staticmethod
+    def backward(ctx, grad_density_output, grad_feats_output, grad_stats):
+        (means3D, opacity, scales, rotations, voxel_size, voxel_range, cov_inv, lb, ub, nvox, g2t_offsets,
+         g2t_tile_ids, density, grid_feats, features, stats) = ctx.saved_tensors
+        gout = grad_density_output.to(torch.float32).contiguous()
+        if features is not None and features.shape[1] > 0:
+            gfeat = grad_feats_output.to(torch.float32).contiguous()
+        else:
+            gfeat = grad_feats_output
+        grad_means, (grad_scales, grad_rot), grad_op, grad_feats, bwd_sec = gaussian_voxelizer_backward(
+            gout, gfeat, means3D, opacity, cov_inv, voxel_size, voxel_range, lb, ub, nvox, g2t_offsets,
+            g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs,
+            scale_rot=(scales, rotations))
+        stats[1] = bwd_sec
+        return (grad_means, grad_op, grad_scales, grad_rot, None, None,
+                grad_feats if features is not None else None, None)
+
+
+class _CovarianceFromScaleRot(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, scales, rotations):
+        ctx.save_for_backward(scales, rotations)
+        return _C.covariance_from_scale_rot(scales, rotations)
+
+    @staticmethod
+    def backward(ctx, grad_cov):
+        scales, rotations = ctx.saved_tensors
+        gs, gq = _C.covariance_from_scale_rot_backward(scales, rotations, grad_cov.to(torch.float32))
+        return gs, gq
+
+
+def covariance_from_scale_rot(scales, rotations):
+    """Differentiable covariances (..., 3, 3) = R(q/|q|) diag(s)^2 R(q/|q|)^T from (..., 3) scales and
+    (..., 4) (r, x, y, z) quaternions: get_covariance(scales, quat_to_rotmat(rotations)) of the reference's
+    GaussTR front end (test/gaussian_voxelizer.py:14-37), one sm_100a kernel each way."""
+    return _CovarianceFromScaleRot.apply(scales, rotations)
+
+
 class PyCudaGaussianVoxelizer(nn.Module):
     """Splat 3D Gaussians (and optional per-Gaussian features) into a dense voxel grid.
 
     forward(means3D (N,3), opacity (N,), covariances (N,9), features (N,C) or None)
         -> (density (X,Y,Z), grid_feats (X,Y,Z,C), stats (2,) CPU float32)
+    or forward(means3D, opacity, features=..., scales=(N,3), rotations=(N,4)) for Gaussians given by
+    scale and rotation quaternion (the covariance is formed and differentiated inside the kernels).
     ``stats[0]`` is the forward device time in seconds, ``stats[1]`` the backward's (filled by
     ``.backward()``).  ``timing=False`` skips the two end-of-call synchronisations that fill them
     (stats stay 0).  Reference: CudaGaussianVoxelizer/__init__.py:69-82.
@@ -78,7 +140,17 @@ class PyCudaGaussianVoxelizer(nn.Module):
         _C._host_values(self.voxel_size, 3, "voxel_size")
         _C._host_values(self.voxel_range, 6, "voxel_range")
 
-    def forward(self, means3D, opacity, covariances, features=None):
+    def forward(self, means3D, opacity, covariances=None, features=None, *, scales=None, rotations=None):
+        """``covariances`` (N,9) as in the reference, or -- in its place -- ``scales`` (N,3) and
+        ``rotations`` (N,4) quaternions (r, x, y, z), as GaussTR's voxelizer accepts them
+        (test/gaussian_voxelizer.py:168-177); gradients then flow to scales and rotations."""
+        if covariances is None:
+            if scales is None or rotations is None:
+                raise RuntimeError("PyCudaGaussianVoxelizer: pass covariances, or scales and rotations")
+            return _CudaGaussianVoxelizeSRFunction.apply(means3D, opacity, scales, rotations, self.voxel_size,
+                                                         self.voxel_range, features, self.timing)
+        if scales is not None or rotations is not None:
+            raise RuntimeError("PyCudaGaussianVoxelizer: pass covariances or scales/rotations, not both")
         return _CudaGaussianVoxelizeFunction.apply(means3D, opacity, covariances, self.voxel_size, self.voxel_range,
                                                    features, self.timing)
 

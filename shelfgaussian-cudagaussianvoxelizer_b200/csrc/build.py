@@ -37,9 +37,11 @@ SOURCES = {
     "g2v_spass_tc.cu": [],
     "g2v_selftest.cu": [],
     "g2v_loss.cu": [],
+    "g2v_cov.cu": [],
 }
 HEADERS_TC = ["g2v_tc.cuh"]
-HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(HERE, "g2v_tc.cuh"), os.path.join(INCLUDE, "g2v.h")]
+HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(HERE, "g2v_tc.cuh"), os.path.join(HERE, "g2v_cov.cuh"),
+           os.path.join(INCLUDE, "g2v.h")]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

@@ -62,9 +62,14 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
                     const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
                     const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s);
 int launch_wait_timeout(int* err, cudaStream_t s, int* gave_up_host);
+// scales / quats / grad_quats non-NULL: grad_cov receives dL/dscales (n,3) and grad_quats dL/dquats (n,4).
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
                     const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
-                    float* grad_opacity, cudaStream_t s);
+                    float* grad_opacity, cudaStream_t s, const float* scales = nullptr,
+                    const float* quats = nullptr, float* grad_quats = nullptr);
+int launch_cov_from_scale_rot(const float* scales, const float* quats, int64_t n, float* cov, cudaStream_t s);
+int launch_cov_from_scale_rot_backward(const float* scales, const float* quats, const float* grad_cov, int64_t n,
+                                       float* grad_scales, float* grad_quats, cudaStream_t s);
 int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const int32_t* lb, const int32_t* ub,
                         int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
                         cudaStream_t s);
@@ -567,18 +572,23 @@ int g2v_forward_prepare_plan_workspace_size(int64_t num_gaussians, size_t* bytes
     return G2V_SUCCESS;
 }
 
-int g2v_forward_prepare_plan(const float* means3d, const float* covariances, int64_t num_gaussians,
-                             const float voxel_size[3], const float voxel_range[6], float* cov_inv,
-                             int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
-                             int32_t* g2t_offsets, int64_t channels, void* workspace, size_t workspace_bytes,
-                             void* stream, int64_t* num_pairs, int64_t* num_block_pairs) {
+}  // extern "C"
+
+// covariances, or (scales, rotations) when scales is non-NULL
+static int prepare_plan_impl(const float* means3d, const float* covariances, const float* scales,
+                             const float* rotations, int64_t num_gaussians, const float voxel_size[3],
+                             const float voxel_range[6], float* cov_inv, int32_t* valid_voxel_lb,
+                             int32_t* valid_voxel_ub, int32_t* num_voxels, int32_t* g2t_offsets, int64_t channels,
+                             void* workspace, size_t workspace_bytes, void* stream, int64_t* num_pairs,
+                             int64_t* num_block_pairs) {
     g_msg[0] = 0;
     Grid G;
     int rc = make_grid(voxel_size, voxel_range, G);
     if (rc) return rc;
+    const bool have_cov = scales ? rotations != nullptr : covariances != nullptr;
     if (num_gaussians < 0 || num_gaussians > INT32_MAX - 1 || channels < 0 || !g2t_offsets || !num_pairs ||
         !num_block_pairs ||
-        (num_gaussians > 0 && (!means3d || !covariances || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
+        (num_gaussians > 0 && (!means3d || !have_cov || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
                                !num_voxels))) {
         set_error("g2v_forward_prepare_plan: invalid pointer or count");
         return G2V_ERROR_INVALID_VALUE;
@@ -593,7 +603,7 @@ int g2v_forward_prepare_plan(const float* means3d, const float* covariances, int
     carve_plan(c.take<char>(carve_plan(nullptr, num_gaussians, wb)), num_gaussians, wb);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if ((rc = launch_prepare_boxes(means3d, covariances, num_gaussians, G, cov_inv, valid_voxel_lb, valid_voxel_ub,
-                                   num_voxels, wp.ntiles, s)))
+                                   num_voxels, wp.ntiles, s, scales, rotations)))
         return rc;
     if ((rc = launch_exclusive_scan(wp.ntiles, num_gaussians, g2t_offsets, wp.total, wp.scan, s))) return rc;
     const bool blocks = channels > 0 && num_gaussians > 0;
@@ -621,6 +631,59 @@ int g2v_forward_prepare_plan(const float* means3d, const float* covariances, int
     return G2V_SUCCESS;
 }
 
+extern "C" {
+
+int g2v_forward_prepare_plan(const float* means3d, const float* covariances, int64_t num_gaussians,
+                             const float voxel_size[3], const float voxel_range[6], float* cov_inv,
+                             int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
+                             int32_t* g2t_offsets, int64_t channels, void* workspace, size_t workspace_bytes,
+                             void* stream, int64_t* num_pairs, int64_t* num_block_pairs) {
+    return prepare_plan_impl(means3d, covariances, nullptr, nullptr, num_gaussians, voxel_size, voxel_range, cov_inv,
+                             valid_voxel_lb, valid_voxel_ub, num_voxels, g2t_offsets, channels, workspace,
+                             workspace_bytes, stream, num_pairs, num_block_pairs);
+}
+
+int g2v_forward_prepare_plan_sr(const float* means3d, const float* scales, const float* rotations,
+                                int64_t num_gaussians, const float voxel_size[3], const float voxel_range[6],
+                                float* cov_inv, int32_t* valid_voxel_lb, int32_t* valid_voxel_ub,
+                                int32_t* num_voxels, int32_t* g2t_offsets, int64_t channels, void* workspace,
+                                size_t workspace_bytes, void* stream, int64_t* num_pairs, int64_t* num_block_pairs) {
+    if (num_gaussians > 0 && (!scales || !rotations)) {
+        g_msg[0] = 0;
+        set_error("g2v_forward_prepare_plan_sr: scales and rotations are required");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    static const float kDummy = 0.f;  // non-NULL marker for the empty case
+    return prepare_plan_impl(means3d, nullptr, scales ? scales : &kDummy, rotations ? rotations : &kDummy,
+                             num_gaussians, voxel_size, voxel_range, cov_inv, valid_voxel_lb, valid_voxel_ub,
+                             num_voxels, g2t_offsets, channels, workspace, workspace_bytes, stream, num_pairs,
+                             num_block_pairs);
+}
+
+int g2v_covariance_from_scale_rot(const float* scales, const float* rotations, int64_t num_gaussians,
+                                  float* covariances, void* stream) {
+    g_msg[0] = 0;
+    if (num_gaussians < 0 || (num_gaussians > 0 && (!scales || !rotations || !covariances))) {
+        set_error("g2v_covariance_from_scale_rot: invalid pointer or count");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return launch_cov_from_scale_rot(scales, rotations, num_gaussians, covariances,
+                                     static_cast<cudaStream_t>(stream));
+}
+
+int g2v_covariance_from_scale_rot_backward(const float* scales, const float* rotations,
+                                           const float* grad_covariances, int64_t num_gaussians, float* grad_scales,
+                                           float* grad_rotations, void* stream) {
+    g_msg[0] = 0;
+    if (num_gaussians < 0 ||
+        (num_gaussians > 0 && (!scales || !rotations || !grad_covariances || !grad_scales || !grad_rotations))) {
+        set_error("g2v_covariance_from_scale_rot_backward: invalid pointer or count");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return launch_cov_from_scale_rot_backward(scales, rotations, grad_covariances, num_gaussians, grad_scales,
+                                              grad_rotations, static_cast<cudaStream_t>(stream));
+}
+
 int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs, int64_t num_block_pairs,
                                 const int dims[3], int64_t channels, size_t* bytes) {
     if (!bytes || !dims || num_gaussians < 0 || num_pairs < 0 || num_block_pairs < 0 || channels < 0) {
@@ -644,7 +707,9 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
                          const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
                          const float* density, const float* grid_feats, float* grad_means3d,
                          float* grad_covariances, float* grad_opacity, float* grad_features, int tile_x_begin,
-                         int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local) {
+                         int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local,
+                         const float* scales = nullptr, const float* rotations = nullptr,
+                         float* grad_rotations = nullptr) {
     (void)grid_feats;
     g_msg[0] = 0;
     Grid G;
@@ -661,7 +726,8 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
         !grad_density || !density || !g2t_offsets || (num_pairs > 0 && !g2t_tile_ids) ||
         (C > 0 && !grad_grid_feats) || (C > 0 && num_gaussians > 0 && !grad_features) ||
         (num_gaussians > 0 && (!means3d || !opacity || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
-                               !grad_means3d || !grad_covariances || !grad_opacity))) {
+                               !grad_means3d || !grad_covariances || !grad_opacity)) ||
+        (num_gaussians > 0 && scales && (!rotations || !grad_rotations))) {
         set_error("g2v_backward: invalid pointer or size");
         return G2V_ERROR_INVALID_VALUE;
     }
@@ -697,7 +763,7 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
         return rc;
     }
     if ((rc = launch_reduce10(w.partial10, g2t_offsets, g2t_tile_ids, num_gaussians, G, tile_x_begin, tile_x_end,
-                              grad_means3d, grad_covariances, grad_opacity, s)))
+                              grad_means3d, grad_covariances, grad_opacity, s, scales, rotations, grad_rotations)))
         return rc;
     if (C > 0 && num_gaussians > 0) {
         int B[3], nb[3];
@@ -797,6 +863,28 @@ int g2v_cosine_loss_backward(const float* grad_loss, const int32_t* count, int32
     return launch_cosine_loss_bwd(grad_loss, reinterpret_cast<const int*>(count), count_host, voxel_label, occ_mask,
                                   grid_feats, gt_feats, num_voxels, (int)channels, grad_grid_feats,
                                   static_cast<cudaStream_t>(stream));
+}
+
+int g2v_backward_sr(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                    const float* opacity, const float* scales, const float* rotations, const float* cov_inv,
+                    const float* features, int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                    const float voxel_range[6], const int dims[3], const int32_t* valid_voxel_lb,
+                    const int32_t* valid_voxel_ub, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids,
+                    int64_t num_pairs, int64_t num_block_pairs, const float* density, const float* grid_feats,
+                    float* grad_means3d, float* grad_scales, float* grad_rotations, float* grad_opacity,
+                    float* grad_features, int tile_x_begin, int tile_x_end, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+    if (num_gaussians > 0 && (!scales || !rotations)) {
+        g_msg[0] = 0;
+        set_error("g2v_backward_sr: scales and rotations are required");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    static const float kDummy = 0.f;  // non-NULL marker for the empty case
+    return backward_impl(grad_density, grad_grid_feats, means3d, opacity, cov_inv, features, num_gaussians, channels,
+                         voxel_size, voxel_range, dims, valid_voxel_lb, valid_voxel_ub, g2t_offsets, g2t_tile_ids,
+                         num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_scales, grad_opacity,
+                         grad_features, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream, false,
+                         scales ? scales : &kDummy, rotations ? rotations : &kDummy, grad_rotations);
 }
 
 }  // extern "C"

@@ -19,6 +19,7 @@
 //   reduce  per Gaussian, in CSR order: sums of the pair partials -> the output gradients.
 #include <algorithm>
 
+#include "g2v_cov.cuh"
 #include "g2v_internal.cuh"
 
 namespace g2v {
@@ -359,12 +360,18 @@ __global__ void __launch_bounds__(kThreads) fpass_kernel(
 }
 
 // Warp per Gaussian: sums the ten partials of its (Gaussian, tile) pairs whose tile lies in the slab.
+// kScaleRot: instead of dL/dSigma, write dL/dscales (n,3) into grad_cov and dL/dquats (n,4) into
+// grad_quats, by the chain rule through Sigma = R(q) diag(s)^2 R(q)^T (g2v_cov.cuh).
+template <bool kScaleRot>
 __global__ void __launch_bounds__(256) reduce10_kernel(const float* __restrict__ partial10,
                                                        const int32_t* __restrict__ g2t_offsets,
                                                        const int32_t* __restrict__ g2t_tile_ids, int64_t n,
                                                        int tyz, int tx_begin, int tx_end,
                                                        float* __restrict__ grad_means, float* __restrict__ grad_cov,
-                                                       float* __restrict__ grad_opacity) {
+                                                       float* __restrict__ grad_opacity,
+                                                       const float* __restrict__ scales,
+                                                       const float* __restrict__ quats,
+                                                       float* __restrict__ grad_quats) {
     const int64_t g = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (g >= n) return;
@@ -386,10 +393,20 @@ __global__ void __launch_bounds__(256) reduce10_kernel(const float* __restrict__
         grad_means[g * 3 + 0] = s[0];
         grad_means[g * 3 + 1] = s[1];
         grad_means[g * 3 + 2] = s[2];
-        float* o = grad_cov + g * 9;
-        o[0] = s[3]; o[1] = s[6]; o[2] = s[7];
-        o[3] = s[6]; o[4] = s[4]; o[5] = s[8];
-        o[6] = s[7]; o[7] = s[8]; o[8] = s[5];
+        const float Gc[9] = {s[3], s[6], s[7], s[6], s[4], s[8], s[7], s[8], s[5]};
+        if (kScaleRot) {
+            const float sc[3] = {scales[g * 3 + 0], scales[g * 3 + 1], scales[g * 3 + 2]};
+            const float q[4] = {quats[g * 4 + 0], quats[g * 4 + 1], quats[g * 4 + 2], quats[g * 4 + 3]};
+            float gs[3], gq[4];
+            scale_rot_grad(sc, q, Gc, gs, gq);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) grad_cov[g * 3 + k] = gs[k];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) grad_quats[g * 4 + k] = gq[k];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 9; ++k) grad_cov[g * 9 + k] = Gc[k];
+        }
         grad_opacity[g] = s[9];
     }
 }
@@ -509,11 +526,22 @@ int launch_fpass(const float* grad_feats, const float* means, const float* opaci
 
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
                     const Grid& G, int tx_begin, int tx_end, float* grad_means, float* grad_cov,
-                    float* grad_opacity, cudaStream_t s) {
+                    float* grad_opacity, cudaStream_t s, const float* scales, const float* quats,
+                    float* grad_quats) {
     if (n == 0) return 0;
     const unsigned blocks = (unsigned)((n * 32 + 255) / 256);
-    G2V_TIMED("reduce10_kernel", s, reduce10_kernel<<<blocks, 256, 0, s>>>(partial10, g2t_offsets, g2t_tile_ids, n, G.tiles[1] * G.tiles[2],
-                                           tx_begin, tx_end, grad_means, grad_cov, grad_opacity));
+    if (scales)
+        G2V_TIMED("reduce10_kernel", s,
+                  (reduce10_kernel<true><<<blocks, 256, 0, s>>>(partial10, g2t_offsets, g2t_tile_ids, n,
+                                                                G.tiles[1] * G.tiles[2], tx_begin, tx_end,
+                                                                grad_means, grad_cov, grad_opacity, scales, quats,
+                                                                grad_quats)));
+    else
+        G2V_TIMED("reduce10_kernel", s,
+                  (reduce10_kernel<false><<<blocks, 256, 0, s>>>(partial10, g2t_offsets, g2t_tile_ids, n,
+                                                                 G.tiles[1] * G.tiles[2], tx_begin, tx_end,
+                                                                 grad_means, grad_cov, grad_opacity, nullptr,
+                                                                 nullptr, nullptr)));
     G2V_LAUNCH_CHECK("reduce10_kernel");
     return 0;
 }

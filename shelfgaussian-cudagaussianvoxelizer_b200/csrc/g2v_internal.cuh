@@ -106,8 +106,10 @@ int cuda_fail(cudaError_t e, const char* what);
 
 // ---------------------------------------------------------------------------------------------
 // Launchers implemented in the .cu files (all return a g2v_status code).
+// scales / quats non-NULL: the covariance is formed from them in the kernel (cov unused).
 int launch_prepare_boxes(const float* means, const float* cov, int64_t n, const Grid& G, float* cov_inv,
-                         int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s);
+                         int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s,
+                         const float* scales = nullptr, const float* quats = nullptr);
 
 size_t scan_workspace_bytes(int64_t n);
 // Exclusive prefix sum of n int32 counts into out[0..n] (out[n] = total).  Fails with

@@ -5,6 +5,7 @@
 // those depend on the rounding of sqrtf and '/' under that flag; using the same source-level
 // operations under the same flags yields the same instructions.  The inverse uses the IEEE reciprocal
 // intrinsic, so it is not affected by the flag.
+#include "g2v_cov.cuh"
 #include "g2v_internal.cuh"
 
 namespace g2v {
@@ -14,16 +15,28 @@ namespace g2v {
 // to the grid; an empty box gives lb = 0, ub = -1, zero counts and a zero inverse.  The tile count is
 // the size of the tile box (voxel box / 4).  The inverse is the adjugate over the determinant, with
 // |det| < 1e-6 replaced by +1e-6 (the reference's clamp, cu:201-220).
+// kScaleRot: the covariance is formed in registers from scales (n,3) and rotation quaternions (n,4)
+// (g2v_cov.cuh, the same bits as cov_from_scale_rot_kernel), `cov` is unused and `scales` / `quats` are
+// read instead.
+template <bool kScaleRot>
 __global__ void __launch_bounds__(256) prepare_boxes_kernel(const float* __restrict__ means,
-                                                            const float* __restrict__ cov, int64_t n, Grid G,
+                                                            const float* __restrict__ cov,
+                                                            const float* __restrict__ scales,
+                                                            const float* __restrict__ quats, int64_t n, Grid G,
                                                             float* __restrict__ cov_inv, int32_t* __restrict__ lb,
                                                             int32_t* __restrict__ ub, int32_t* __restrict__ nvox,
                                                             int32_t* __restrict__ ntiles) {
     const int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (g >= n) return;
     float A[9];
+    if (kScaleRot) {
+        const float sc[3] = {scales[g * 3 + 0], scales[g * 3 + 1], scales[g * 3 + 2]};
+        const float q[4] = {quats[g * 4 + 0], quats[g * 4 + 1], quats[g * 4 + 2], quats[g * 4 + 3]};
+        scale_rot_to_cov(sc, q, A);
+    } else {
 #pragma unroll
-    for (int k = 0; k < 9; ++k) A[k] = cov[g * 9 + k];
+        for (int k = 0; k < 9; ++k) A[k] = cov[g * 9 + k];
+    }
 
     int lo[3], hi[3];
 #pragma unroll
@@ -86,12 +99,19 @@ __global__ void __launch_bounds__(256) prepare_boxes_kernel(const float* __restr
 }
 
 int launch_prepare_boxes(const float* means, const float* cov, int64_t n, const Grid& G, float* cov_inv,
-                         int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s) {
+                         int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s,
+                         const float* scales, const float* quats) {
     if (n == 0) return 0;
     const int threads = 256;
     const int64_t blocks = (n + threads - 1) / threads;
-    G2V_TIMED("prepare_boxes_kernel", s, prepare_boxes_kernel<<<(unsigned)blocks, threads, 0, s>>>(means, cov, n, G, cov_inv, lb, ub, num_voxels,
-                                                              num_tiles));
+    if (scales)
+        G2V_TIMED("prepare_boxes_kernel", s,
+                  (prepare_boxes_kernel<true><<<(unsigned)blocks, threads, 0, s>>>(
+                      means, nullptr, scales, quats, n, G, cov_inv, lb, ub, num_voxels, num_tiles)));
+    else
+        G2V_TIMED("prepare_boxes_kernel", s,
+                  (prepare_boxes_kernel<false><<<(unsigned)blocks, threads, 0, s>>>(
+                      means, cov, nullptr, nullptr, n, G, cov_inv, lb, ub, num_voxels, num_tiles)));
     G2V_LAUNCH_CHECK("prepare_boxes_kernel");
     return 0;
 }
