@@ -506,6 +506,128 @@ def run_single_scene(args, rank, world, dev):
     }
 
 
+def run_batched(args, rank, world, dev):
+    """--scenes B: every step splats B scenes of the config (independent seeds) through ONE batched call
+    (PyCudaGaussianVoxelizer with scene_sizes: one preparation + synchronisation, one splat, one
+    backward for the batch), against the same B scenes as B single-scene calls (`loop_ms_per_step`).
+    `value` is the batched step; per-rank work is fixed (weak scaling over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer, _C, _lib
+
+    cfg = CONFIGS[args.config]
+    B = args.scenes
+    scenes = [make_inputs(cfg, seed=args.seed + rank * B + b) for b in range(B)]
+    size, rng = scenes[0][0], scenes[0][1]
+    (X, Y, Z), tiles = _C.grid_shape(size, rng)
+    V = X * Y * Z
+    n, c = cfg["n"], cfg["c"]
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gD = torch.randn((B, X, Y, Z), device=dev, generator=g)
+    gF = torch.randn((B, X, Y, Z, c), device=dev, generator=g)
+    host_in = [torch.cat([sc[2 + k] for sc in scenes]) for k in range(4)]
+    leaves = [t.to(dev).requires_grad_() for t in host_in]
+    sizes = [n] * B
+    vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+
+    def step():
+        density, grid_feats, _ = vox(*leaves, scene_sizes=sizes)
+        return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
+
+    per_scene = [[t[b * n:(b + 1) * n].detach().clone().requires_grad_() for t in leaves] for b in range(B)]
+
+    def loop_step():
+        out = []
+        for b in range(B):
+            density, grid_feats, _ = vox(*per_scene[b])
+            out.append(torch.autograd.grad([density, grid_feats], per_scene[b], [gD[b], gF[b]]))
+        return out
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    sampler = ClockSampler(gpu_id_for(dev.index))
+    ms = timed(step)
+    clocks = sampler.stop()
+    loop_ms = timed(loop_step)
+
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    launches = sum(v[1] for v in prof.values())
+    off, nsc = _C._scene_offsets(sizes, n * B, dev)
+    out, MB = _C._forward_impl(*[t.detach() for t in leaves[:3]], size, rng, leaves[3].detach(), False,
+                               scenes=(off, nsc))
+    M = int(out[7].numel())
+    del out
+    ntiles = tiles[0] * tiles[1] * tiles[2]
+    peak, peak_kind = load_peaks()
+    kname, (kms, kcount) = max(prof.items(), key=lambda kv: kv[1][0])
+    kbytes = algorithmic_bytes(kname, n * B, c, V * B, M, MB, ntiles * B)
+    avg_ms = kms / kcount
+    achieved = kbytes / (avg_ms * 1e-3) / 1e9 if kbytes else None
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": (achieved / peak) if achieved else None, "traffic": None,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": avg_ms,
+                "kernel_share": {k: round(v[0] / sum(x[0] for x in prof.values()), 4) for k, v in prof.items()}}
+    sb = step_bytes(n, c, V, M // B) * B
+
+    host = [t.pin_memory() for t in host_in]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+
+    def e2e_step():
+        ls = [t.to(dev, non_blocking=True).requires_grad_() for t in host]
+        density, grid_feats, _ = vox(*ls, scene_sizes=sizes)
+        grads = torch.autograd.grad([density, grid_feats], ls, [gD, gF])
+        return grads[0].reshape(-1)[:1].to("cpu").item()
+
+    e2e_ms = timed(e2e_step)
+    return {
+        "metric": METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference distributions)",
+        "config": {"workload": f"{args.config} x {B} scenes per rank in one batched call: N={n} Gaussians, C={c}, "
+                               f"{X}x{Y}x{Z} voxels per scene, fwd+bwd with randn upstream grads",
+                   "global_batch": B * world, "scenes_per_rank": B, "pairs_M": M, "block_pairs": MB,
+                   "l2": "inputs larger than L2", "parallelism": f"dp{world} x batched {B}"},
+        "per_scene_ms": round(ms / B, 4), "loop_ms_per_step": round(loop_ms, 4),
+        "batched_speedup_vs_loop": round(loop_ms / ms, 3),
+        "roofline": roofline,
+        "step_roofline": {"algorithmic_bytes": sb, "achieved_gbs": sb / (ms * 1e-3) / 1e9,
+                          "frac": sb / (ms * 1e-3) / 1e9 / peak},
+        "cpu_baseline": None,
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
 LOSS_METRIC = "feature cosine loss fwd+bwd ms/step over the voxel grid and % HBM roofline"
 
 
@@ -744,6 +866,8 @@ def main():
     ap.add_argument("--path", default="voxelizer", choices=["voxelizer", "loss"],
                     help="voxelizer: the G2V fwd+bwd step (default); loss: the feature cosine loss fwd+bwd")
     ap.add_argument("--loss-channels", type=int, default=0, help="channels of the loss workload (default: config C)")
+    ap.add_argument("--scenes", type=int, default=1,
+                    help="scenes per rank per step, splatted in one batched call (compared with a loop of calls)")
     ap.add_argument("--cov-input", default="cov", choices=["cov", "sr"],
                     help="voxelizer inputs: covariances (default) or scales + rotation quaternions")
     ap.add_argument("--single-scene", action="store_true",
@@ -774,7 +898,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     try:
-        run = run_loss if args.path == "loss" else (run_single_scene if args.single_scene else run_ours)
+        run = (run_loss if args.path == "loss" else run_single_scene if args.single_scene else
+               run_batched if args.scenes > 1 else run_ours)
         line = run(args, rank, world, dev)
         if rank == 0:
             print(json.dumps(line), flush=True)

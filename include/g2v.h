@@ -160,6 +160,29 @@ G2V_API int g2v_forward_prepare_plan(const float* means3d, const float* covarian
 G2V_API int g2v_forward_prepare_plan_workspace_size(int64_t num_gaussians, size_t* bytes);
 
 /*
+ * Batches of scenes in one call (no reference counterpart: GaussTR-style callers loop over the batch,
+ * one forward with its synchronisation per scene).  B scenes share voxel_size / voxel_range; scene b owns
+ * the Gaussians [scene_offsets[b], scene_offsets[b+1]) of the concatenated per-Gaussian arrays (ragged
+ * sizes; scene_offsets is a device int32 array of B+1 entries from 0 to num_gaussians) and voxel x rows
+ * [b X, (b+1) X) of the volume arrays, which are therefore (B, X, Y, Z) and (B, X, Y, Z, C).  Boxes
+ * are clamped to each Gaussian's own scene; valid_voxel_lb / ub and g2t_tile_ids are in the coordinates
+ * of this stacked grid (x + b X, tile id of the (B*X, Y, Z) grid), and every *_workspace_size / dims
+ * argument takes the stacked dims (B*X, Y, Z).  X must be a multiple of 4 when B > 1
+ * (G2V_ERROR_NOT_SUPPORTED otherwise).  Per scene the results are those of a single-scene call.
+ *
+ * g2v_forward_prepare_plan_batched: g2v_forward_prepare_plan for the batch -- covariances, or (when
+ * scales is non-NULL) scales + rotations as in g2v_forward_prepare_plan_sr; one synchronisation for the
+ * whole batch.
+ */
+G2V_API int g2v_forward_prepare_plan_batched(const float* means3d, const float* covariances, const float* scales,
+                                             const float* rotations, const int32_t* scene_offsets, int num_scenes,
+                                             int64_t num_gaussians, const float voxel_size[3],
+                                             const float voxel_range[6], float* cov_inv, int32_t* valid_voxel_lb,
+                                             int32_t* valid_voxel_ub, int32_t* num_voxels, int32_t* g2t_offsets,
+                                             int64_t channels, void* workspace, size_t workspace_bytes,
+                                             void* stream, int64_t* num_pairs, int64_t* num_block_pairs);
+
+/*
  * Covariances from per-Gaussian scales (N,3) and rotation quaternions (N,4, (r, x, y, z), any norm):
  * covariances (N,9) = R(q/|q|) diag(s)^2 R(q/|q|)^T, row-major.  Replaces the GaussTR front end that
  * feeds the voxelizer, get_covariance(scales, quat_to_rotmat(rotations)) (test/gaussian_voxelizer.py:
@@ -231,6 +254,33 @@ G2V_API int g2v_backward_sr(const float* grad_density, const float* grad_grid_fe
                             float* grad_means3d, float* grad_scales, float* grad_rotations, float* grad_opacity,
                             float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
                             size_t workspace_bytes, void* stream);
+
+/* g2v_forward_splat for a batch of num_scenes stacked scenes (see g2v_forward_prepare_plan_batched). */
+G2V_API int g2v_forward_splat_batched(int num_scenes, const float* means3d, const float* opacity,
+                                      const float* features, int64_t num_gaussians, int64_t channels,
+                                      const float voxel_size[3], const float voxel_range[6], const float* cov_inv,
+                                      const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub,
+                                      const int32_t* g2t_offsets, int64_t num_pairs, int32_t* g2t_tile_ids,
+                                      float* density, float* grid_feats, int tile_x_begin, int tile_x_end,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * g2v_backward for a batch of num_scenes stacked scenes; dims = (B*X, Y, Z).  With scales == NULL the
+ * covariance gradient goes to grad_covariances_or_scales (N,9) and grad_rotations is unused; with scales
+ * and rotations (the batch was prepared from them) grad_covariances_or_scales receives grad_scales (N,3)
+ * and grad_rotations (N,4), as in g2v_backward_sr.
+ */
+G2V_API int g2v_backward_batched(int num_scenes, const float* grad_density, const float* grad_grid_feats,
+                                 const float* means3d, const float* opacity, const float* scales,
+                                 const float* rotations, const float* cov_inv, const float* features,
+                                 int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                                 const float voxel_range[6], const int dims[3], const int32_t* valid_voxel_lb,
+                                 const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                                 const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                                 const float* density, const float* grid_feats, float* grad_means3d,
+                                 float* grad_covariances_or_scales, float* grad_rotations, float* grad_opacity,
+                                 float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /*
  * g2v_backward for one x-slab with slab-local volume arrays (grad_density, grad_grid_feats, density,

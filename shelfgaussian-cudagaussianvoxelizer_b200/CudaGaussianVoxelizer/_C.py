@@ -95,10 +95,23 @@ def _scale_rot_inputs(scales, rotations, n, dev):
     return scales.contiguous(), rotations.contiguous()
 
 
+def _scene_offsets(scene_sizes, n, dev):
+    """Device int32 offsets (B+1) of ragged scene sizes (a list of ints or a 1-D integer tensor)."""
+    sizes = [int(v) for v in (scene_sizes.tolist() if isinstance(scene_sizes, torch.Tensor) else scene_sizes)]
+    if not sizes or any(v < 0 for v in sizes) or sum(sizes) != n:
+        raise RuntimeError(f"scene_sizes must be non-negative and sum to the {n} Gaussians, got {sizes}")
+    off = [0]
+    for v in sizes:
+        off.append(off[-1] + v)
+    return torch.tensor(off, dtype=torch.int32).to(dev, non_blocking=True), len(sizes)
+
+
 def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False,
-                  plan=False, scale_rot=None):
+                  plan=False, scale_rot=None, scenes=None):
     """The forward; ``scale_rot=(scales, rotations)`` replaces ``covariances`` (then ``plan`` is implied and
-    the covariances are formed inside the preparation kernel)."""
+    the covariances are formed inside the preparation kernel).  ``scenes=(scene_offsets (B+1) device int32,
+    B)``: the Gaussians are a ragged batch of B scenes, splatted in one call into (B, X, Y, Z[, C]) volumes
+    (boxes and tile ids in the coordinates of the scenes stacked along x; ``plan`` implied)."""
     lib = _lib.load()
     size_h = _host_values(voxel_size, 3, "voxel_size")
     range_h = _host_values(voxel_range, 6, "voxel_range")
@@ -125,6 +138,13 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
     if covariances is not None:
         covariances = covariances.contiguous()
     (X, Y, Z), _ = _lib.grid_shape(size_h, range_h)
+    nsc = 1
+    if scenes is not None:
+        plan = True
+        scene_off, nsc = scenes
+        if keep_t2g:
+            raise RuntimeError("t2g maps are not exposed for batched scenes")
+    XS = X * nsc  # x rows of the stacked volume arrays
     i32 = dict(dtype=torch.int32, device=dev)
     f32 = dict(dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
@@ -149,7 +169,14 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
             ev0.record(stream)
         m = ctypes.c_int64()
         mb = ctypes.c_int64()
-        if scale_rot is not None:  # covariances formed in the preparation kernel
+        if scenes is not None:
+            _lib.check(lib.g2v_forward_prepare_plan_batched(
+                _ptr(means3D), _ptr(covariances) if scale_rot is None else None,
+                _ptr(scales) if scale_rot is not None else None, _ptr(rotations) if scale_rot is not None else None,
+                _ptr(scene_off), nsc, n, _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub),
+                _ptr(nvox), _ptr(g2t_offsets), c, _ptr(ws1), ws1.numel(), sptr, ctypes.byref(m), ctypes.byref(mb)),
+                "g2v_forward_prepare_plan_batched")
+        elif scale_rot is not None:  # covariances formed in the preparation kernel
             _lib.check(lib.g2v_forward_prepare_plan_sr(_ptr(means3D), _ptr(scales), _ptr(rotations), n,
                                                        _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb),
                                                        _ptr(ub), _ptr(nvox), _ptr(g2t_offsets), c, _ptr(ws1),
@@ -167,15 +194,25 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
                        "g2v_forward_prepare")
         m = int(m.value)
         g2t_tile_ids = torch.empty((m,), **i32)
-        density = torch.empty((X, Y, Z), **f32)
-        grid_feats = torch.empty((X, Y, Z, c), **f32)
-        _lib.check(lib.g2v_forward_splat_workspace_size(n, m, _lib.i3((X, Y, Z)), c, ctypes.byref(nbytes)),
+        vshape = (X, Y, Z) if scenes is None else (nsc, X, Y, Z)
+        density = torch.empty(vshape, **f32)
+        grid_feats = torch.empty(vshape + (c,), **f32)
+        _lib.check(lib.g2v_forward_splat_workspace_size(n, m, _lib.i3((XS, Y, Z)), c, ctypes.byref(nbytes)),
                    "g2v_forward_splat_workspace_size")
         ws2 = _workspace(nbytes.value, dev)
-        _lib.check(lib.g2v_forward_splat(_ptr(means3D), _ptr(opacity), _features_ptr(features, density),
-                                         n, c, _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub),
-                                         _ptr(g2t_offsets), m, _ptr(g2t_tile_ids), _ptr(density), _ptr(grid_feats),
-                                         0, 0, _ptr(ws2), ws2.numel(), sptr), "g2v_forward_splat")
+        if scenes is not None:
+            _lib.check(lib.g2v_forward_splat_batched(nsc, _ptr(means3D), _ptr(opacity),
+                                                     _features_ptr(features, density), n, c, _lib.f3(size_h),
+                                                     _lib.f6(range_h), _ptr(cov_inv), _ptr(lb), _ptr(ub),
+                                                     _ptr(g2t_offsets), m, _ptr(g2t_tile_ids), _ptr(density),
+                                                     _ptr(grid_feats), 0, 0, _ptr(ws2), ws2.numel(), sptr),
+                       "g2v_forward_splat_batched")
+        else:
+            _lib.check(lib.g2v_forward_splat(_ptr(means3D), _ptr(opacity), _features_ptr(features, density),
+                                             n, c, _lib.f3(size_h), _lib.f6(range_h), _ptr(cov_inv), _ptr(lb),
+                                             _ptr(ub), _ptr(g2t_offsets), m, _ptr(g2t_tile_ids), _ptr(density),
+                                             _ptr(grid_feats), 0, 0, _ptr(ws2), ws2.numel(), sptr),
+                       "g2v_forward_splat")
         sec = 0.0
         if timing:
             ev1.record(stream)
@@ -231,7 +268,8 @@ def backward_plan(valid_voxel_lb, valid_voxel_ub, dims, channels) -> int:
 def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity, cov_inv, voxel_size, voxel_range,
                                 valid_voxel_lb, valid_voxel_ub, num_voxels_per_gaussian, g2t_offsets, g2t_tile_ids,
                                 density, grid_feats, features=None, *, timing: bool = True,
-                                num_block_pairs: int | None = None, tile_x_range=None, scale_rot=None):
+                                num_block_pairs: int | None = None, tile_x_range=None, scale_rot=None,
+                                num_scenes: int = 1):
     """Backward of the G2V splat (reference src/bindings.cpp:30-64, cu:1920-2057).
 
     Returns ``(grad_means3D (N,3), grad_cov (N,9), grad_opacity (N,), grad_feats (N,C), bwd_sec)``;
@@ -241,6 +279,8 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
     ``scale_rot=(scales (N,3), rotations (N,4))``: the Gaussians' covariances came from them; the second
     output is then the pair ``(grad_scales (N,3), grad_rotations (N,4))`` in place of grad_cov (the chain
     rule runs inside the gradient reduction).
+    ``num_scenes=B``: the state of a batched forward; grad_output / density are (B, X, Y, Z) and
+    grad_feats_output / grid_feats (B, X, Y, Z, C).
     """
     lib = _lib.load()
     dev = means3D.device
@@ -261,11 +301,14 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
         _need_contig(features, "features", torch.float32, dev)
         c = int(features.shape[1])
         _need_contig(grad_feats_output, "grad_feats_output", torch.float32, dev)
-    dims = tuple(int(s) for s in grad_output.shape)
-    if len(dims) != 3 or tuple(density.shape) != dims:
-        raise RuntimeError("grad_output and density must be (X,Y,Z)")
-    if c > 0 and tuple(grad_feats_output.shape) != dims + (c,):
-        raise RuntimeError(f"grad_feats_output must be {dims + (c,)}")
+    vdims = tuple(int(s) for s in grad_output.shape)
+    if tuple(density.shape) != vdims or len(vdims) != (3 if num_scenes == 1 else 4) or (
+            num_scenes > 1 and vdims[0] != num_scenes):
+        raise RuntimeError("grad_output and density must be (X,Y,Z)" if num_scenes == 1 else
+                           f"grad_output and density must be ({num_scenes},X,Y,Z)")
+    if c > 0 and tuple(grad_feats_output.shape) != vdims + (c,):
+        raise RuntimeError(f"grad_feats_output must be {vdims + (c,)}")
+    dims = vdims if num_scenes == 1 else (vdims[0] * vdims[1], vdims[2], vdims[3])  # stacked along x
     m = g2t_tile_ids.numel()
     f32 = dict(dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
@@ -292,7 +335,16 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record(stream)
         fptr = _features_ptr(features, grad_op if grad_op.numel() else density)
-        if scale_rot is not None:
+        if num_scenes > 1:
+            sr = scale_rot is not None
+            _lib.check(lib.g2v_backward_batched(
+                num_scenes, _ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None, _ptr(means3D),
+                _ptr(opacity), _ptr(scales) if sr else None, _ptr(rotations) if sr else None, _ptr(cov_inv), fptr, n,
+                c, _lib.f3(size_h), _lib.f6(range_h), _lib.i3(dims), _ptr(valid_voxel_lb), _ptr(valid_voxel_ub),
+                _ptr(g2t_offsets), _ptr(g2t_tile_ids), m, int(num_block_pairs), _ptr(density), _ptr(grid_feats),
+                _ptr(grad_means), _ptr(grad_cov), _ptr(grad_rot) if sr else None, _ptr(grad_op), _ptr(grad_feats),
+                tb, te, _ptr(ws), ws.numel(), sptr), "g2v_backward_batched")
+        elif scale_rot is not None:
             _lib.check(lib.g2v_backward_sr(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None,
                                            _ptr(means3D), _ptr(opacity), _ptr(scales), _ptr(rotations), _ptr(cov_inv),
                                            fptr, n, c, _lib.f3(size_h), _lib.f6(range_h), _lib.i3(dims),

@@ -30,11 +30,12 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
     """Autograd function of the splat (reference CudaGaussianVoxelizer/__init__.py:10-47)."""
 
     @staticmethod
-    def forward(ctx, means3D, opacity, covariances, voxel_size, voxel_range, features, timing=True):
+    def forward(ctx, means3D, opacity, covariances, voxel_size, voxel_range, features, timing=True, scenes=None):
         # the forward also counts the backward's (Gaussian, block) pairs in its one synchronisation
         ((density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, fwd_sec),
          num_block_pairs) = _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing,
-                                          plan=True)
+                                          plan=True, scenes=scenes)
+        ctx.num_scenes = 1 if scenes is None else scenes[1]
         stats = torch.zeros(2, dtype=torch.float32, device="cpu")
         stats[0] = fwd_sec
         ctx.save_for_backward(means3D, opacity, voxel_size, voxel_range, cov_inv, lb, ub, nvox, g2t_offsets,
@@ -55,9 +56,10 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
             gfeat = grad_feats_output
         grad_means, grad_cov, grad_op, grad_feats, bwd_sec = gaussian_voxelizer_backward(
             gout, gfeat, means3D, opacity, cov_inv, voxel_size, voxel_range, lb, ub, nvox, g2t_offsets,
-            g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs)
+            g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs,
+            num_scenes=ctx.num_scenes)
         stats[1] = bwd_sec
-        return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None)
+        return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None, None)
 
 
 class _CudaGaussianVoxelizeSRFunction(torch.autograd.Function):
@@ -68,10 +70,12 @@ class _CudaGaussianVoxelizeSRFunction(torch.autograd.Function):
     voxelizer with GaussTR's get_covariance / quat_to_rotmat, test/gaussian_voxelizer.py:14-37)."""
 
     @staticmethod
-    def forward(ctx, means3D, opacity, scales, rotations, voxel_size, voxel_range, features, timing=True):
+    def forward(ctx, means3D, opacity, scales, rotations, voxel_size, voxel_range, features, timing=True,
+                scenes=None):
         ((density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, fwd_sec),
          num_block_pairs) = _forward_impl(means3D, opacity, None, voxel_size, voxel_range, features, timing,
-                                          scale_rot=(scales, rotations))
+                                          scale_rot=(scales, rotations), scenes=scenes)
+        ctx.num_scenes = 1 if scenes is None else scenes[1]
         stats = torch.zeros(2, dtype=torch.float32, device="cpu")
         stats[0] = fwd_sec
         ctx.save_for_backward(means3D, opacity, scales, rotations, voxel_size, voxel_range, cov_inv, lb, ub, nvox,
@@ -93,10 +97,10 @@ class _CudaGaussianVoxelizeSRFunction(torch.autograd.Function):
         grad_means, (grad_scales, grad_rot), grad_op, grad_feats, bwd_sec = gaussian_voxelizer_backward(
             gout, gfeat, means3D, opacity, cov_inv, voxel_size, voxel_range, lb, ub, nvox, g2t_offsets,
             g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs,
-            scale_rot=(scales, rotations))
+            scale_rot=(scales, rotations), num_scenes=ctx.num_scenes)
         stats[1] = bwd_sec
         return (grad_means, grad_op, grad_scales, grad_rot, None, None,
-                grad_feats if features is not None else None, None)
+                grad_feats if features is not None else None, None, None)
 
 
 class _CovarianceFromScaleRot(torch.autograd.Function):
@@ -140,19 +144,36 @@ class PyCudaGaussianVoxelizer(nn.Module):
         _C._host_values(self.voxel_size, 3, "voxel_size")
         _C._host_values(self.voxel_range, 6, "voxel_range")
 
-    def forward(self, means3D, opacity, covariances=None, features=None, *, scales=None, rotations=None):
+    def forward(self, means3D, opacity, covariances=None, features=None, *, scales=None, rotations=None,
+                scene_sizes=None):
         """``covariances`` (N,9) as in the reference, or -- in its place -- ``scales`` (N,3) and
         ``rotations`` (N,4) quaternions (r, x, y, z), as GaussTR's voxelizer accepts them
-        (test/gaussian_voxelizer.py:168-177); gradients then flow to scales and rotations."""
+        (test/gaussian_voxelizer.py:168-177); gradients then flow to scales and rotations.
+
+        Batches of scenes splat in one call: either a leading batch dimension on every per-Gaussian input
+        (means3D (B,N,3), opacity (B,N), covariances (B,N,9) or (B,N,3,3), features (B,N,C), scales (B,N,3),
+        rotations (B,N,4)), or the scenes' Gaussians concatenated along N with ``scene_sizes`` (B counts,
+        ragged).  The outputs are then (B,X,Y,Z) and (B,X,Y,Z,C); each scene's result is that of a
+        single-scene call.  X must be a multiple of 4 for B > 1."""
+        scenes = None
+        if means3D.dim() == 3:  # (B, N, ...) equal-size batch
+            b, n = means3D.shape[:2]
+            flat = lambda t, k: None if t is None else t.reshape(b * n, *k)  # noqa: E731
+            means3D, opacity = flat(means3D, (3,)), flat(opacity, ())
+            covariances, scales, rotations = flat(covariances, (9,)), flat(scales, (3,)), flat(rotations, (4,))
+            features = None if features is None else features.reshape(b * n, features.shape[-1])
+            scene_sizes = [n] * b
+        if scene_sizes is not None:
+            scenes = _C._scene_offsets(scene_sizes, means3D.shape[0], means3D.device)
         if covariances is None:
             if scales is None or rotations is None:
                 raise RuntimeError("PyCudaGaussianVoxelizer: pass covariances, or scales and rotations")
             return _CudaGaussianVoxelizeSRFunction.apply(means3D, opacity, scales, rotations, self.voxel_size,
-                                                         self.voxel_range, features, self.timing)
+                                                         self.voxel_range, features, self.timing, scenes)
         if scales is not None or rotations is not None:
             raise RuntimeError("PyCudaGaussianVoxelizer: pass covariances or scales/rotations, not both")
         return _CudaGaussianVoxelizeFunction.apply(means3D, opacity, covariances, self.voxel_size, self.voxel_range,
-                                                   features, self.timing)
+                                                   features, self.timing, scenes)
 
 
 class _CudaFeatsCosinelossFunction(torch.autograd.Function):

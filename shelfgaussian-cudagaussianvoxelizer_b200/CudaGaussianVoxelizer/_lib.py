@@ -34,6 +34,12 @@ SIGNATURES = {
                                        ctypes.POINTER(I64)]),
     "g2v_forward_prepare_plan_sr": (I32, [P, P, P, I64, F3, F6, P, P, P, P, P, I64, P, SZ, P, ctypes.POINTER(I64),
                                           ctypes.POINTER(I64)]),
+    "g2v_forward_prepare_plan_batched": (I32, [P, P, P, P, P, I32, I64, F3, F6, P, P, P, P, P, I64, P, SZ, P,
+                                               ctypes.POINTER(I64), ctypes.POINTER(I64)]),
+    "g2v_forward_splat_batched": (I32, [I32, P, P, P, I64, I64, F3, F6, P, P, P, P, I64, P, P, P, I32, I32, P, SZ,
+                                        P]),
+    "g2v_backward_batched": (I32, [I32, P, P, P, P, P, P, P, P, I64, I64, F3, F6, I3, P, P, P, P, I64, I64, P, P, P,
+                                   P, P, P, P, I32, I32, P, SZ, P]),
     "g2v_covariance_from_scale_rot": (I32, [P, P, I64, P, P]),
     "g2v_covariance_from_scale_rot_backward": (I32, [P, P, P, I64, P, P, P]),
     "g2v_forward_splat_workspace_size": (I32, [I64, I64, I3, I64, ctypes.POINTER(SZ)]),

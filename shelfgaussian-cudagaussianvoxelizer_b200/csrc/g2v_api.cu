@@ -153,12 +153,40 @@ int make_grid(const float size[3], const float range[6], Grid& G) {
     }
     G.xoff = 0;
     G.xlen = G.dims[0];
+    G.scene_x = 0;
     const int64_t ntiles = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
     const int64_t nvox = (int64_t)G.dims[0] * G.dims[1] * G.dims[2];
     if (ntiles > INT32_MAX / 2 || nvox > ((int64_t)1 << 40)) {
         set_error("voxel grid %dx%dx%d is too large", G.dims[0], G.dims[1], G.dims[2]);
         return G2V_ERROR_SIZE_LIMIT;
     }
+    return 0;
+}
+
+// A batch of num_scenes scenes of the same grid stacked along x: scene b occupies voxel x rows
+// [b X, (b+1) X) of the volume arrays, i.e. the arrays are (B, X, Y, Z[, C]).  Tiles must not straddle
+// scenes, so X must be a multiple of the tile edge.
+int stack_scenes(Grid& G, int num_scenes) {
+    if (num_scenes < 1) {
+        set_error("num_scenes must be >= 1, got %d", num_scenes);
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    if (num_scenes == 1) return 0;
+    if (G.dims[0] % kTile != 0) {
+        set_error("a batch of scenes needs the grid's X (%d) to be a multiple of %d", G.dims[0], kTile);
+        return G2V_ERROR_NOT_SUPPORTED;
+    }
+    const int64_t X = (int64_t)G.dims[0] * num_scenes;
+    const int64_t ntiles = (X / kTile) * G.tiles[1] * G.tiles[2];
+    if (X > INT32_MAX / 2 || ntiles > INT32_MAX / 2 || X * G.dims[1] * G.dims[2] > ((int64_t)1 << 40)) {
+        set_error("a batch of %d scenes of %dx%dx%d voxels is too large", num_scenes, G.dims[0], G.dims[1],
+                  G.dims[2]);
+        return G2V_ERROR_SIZE_LIMIT;
+    }
+    G.scene_x = G.dims[0];
+    G.dims[0] = (int)X;
+    G.tiles[0] = (int)(X / kTile);
+    G.xlen = G.dims[0];
     return 0;
 }
 
@@ -386,11 +414,13 @@ static int forward_splat_impl(const float* means3d, const float* opacity, const 
                               const float voxel_range[6], const float* cov_inv, const int32_t* valid_voxel_lb,
                               const int32_t* valid_voxel_ub, const int32_t* g2t_offsets, int64_t num_pairs,
                               int32_t* g2t_tile_ids, float* density, float* grid_feats, int tile_x_begin,
-                              int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local) {
+                              int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local,
+                              int num_scenes = 1) {
     g_msg[0] = 0;
     Grid G;
     int rc = make_grid(voxel_size, voxel_range, G);
     if (rc) return rc;
+    if ((rc = stack_scenes(G, num_scenes))) return rc;
     if ((rc = check_slab(G, tile_x_begin, tile_x_end))) return rc;
     if (local) set_slab_local(G, tile_x_begin, tile_x_end);
     const int C = features ? (int)channels : 0;
@@ -580,11 +610,17 @@ static int prepare_plan_impl(const float* means3d, const float* covariances, con
                              const float voxel_range[6], float* cov_inv, int32_t* valid_voxel_lb,
                              int32_t* valid_voxel_ub, int32_t* num_voxels, int32_t* g2t_offsets, int64_t channels,
                              void* workspace, size_t workspace_bytes, void* stream, int64_t* num_pairs,
-                             int64_t* num_block_pairs) {
+                             int64_t* num_block_pairs, const int32_t* scene_offsets = nullptr,
+                             int num_scenes = 1) {
     g_msg[0] = 0;
     Grid G;
     int rc = make_grid(voxel_size, voxel_range, G);
     if (rc) return rc;
+    if ((rc = stack_scenes(G, num_scenes))) return rc;
+    if (num_scenes > 1 && !scene_offsets) {
+        set_error("g2v_forward_prepare_plan_batched: scene_offsets is required for %d scenes", num_scenes);
+        return G2V_ERROR_INVALID_VALUE;
+    }
     const bool have_cov = scales ? rotations != nullptr : covariances != nullptr;
     if (num_gaussians < 0 || num_gaussians > INT32_MAX - 1 || channels < 0 || !g2t_offsets || !num_pairs ||
         !num_block_pairs ||
@@ -603,7 +639,8 @@ static int prepare_plan_impl(const float* means3d, const float* covariances, con
     carve_plan(c.take<char>(carve_plan(nullptr, num_gaussians, wb)), num_gaussians, wb);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if ((rc = launch_prepare_boxes(means3d, covariances, num_gaussians, G, cov_inv, valid_voxel_lb, valid_voxel_ub,
-                                   num_voxels, wp.ntiles, s, scales, rotations)))
+                                   num_voxels, wp.ntiles, s, scales, rotations, num_scenes > 1 ? scene_offsets : nullptr,
+                                   num_scenes)))
         return rc;
     if ((rc = launch_exclusive_scan(wp.ntiles, num_gaussians, g2t_offsets, wp.total, wp.scan, s))) return rc;
     const bool blocks = channels > 0 && num_gaussians > 0;
@@ -616,11 +653,21 @@ static int prepare_plan_impl(const float* means3d, const float* covariances, con
     }
     int64_t m = 0, mb = 0;
     int word = 0;
+    int32_t ends[2] = {0, (int32_t)num_gaussians};
     G2V_CUDA(cudaMemcpyAsync(&m, wp.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     if (blocks) G2V_CUDA(cudaMemcpyAsync(&mb, wb.total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    if (num_scenes > 1) {
+        G2V_CUDA(cudaMemcpyAsync(&ends[0], scene_offsets, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+        G2V_CUDA(cudaMemcpyAsync(&ends[1], scene_offsets + num_scenes, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    }
     if ((rc = queue_error_read(s, &word))) return rc;
     G2V_CUDA(cudaStreamSynchronize(s));
     if ((rc = report_device_error(word, s))) return rc;
+    if (ends[0] != 0 || ends[1] != (int32_t)num_gaussians) {
+        set_error("scene_offsets must run from 0 to num_gaussians (%lld), got %d .. %d", (long long)num_gaussians,
+                  ends[0], ends[1]);
+        return G2V_ERROR_INVALID_VALUE;
+    }
     if (m > INT32_MAX || mb > INT32_MAX) {
         set_error("%lld tile pairs / %lld block pairs exceed the int32 range of the CSR maps", (long long)m,
                   (long long)mb);
@@ -658,6 +705,26 @@ int g2v_forward_prepare_plan_sr(const float* means3d, const float* scales, const
                              num_gaussians, voxel_size, voxel_range, cov_inv, valid_voxel_lb, valid_voxel_ub,
                              num_voxels, g2t_offsets, channels, workspace, workspace_bytes, stream, num_pairs,
                              num_block_pairs);
+}
+
+int g2v_forward_prepare_plan_batched(const float* means3d, const float* covariances, const float* scales,
+                                     const float* rotations, const int32_t* scene_offsets, int num_scenes,
+                                     int64_t num_gaussians, const float voxel_size[3], const float voxel_range[6],
+                                     float* cov_inv, int32_t* valid_voxel_lb, int32_t* valid_voxel_ub,
+                                     int32_t* num_voxels, int32_t* g2t_offsets, int64_t channels, void* workspace,
+                                     size_t workspace_bytes, void* stream, int64_t* num_pairs,
+                                     int64_t* num_block_pairs) {
+    if (num_gaussians > 0 && (scales ? !rotations : !covariances)) {
+        g_msg[0] = 0;
+        set_error("g2v_forward_prepare_plan_batched: covariances, or scales and rotations, are required");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    static const float kDummy = 0.f;  // non-NULL marker for the empty case
+    const float* sc = scales ? scales : nullptr;
+    const float* cv = scales ? nullptr : (covariances ? covariances : &kDummy);
+    return prepare_plan_impl(means3d, cv, sc, scales ? rotations : nullptr, num_gaussians, voxel_size, voxel_range,
+                             cov_inv, valid_voxel_lb, valid_voxel_ub, num_voxels, g2t_offsets, channels, workspace,
+                             workspace_bytes, stream, num_pairs, num_block_pairs, scene_offsets, num_scenes);
 }
 
 int g2v_covariance_from_scale_rot(const float* scales, const float* rotations, int64_t num_gaussians,
@@ -709,12 +776,13 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
                          float* grad_covariances, float* grad_opacity, float* grad_features, int tile_x_begin,
                          int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local,
                          const float* scales = nullptr, const float* rotations = nullptr,
-                         float* grad_rotations = nullptr) {
+                         float* grad_rotations = nullptr, int num_scenes = 1) {
     (void)grid_feats;
     g_msg[0] = 0;
     Grid G;
     int rc = make_grid(voxel_size, voxel_range, G);
     if (rc) return rc;
+    if ((rc = stack_scenes(G, num_scenes))) return rc;
     if (!dims || dims[0] != G.dims[0] || dims[1] != G.dims[1] || dims[2] != G.dims[2]) {
         set_error("g2v_backward: dims do not match the voxel grid %dx%dx%d", G.dims[0], G.dims[1], G.dims[2]);
         return G2V_ERROR_INVALID_VALUE;
@@ -863,6 +931,41 @@ int g2v_cosine_loss_backward(const float* grad_loss, const int32_t* count, int32
     return launch_cosine_loss_bwd(grad_loss, reinterpret_cast<const int*>(count), count_host, voxel_label, occ_mask,
                                   grid_feats, gt_feats, num_voxels, (int)channels, grad_grid_feats,
                                   static_cast<cudaStream_t>(stream));
+}
+
+int g2v_forward_splat_batched(int num_scenes, const float* means3d, const float* opacity, const float* features,
+                              int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                              const float voxel_range[6], const float* cov_inv, const int32_t* valid_voxel_lb,
+                              const int32_t* valid_voxel_ub, const int32_t* g2t_offsets, int64_t num_pairs,
+                              int32_t* g2t_tile_ids, float* density, float* grid_feats, int tile_x_begin,
+                              int tile_x_end, void* workspace, size_t workspace_bytes, void* stream) {
+    return forward_splat_impl(means3d, opacity, features, num_gaussians, channels, voxel_size, voxel_range, cov_inv,
+                              valid_voxel_lb, valid_voxel_ub, g2t_offsets, num_pairs, g2t_tile_ids, density,
+                              grid_feats, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream, false,
+                              num_scenes);
+}
+
+int g2v_backward_batched(int num_scenes, const float* grad_density, const float* grad_grid_feats,
+                         const float* means3d, const float* opacity, const float* scales, const float* rotations,
+                         const float* cov_inv, const float* features, int64_t num_gaussians, int64_t channels,
+                         const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                         const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                         const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                         const float* density, const float* grid_feats, float* grad_means3d,
+                         float* grad_covariances_or_scales, float* grad_rotations, float* grad_opacity,
+                         float* grad_features, int tile_x_begin, int tile_x_end, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    if (num_gaussians > 0 && scales && !rotations) {
+        g_msg[0] = 0;
+        set_error("g2v_backward_batched: rotations are required with scales");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return backward_impl(grad_density, grad_grid_feats, means3d, opacity, cov_inv, features, num_gaussians, channels,
+                         voxel_size, voxel_range, dims, valid_voxel_lb, valid_voxel_ub, g2t_offsets, g2t_tile_ids,
+                         num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_covariances_or_scales,
+                         grad_opacity, grad_features, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream,
+                         false, scales, scales ? rotations : nullptr, scales ? grad_rotations : nullptr,
+                         num_scenes);
 }
 
 int g2v_backward_sr(const float* grad_density, const float* grad_grid_feats, const float* means3d,

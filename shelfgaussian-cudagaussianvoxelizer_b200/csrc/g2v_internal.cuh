@@ -22,6 +22,7 @@ struct Grid {
     int tiles[3];    // Tx, Ty, Tz tiles
     int xoff;        // voxel x of the first row of the volume arrays (0: the arrays cover the whole grid)
     int xlen;        // voxel x rows held by the volume arrays (dims[0] for whole-grid arrays)
+    int scene_x;     // scenes stacked along x: voxel x rows per scene (0: one scene); dims/tiles[0] cover all
 };
 
 // Row (voxel index) of voxel (x, y, z) in the volume arrays (density, grid_feats and their gradients).
@@ -29,8 +30,11 @@ __host__ __device__ __forceinline__ int64_t grid_row(const Grid& G, int x, int y
     return ((int64_t)(x - G.xoff) * G.dims[1] + y) * G.dims[2] + z;
 }
 
-// Voxel centre along one axis: origin + (i + 1/2) * h (reference cu:825-828).
+// Voxel centre along one axis: origin + (i + 1/2) * h (reference cu:825-828).  For a batch of scenes
+// stacked along x the index is first made scene-local (an integer step, so the centre is the same float
+// as in a single-scene call).
 __device__ __forceinline__ float voxel_centre(const Grid& G, int a, int i) {
+    if (a == 0 && G.scene_x > 0) i -= (i / G.scene_x) * G.scene_x;
     return G.r0[a] + (static_cast<float>(i) + 0.5f) * G.h[a];
 }
 
@@ -107,9 +111,13 @@ int cuda_fail(cudaError_t e, const char* what);
 // ---------------------------------------------------------------------------------------------
 // Launchers implemented in the .cu files (all return a g2v_status code).
 // scales / quats non-NULL: the covariance is formed from them in the kernel (cov unused).
+// scene_offsets (num_scenes + 1, int32) non-NULL: Gaussians [scene_offsets[b], scene_offsets[b+1]) belong
+// to scene b of a batch stacked along x (G.scene_x rows per scene); their boxes are clamped to the scene
+// and returned in stacked coordinates (x + b * scene_x).
 int launch_prepare_boxes(const float* means, const float* cov, int64_t n, const Grid& G, float* cov_inv,
                          int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s,
-                         const float* scales = nullptr, const float* quats = nullptr);
+                         const float* scales = nullptr, const float* quats = nullptr,
+                         const int32_t* scene_offsets = nullptr, int num_scenes = 1);
 
 size_t scan_workspace_bytes(int64_t n);
 // Exclusive prefix sum of n int32 counts into out[0..n] (out[n] = total).  Fails with

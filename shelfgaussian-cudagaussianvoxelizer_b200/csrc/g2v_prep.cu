@@ -25,9 +25,24 @@ __global__ void __launch_bounds__(256) prepare_boxes_kernel(const float* __restr
                                                             const float* __restrict__ quats, int64_t n, Grid G,
                                                             float* __restrict__ cov_inv, int32_t* __restrict__ lb,
                                                             int32_t* __restrict__ ub, int32_t* __restrict__ nvox,
-                                                            int32_t* __restrict__ ntiles) {
+                                                            int32_t* __restrict__ ntiles,
+                                                            const int32_t* __restrict__ scene_offsets,
+                                                            int num_scenes) {
     const int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (g >= n) return;
+    // scene of this Gaussian (last b with scene_offsets[b] <= g) and the scene's x extent
+    int scene = 0;
+    if (scene_offsets) {
+        int lo_b = 0, hi_b = num_scenes - 1;
+        while (lo_b < hi_b) {
+            const int mid = (lo_b + hi_b + 1) >> 1;
+            if (scene_offsets[mid] <= g) lo_b = mid;
+            else hi_b = mid - 1;
+        }
+        scene = lo_b;
+    }
+    const int dims_s[3] = {G.scene_x > 0 ? G.scene_x : G.dims[0], G.dims[1], G.dims[2]};
+    const int tiles_s[3] = {G.scene_x > 0 ? G.scene_x / kTile : G.tiles[0], G.tiles[1], G.tiles[2]};
     float A[9];
     if (kScaleRot) {
         const float sc[3] = {scales[g * 3 + 0], scales[g * 3 + 1], scales[g * 3 + 2]};
@@ -51,7 +66,7 @@ __global__ void __launch_bounds__(256) prepare_boxes_kernel(const float* __restr
         const int l = (int)floorf((lower - G.r0[a]) / G.h[a]);
         const int u = (int)floorf((upper - G.r0[a]) / G.h[a]);
         lo[a] = max(l, 0);
-        hi[a] = min(u, G.dims[a] - 1);
+        hi[a] = min(u, dims_s[a] - 1);
     }
     const bool empty = lo[0] > hi[0] || lo[1] > hi[1] || lo[2] > hi[2];
     if (empty) {
@@ -69,11 +84,12 @@ __global__ void __launch_bounds__(256) prepare_boxes_kernel(const float* __restr
     int tcount = 1, vcount = 1;
 #pragma unroll
     for (int a = 0; a < 3; ++a) {
-        lb[g * 3 + a] = lo[a];
-        ub[g * 3 + a] = hi[a];
+        const int shift = a == 0 ? scene * dims_s[0] : 0;  // stacked-batch coordinates
+        lb[g * 3 + a] = lo[a] + shift;
+        ub[g * 3 + a] = hi[a] + shift;
         vcount *= hi[a] - lo[a] + 1;
         const int tl = max(lo[a] / kTile, 0);
-        const int th = min(hi[a] / kTile, G.tiles[a] - 1);
+        const int th = min(hi[a] / kTile, tiles_s[a] - 1);
         tcount *= th - tl + 1;
     }
     nvox[g] = vcount;
@@ -100,18 +116,20 @@ __global__ void __launch_bounds__(256) prepare_boxes_kernel(const float* __restr
 
 int launch_prepare_boxes(const float* means, const float* cov, int64_t n, const Grid& G, float* cov_inv,
                          int32_t* lb, int32_t* ub, int32_t* num_voxels, int32_t* num_tiles, cudaStream_t s,
-                         const float* scales, const float* quats) {
+                         const float* scales, const float* quats, const int32_t* scene_offsets, int num_scenes) {
     if (n == 0) return 0;
     const int threads = 256;
     const int64_t blocks = (n + threads - 1) / threads;
     if (scales)
         G2V_TIMED("prepare_boxes_kernel", s,
                   (prepare_boxes_kernel<true><<<(unsigned)blocks, threads, 0, s>>>(
-                      means, nullptr, scales, quats, n, G, cov_inv, lb, ub, num_voxels, num_tiles)));
+                      means, nullptr, scales, quats, n, G, cov_inv, lb, ub, num_voxels, num_tiles, scene_offsets,
+                      num_scenes)));
     else
         G2V_TIMED("prepare_boxes_kernel", s,
                   (prepare_boxes_kernel<false><<<(unsigned)blocks, threads, 0, s>>>(
-                      means, cov, nullptr, nullptr, n, G, cov_inv, lb, ub, num_voxels, num_tiles)));
+                      means, cov, nullptr, nullptr, n, G, cov_inv, lb, ub, num_voxels, num_tiles, scene_offsets,
+                      num_scenes)));
     G2V_LAUNCH_CHECK("prepare_boxes_kernel");
     return 0;
 }

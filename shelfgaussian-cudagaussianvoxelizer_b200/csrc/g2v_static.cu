@@ -85,6 +85,9 @@ extern "C" int g2v_forward_prepare_static(const float* means3d, const float* cov
         G.dims[a] = static_cast<int>(q);
         G.tiles[a] = (G.dims[a] + kTile - 1) / kTile;
     }
+    G.xoff = 0;
+    G.xlen = G.dims[0];
+    G.scene_x = 0;
     void* base = nullptr;
     int rc = scratch_address(&base);
     if (rc) return rc;
