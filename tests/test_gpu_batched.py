@@ -121,7 +121,7 @@ def test_ragged_scale_rot_batch():
 
 def test_batch_needs_x_multiple_of_four_and_consistent_sizes():
     from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer
-    vox = PyCudaGaussianVoxelizer(voxel_size=[0.3] * 3, voxel_range=[-8.0, -8.0, -1.0, 7.9, 8.0, 5.4])
+    vox = PyCudaGaussianVoxelizer(voxel_size=[0.5] * 3, voxel_range=[-8.0, -8.0, -1.0, 8.5, 8.0, 5.0])  # X = 33
     m, o, cov, f = _scene(20, 4, seed=1)
     with pytest.raises(RuntimeError, match="multiple of 4"):
         vox(m, o, cov, f, scene_sizes=[10, 10])
