@@ -162,6 +162,8 @@ def run_ours(args, rank, world, dev):
     from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer, _C, _lib
 
     cfg = CONFIGS[args.config]
+    if args.density_only:
+        cfg = dict(cfg, c=0)
     size, rng, m_h, o_h, c_h, f_h = make_inputs(cfg, seed=args.seed + rank)
     (X, Y, Z), tiles = _C.grid_shape(size, rng)
     V = X * Y * Z
@@ -176,17 +178,31 @@ def run_ours(args, rank, world, dev):
         host_in = (m_h, o_h, s_h, q_h, f_h)
     else:
         host_in = (m_h, o_h, c_h, f_h)
+    if args.density_only:  # features=None: the density-only kernels
+        host_in = host_in[:-1]
     leaves = [t.to(dev).requires_grad_() for t in host_in]
-    vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+    if args.graph:
+        from CudaGaussianVoxelizer import GraphedGaussianVoxelizer
+        if sr:
+            raise SystemExit("--graph takes covariance inputs")
+        vox = GraphedGaussianVoxelizer(voxel_size=size, voxel_range=rng)
+    else:
+        vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
 
     def call(v, ls):
+        f = None if args.density_only else ls[-1]
         if sr:
-            return v(ls[0], ls[1], features=ls[4], scales=ls[2], rotations=ls[3])
-        return v(*ls)
+            return v(ls[0], ls[1], features=f, scales=ls[2], rotations=ls[3])
+        return v(ls[0], ls[1], ls[2], f)
+
+    def grads(density, grid_feats, ls):
+        if args.density_only:
+            return torch.autograd.grad([density], ls, [gD])
+        return torch.autograd.grad([density, grid_feats], ls, [gD, gF])
 
     def step():
         density, grid_feats, _ = call(vox, leaves)
-        return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
+        return grads(density, grid_feats, leaves)
 
     def barrier():
         if world > 1:
@@ -223,12 +239,12 @@ def run_ours(args, rank, world, dev):
     launches_per_step = sum(v[1] for v in prof.values()) / args.steps
 
     # sizes for the roofline
+    feat_d = None if args.density_only else leaves[-1].detach()
     if sr:
-        out = _C._forward_impl(leaves[0].detach(), leaves[1].detach(), None, size, rng, leaves[4].detach(), False,
+        out = _C._forward_impl(leaves[0].detach(), leaves[1].detach(), None, size, rng, feat_d, False,
                                scale_rot=(leaves[2].detach(), leaves[3].detach()))[0]
     else:
-        out = _C.gaussian_voxelizer_forward(*[t.detach() for t in leaves[:3]], size, rng, leaves[3].detach(),
-                                            timing=False)
+        out = _C.gaussian_voxelizer_forward(*[t.detach() for t in leaves[:3]], size, rng, feat_d, timing=False)
     M = int(out[7].numel())
     MB = _C.backward_plan(out[2], out[3], (X, Y, Z), c)
     del out
@@ -255,15 +271,15 @@ def run_ours(args, rank, world, dev):
     host = [t.pin_memory() for t in host_in]
     h2d = sum(t.numel() * t.element_size() for t in host)
     # stats timing off: the reference-style per-call timing synchronisations are optional
-    vox_e2e = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+    vox_e2e = vox if args.graph else PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
 
     def e2e_step():
         # H2D of the inputs, forward, backward with the same upstream gradients as the device-timed step,
         # and a D2H read of one element of the result (4 bytes)
         ls = [t.to(dev, non_blocking=True).requires_grad_() for t in host]
         density, grid_feats, _ = call(vox_e2e, ls)
-        grads = torch.autograd.grad([density, grid_feats], ls, [gD, gF])
-        return grads[0].reshape(-1)[:1].to("cpu").item()
+        gr = grads(density, grid_feats, ls)
+        return gr[0].reshape(-1)[:1].to("cpu").item()
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -291,7 +307,10 @@ def run_ours(args, rank, world, dev):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference distributions)",
         "config": {"workload": f"{args.config}: N={n} Gaussians, C={c} fp32 features, {X}x{Y}x{Z} voxels, "
                                f"fwd+bwd with randn upstream grads"
-                               + (", Gaussians as scales + rotation quaternions (grads to both)" if sr else ""),
+                               + (", Gaussians as scales + rotation quaternions (grads to both)" if sr else "")
+                               + (", density only (features=None)" if args.density_only else "")
+                               + (", forward and backward replayed from CUDA graphs (capacity-capped, no host "
+                                  "sync)" if args.graph else ""),
                    "global_batch": world,
                    "scenes_per_rank": 1, "l2": "inputs larger than L2 (grid_feats 4*V*C bytes)",
                    "pairs_M": M, "block_pairs": MB, "parallelism": f"dp{world} (independent scenes)",
@@ -866,6 +885,9 @@ def main():
     ap.add_argument("--path", default="voxelizer", choices=["voxelizer", "loss"],
                     help="voxelizer: the G2V fwd+bwd step (default); loss: the feature cosine loss fwd+bwd")
     ap.add_argument("--loss-channels", type=int, default=0, help="channels of the loss workload (default: config C)")
+    ap.add_argument("--density-only", action="store_true", help="features=None (the density-only kernels)")
+    ap.add_argument("--graph", action="store_true",
+                    help="GraphedGaussianVoxelizer: forward and backward replayed from CUDA graphs")
     ap.add_argument("--scenes", type=int, default=1,
                     help="scenes per rank per step, splatted in one batched call (compared with a loop of calls)")
     ap.add_argument("--cov-input", default="cov", choices=["cov", "sr"],

@@ -79,6 +79,23 @@ G2V_API int g2v_forward_prepare(const float* means3d, const float* covariances, 
                         int64_t* num_pairs);
 
 /*
+ * Forward, stage 1, without any host synchronisation (no counterpart in the reference): the same outputs
+ * as g2v_forward_prepare except that M is not read back.  The caller chooses the capacity max_pairs in
+ * advance (e.g. from an earlier g2v_forward_prepare on the same scene, with headroom) and passes it as
+ * num_pairs to g2v_forward_splat and g2v_backward (and its own block-pair capacity as num_block_pairs);
+ * every offset is clamped to its capacity, and a call that needed more sets the capacity bit (8) of the
+ * device error word -- its results are then invalid, and the next synchronising call or
+ * g2v_device_error reports it.  The sequence capped prepare -> splat -> backward contains no host
+ * synchronisation and no size-dependent allocation, so it can be captured in a CUDA graph and replayed
+ * (the density-only fast path of training loops with a fixed number of Gaussians).
+ */
+G2V_API int g2v_forward_prepare_capped(const float* means3d, const float* covariances, int64_t num_gaussians,
+                                       const float voxel_size[3], const float voxel_range[6], int64_t max_pairs,
+                                       float* cov_inv, int32_t* valid_voxel_lb, int32_t* valid_voxel_ub,
+                                       int32_t* num_voxels, int32_t* g2t_offsets, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
+/*
  * Forward, stage 1, for callers that cannot allocate device memory (no counterpart in the reference).
  * Same inputs, outputs and single stream synchronisation as g2v_forward_prepare, but no workspace: some
  * callers cannot provide one -- e.g. a serving process that reserves all device memory at start-up and

@@ -20,7 +20,10 @@ from ._C import (CudaFeatsCosinelossBackward, CudaFeatsCosinelossForward, _cosin
 
 _lib.load()  # fail loudly at import when the native library is missing
 
-__all__ = ["PyCudaGaussianVoxelizer", "_CudaGaussianVoxelizeFunction", "_CudaGaussianVoxelizeSRFunction",
+from .graphs import GraphedGaussianVoxelizer  # noqa: E402
+
+__all__ = ["PyCudaGaussianVoxelizer", "GraphedGaussianVoxelizer", "_CudaGaussianVoxelizeFunction",
+           "_CudaGaussianVoxelizeSRFunction",
            "covariance_from_scale_rot", "gaussian_voxelizer_forward",
            "gaussian_voxelizer_backward", "PyCudaFeatsCosineLoss", "_CudaFeatsCosinelossFunction",
            "CudaFeatsCosinelossForward", "CudaFeatsCosinelossBackward", "_C"]

@@ -29,6 +29,7 @@ SIGNATURES = {
     "g2v_forward_prepare_workspace_size": (I32, [I64, ctypes.POINTER(SZ)]),
     "g2v_forward_prepare": (I32, [P, P, I64, F3, F6, P, P, P, P, P, P, SZ, P, ctypes.POINTER(I64)]),
     "g2v_forward_prepare_static": (I32, [P, P, I64, F3, F6, P, P, P, P, P, P, ctypes.POINTER(I64)]),
+    "g2v_forward_prepare_capped": (I32, [P, P, I64, F3, F6, I64, P, P, P, P, P, P, SZ, P]),
     "g2v_forward_prepare_plan_workspace_size": (I32, [I64, ctypes.POINTER(SZ)]),
     "g2v_forward_prepare_plan": (I32, [P, P, I64, F3, F6, P, P, P, P, P, I64, P, SZ, P, ctypes.POINTER(I64),
                                        ctypes.POINTER(I64)]),

@@ -29,7 +29,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                      const int ncells_dim[3], int cell_x_begin, int cell_x_end, const int32_t* g2t_offsets,
                      int32_t* g2t_tile_ids, int64_t g2t_cap, int32_t* per_gaussian, int32_t* counts, int32_t* cell_offsets,
-                     int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s);
+                     int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s,
+                     int64_t list_cap, int* err);
 int count_gaussian_cells(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                          int32_t* per_gaussian, int32_t* dummy_counts, cudaStream_t s);
 int launch_splat_simt(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
@@ -72,7 +73,7 @@ int launch_cov_from_scale_rot_backward(const float* scales, const float* quats, 
                                        float* grad_scales, float* grad_quats, cudaStream_t s);
 int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const int32_t* lb, const int32_t* ub,
                         int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
-                        cudaStream_t s);
+                        cudaStream_t s, int64_t row_cap);
 size_t cosine_loss_workspace_bytes();
 int launch_cosine_loss_fwd(const float* label, const uint8_t* mask, const float* p, const float* g, int64_t V, int C,
                            float* loss, int* count, void* ws, cudaStream_t s);
@@ -121,8 +122,12 @@ int report_device_error(int word, cudaStream_t s) {
     if (word == 0) return 0;
     int* p = nullptr;
     if (device_error_ptr(&p) == 0) cudaMemsetAsync(p, 0, sizeof(int), s);
-    set_error("a kernel's bounded wait gave up (device error word 0x%x); results of the preceding calls are "
-              "invalid", word);
+    if (word & kErrCapacity)
+        set_error("a capacity-capped call needed more pairs than its capacity (device error word 0x%x); results "
+                  "of the preceding calls are invalid", word);
+    else
+        set_error("a kernel's bounded wait gave up (device error word 0x%x); results of the preceding calls are "
+                  "invalid", word);
     return G2V_ERROR_CUDA;
 }
 
@@ -393,6 +398,35 @@ int g2v_forward_prepare(const float* means3d, const float* covariances, int64_t 
     return G2V_SUCCESS;
 }
 
+int g2v_forward_prepare_capped(const float* means3d, const float* covariances, int64_t num_gaussians,
+                               const float voxel_size[3], const float voxel_range[6], int64_t max_pairs,
+                               float* cov_inv, int32_t* valid_voxel_lb, int32_t* valid_voxel_ub,
+                               int32_t* num_voxels, int32_t* g2t_offsets, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    g_msg[0] = 0;
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if (num_gaussians < 0 || num_gaussians > INT32_MAX - 1 || max_pairs < 0 || max_pairs > INT32_MAX ||
+        !g2t_offsets ||
+        (num_gaussians > 0 && (!means3d || !covariances || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
+                               !num_voxels))) {
+        set_error("g2v_forward_prepare_capped: invalid pointer, count or capacity");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    PrepareWs w;
+    const size_t need = carve_prepare(nullptr, num_gaussians, w);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    carve_prepare(workspace, num_gaussians, w);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int* err = nullptr;
+    if ((rc = device_error_ptr(&err))) return rc;
+    if ((rc = launch_prepare_boxes(means3d, covariances, num_gaussians, G, cov_inv, valid_voxel_lb, valid_voxel_ub,
+                                   num_voxels, w.ntiles, s)))
+        return rc;
+    return launch_exclusive_scan(w.ntiles, num_gaussians, g2t_offsets, w.total, w.scan, s, max_pairs, err);
+}
+
 int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3],
                                      int64_t channels, size_t* bytes) {
     if (!bytes || !dims || num_gaussians < 0 || num_pairs < 0 || channels < 0) {
@@ -439,10 +473,12 @@ static int forward_splat_impl(const float* means3d, const float* opacity, const 
     carve_t2g(c, ntiles_all, num_pairs, w);
     carve_t2g(c, ntiles_all, num_pairs, wu);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int* err = nullptr;
+    if ((rc = device_error_ptr(&err))) return rc;
     const int one[3] = {1, 1, 1};
     if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
                                tile_x_end, g2t_offsets, g2t_tile_ids, num_pairs, nullptr, w.counts, w.tile_offsets, w.unsorted,
-                               w.lists, w.scan, w.total, s)))
+                               w.lists, w.scan, w.total, s, num_pairs, err)))
         return rc;
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
@@ -452,11 +488,9 @@ static int forward_splat_impl(const float* means3d, const float* opacity, const 
         spass_tc_unit_shape(G, cell, ncells);
         if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
                                    tile_x_end, g2t_offsets, nullptr, 0, nullptr, wu.counts, wu.tile_offsets,
-                                   wu.unsorted, wu.lists, wu.scan, wu.total, s)))
+                                   wu.unsorted, wu.lists, wu.scan, wu.total, s, num_pairs, err)))
             return rc;
         void* split = c.take<char>(splat_tc_split_bytes(num_gaussians, C));
-        int* err = nullptr;
-        if ((rc = device_error_ptr(&err))) return rc;
         return launch_splat_tc(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, features, num_gaussians, C,
                                wu.tile_offsets, wu.lists, tile_x_begin, tile_x_end, G, density, grid_feats, split,
                                err, s);
@@ -809,15 +843,15 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
     // (z pairs of tiles); both fit the tile-sized buffers (fewer cells, at most M entries)
     int cell[3] = {1, 1, 1}, ncells[3] = {G.tiles[0], G.tiles[1], G.tiles[2]};
     if (tcore) spass_tc_unit_shape(G, cell, ncells);
+    int* err = nullptr;
+    if ((rc = device_error_ptr(&err))) return rc;
     if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
                                tile_x_end, g2t_offsets, nullptr, 0, nullptr, w.t2g.counts, w.t2g.tile_offsets,
-                               w.t2g.unsorted, w.t2g.lists, w.t2g.scan, w.t2g.total, s)))
+                               w.t2g.unsorted, w.t2g.lists, w.t2g.scan, w.t2g.total, s, num_pairs, err)))
         return rc;
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
-    int* err = nullptr;
     if (tcore) {
-        if ((rc = device_error_ptr(&err))) return rc;
         if ((rc = launch_pack_params(means3d, opacity, cov_inv, valid_voxel_lb, valid_voxel_ub, num_gaussians,
                                      w.gparams, s)))
             return rc;
@@ -842,9 +876,11 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
         // per-Gaussian block counts, then the offsets of the partial rows
         if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, B, nb, bx_begin, bx_end,
                                    nullptr, nullptr, 0, w.g2b_counts, w.block_counts, w.block_offsets,
-                                   w.block_unsorted, w.block_lists, w.block_scan, total, s)))
+                                   w.block_unsorted, w.block_lists, w.block_scan, total, s, num_block_pairs, err)))
             return rc;
-        if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s))) return rc;
+        if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s,
+                                        num_block_pairs, err)))
+            return rc;
         if (tcore) {
             if ((rc = launch_fpass_tc(grad_grid_feats, C, density, w.gparams, w.block_offsets, w.block_lists,
                                       w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1], nb[2], B, tile_x_begin,
@@ -857,7 +893,7 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
             return rc;
         }
         if ((rc = launch_reduce_feats(w.partialF, w.g2b_offsets, valid_voxel_lb, valid_voxel_ub, num_gaussians, C, B,
-                                      bx_begin, bx_end, grad_features, s)))
+                                      bx_begin, bx_end, grad_features, s, num_block_pairs)))
             return rc;
     }
     return G2V_SUCCESS;

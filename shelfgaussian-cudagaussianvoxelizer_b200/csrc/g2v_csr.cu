@@ -98,7 +98,8 @@ __global__ void __launch_bounds__(256) cells_scatter_kernel(const int32_t* __res
         const int lz = r - ly * b.ext[2];
         const int c = ((xa + lx - cell_x_begin) * ncy + b.lo[1] + ly) * ncz + b.lo[2] + lz;
         const int pos = atomicAdd(&cursor[c], 1);
-        lists[cell_offsets[c] + pos] = (int32_t)g;
+        // offsets clamped to a capacity (capped calls): a full cell drops the entries beyond it
+        if (cell_offsets[c] + pos < cell_offsets[c + 1]) lists[cell_offsets[c] + pos] = (int32_t)g;
     }
 }
 
@@ -220,7 +221,8 @@ __global__ void __launch_bounds__(kSortThreads) cells_sort_kernel(const int32_t*
 int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                      const int ncells_dim[3], int cell_x_begin, int cell_x_end, const int32_t* g2t_offsets,
                      int32_t* g2t_tile_ids, int64_t g2t_cap, int32_t* per_gaussian, int32_t* counts, int32_t* cell_offsets,
-                     int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s) {
+                     int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s,
+                     int64_t list_cap, int* err) {
     const int nx = cell_x_end - cell_x_begin;
     const int64_t ncells = (int64_t)nx * ncells_dim[1] * ncells_dim[2];
     if (ncells > 0) G2V_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)ncells, s));
@@ -232,7 +234,7 @@ int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid
                                                   g2t_tile_ids, g2t_cap, counts, per_gaussian));
         G2V_LAUNCH_CHECK("cells_count_kernel");
     }
-    int rc = launch_exclusive_scan(counts, ncells, cell_offsets, total, scan_ws, s);
+    int rc = launch_exclusive_scan(counts, ncells, cell_offsets, total, scan_ws, s, list_cap, err);
     if (rc) return rc;
     if (n > 0 && ncells > 0) {
         G2V_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)ncells, s));

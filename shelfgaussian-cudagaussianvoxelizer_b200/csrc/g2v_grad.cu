@@ -421,10 +421,10 @@ __global__ void __launch_bounds__(256) reduce_feats_kernel(const float* __restri
                                                            const int32_t* __restrict__ lb,
                                                            const int32_t* __restrict__ ub, int C, int BX, int BY,
                                                            int BZ, int bx_begin, int bx_end,
-                                                           float* __restrict__ grad_features) {
+                                                           float* __restrict__ grad_features, int64_t row_cap) {
     const int64_t g = blockIdx.x;
     int tlo[3], thi[3];
-    const bool ok = tile_box(lb, ub, g, tlo, thi);
+    bool ok = tile_box(lb, ub, g, tlo, thi);
     int blo[3] = {0, 0, 0}, ext[3] = {0, 0, 0};
     if (ok) {
         const int B[3] = {BX, BY, BZ};
@@ -436,6 +436,7 @@ __global__ void __launch_bounds__(256) reduce_feats_kernel(const float* __restri
     }
     const int64_t base = g2b_offsets[g];
     const int run = ext[1] * ext[2];  // rows of one block-x column
+    ok = ok && base + (int64_t)ext[0] * run <= row_cap;  // rows beyond a capped call's capacity: flagged, skipped
     if (kVec) {
         const int C4 = C >> 2;
         for (int c4 = threadIdx.x; c4 < C4; c4 += blockDim.x) {
@@ -548,7 +549,7 @@ int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const in
 
 int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const int32_t* lb, const int32_t* ub,
                         int64_t n, int C, const int B[3], int bx_begin, int bx_end, float* grad_features,
-                        cudaStream_t s) {
+                        cudaStream_t s, int64_t row_cap) {
     if (n == 0 || C == 0) return 0;
     // 16-byte rows: C % 4 == 0 and 16-byte aligned bases (the partial rows live in the library's workspace)
     const bool vec = C % 4 == 0 && (reinterpret_cast<uintptr_t>(partialF) & 15) == 0 &&
@@ -558,12 +559,12 @@ int launch_reduce_feats(const float* partialF, const int32_t* g2b_offsets, const
         G2V_TIMED("reduce_feats_kernel", s,
                   reduce_feats_kernel<true><<<(unsigned)n, threads, 0, s>>>(partialF, g2b_offsets, lb, ub, C, B[0],
                                                                             B[1], B[2], bx_begin, bx_end,
-                                                                            grad_features));
+                                                                            grad_features, row_cap));
     else
         G2V_TIMED("reduce_feats_kernel", s,
                   reduce_feats_kernel<false><<<(unsigned)n, threads, 0, s>>>(partialF, g2b_offsets, lb, ub, C, B[0],
                                                                              B[1], B[2], bx_begin, bx_end,
-                                                                             grad_features));
+                                                                             grad_features, row_cap));
     G2V_LAUNCH_CHECK("reduce_feats_kernel");
     return 0;
 }

@@ -11,6 +11,9 @@ namespace g2v {
 constexpr int kTile = 4;                          // tile edge in voxels (reference include/utils.cuh:50-52)
 constexpr int kVoxPerTile = kTile * kTile * kTile;  // 64
 constexpr float kEps = 1e-6f;                     // density clamp of the normalisation (utils.cuh:80)
+// Bits of the library's device error word (bits 1, 2, 4: bounded waits and CSR capacity guards of the
+// tensor-core kernels).
+constexpr int kErrCapacity = 8;                   // a capacity-capped call needed more pairs than its cap
 
 // ---------------------------------------------------------------------------------------------
 // Grid geometry passed by value to kernels.
@@ -120,10 +123,11 @@ int launch_prepare_boxes(const float* means, const float* cov, int64_t n, const 
                          const int32_t* scene_offsets = nullptr, int num_scenes = 1);
 
 size_t scan_workspace_bytes(int64_t n);
-// Exclusive prefix sum of n int32 counts into out[0..n] (out[n] = total).  Fails with
-// G2V_ERROR_SIZE_LIMIT when the total does not fit int32.  `total` (device, int64) receives the sum.
+// Exclusive prefix sum of n int32 counts into out[0..n] (out[n] = total).  `total` (device, int64)
+// receives the sum.  cap >= 0: the offsets are clamped to cap and a larger total sets kErrCapacity in
+// *err (capacity-capped calls that never read the total back on the host).
 int launch_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_t* total, void* ws,
-                          cudaStream_t s);
+                          cudaStream_t s, int64_t cap = -1, int* err = nullptr);
 
 }  // namespace g2v
 

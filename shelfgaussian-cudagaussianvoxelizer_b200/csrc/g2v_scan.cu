@@ -72,10 +72,14 @@ __global__ void __launch_bounds__(1024) scan_block_sums_kernel(int64_t* __restri
     if (threadIdx.x == 0) *total = carry;
 }
 
+// cap >= 0: every offset is clamped to cap (the capacity of the arrays the offsets index) and a total
+// above it sets kErrCapacity in *err, so that a capacity chosen by the caller in advance can never be
+// overrun (the results are then flagged invalid instead).
 __global__ void __launch_bounds__(kScanThreads) scan_write_kernel(const int32_t* __restrict__ in, int64_t n,
                                                                   const int64_t* __restrict__ block_offsets,
                                                                   const int64_t* __restrict__ total,
-                                                                  int32_t* __restrict__ out) {
+                                                                  int32_t* __restrict__ out, int64_t cap,
+                                                                  int* __restrict__ err) {
     // blocked arrangement: thread t owns items [base + t*kScanItems, +kScanItems)
     __shared__ int32_t stage[kScanTile];
     const int64_t base = blockIdx.x * (int64_t)kScanTile;
@@ -97,7 +101,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_write_kernel(const int32_t*
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k) {
-        stage[threadIdx.x * kScanItems + k] = static_cast<int32_t>(run);
+        stage[threadIdx.x * kScanItems + k] = static_cast<int32_t>(cap >= 0 && run > cap ? cap : run);
         run += v[k];
     }
     __syncthreads();
@@ -106,7 +110,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_write_kernel(const int32_t*
         const int64_t i = base + k * kScanThreads + threadIdx.x;
         if (i < n) out[i] = stage[k * kScanThreads + threadIdx.x];
     }
-    if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) out[n] = static_cast<int32_t>(*total);
+    if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+        const int64_t t = *total;
+        out[n] = static_cast<int32_t>(cap >= 0 && t > cap ? cap : t);
+        if (cap >= 0 && t > cap && err) atomicOr(err, kErrCapacity);
+    }
 }
 
 __global__ void scan_empty_kernel(int32_t* out, int64_t* total) {
@@ -121,7 +129,7 @@ size_t scan_workspace_bytes(int64_t n) {
 }
 
 int launch_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_t* total, void* ws,
-                          cudaStream_t s) {
+                          cudaStream_t s, int64_t cap, int* err) {
     if (n == 0) {
         G2V_TIMED("scan_empty_kernel", s, scan_empty_kernel<<<1, 1, 0, s>>>(out, total));
         G2V_LAUNCH_CHECK("scan_empty_kernel");
@@ -133,7 +141,7 @@ int launch_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_
     G2V_LAUNCH_CHECK("scan_reduce_kernel");
     G2V_TIMED("scan_block_sums_kernel", s, scan_block_sums_kernel<<<1, 1024, 0, s>>>(sums, nb, total));
     G2V_LAUNCH_CHECK("scan_block_sums_kernel");
-    G2V_TIMED("scan_write_kernel", s, scan_write_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(counts, n, sums, total, out));
+    G2V_TIMED("scan_write_kernel", s, scan_write_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(counts, n, sums, total, out, cap, err));
     G2V_LAUNCH_CHECK("scan_write_kernel");
     return 0;
 }
