@@ -229,10 +229,19 @@ def run_ours(args, rank, world, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
-    # per-kernel device time (CUDA events on the launch stream, inside the library) over K steps
+    # per-kernel device time (CUDA events on the launch stream, inside the library) over K steps; graph
+    # replays launch nothing from the host, so --graph profiles the same kernels through the eager module
+    if args.graph:
+        vox_prof = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+
+        def prof_step():
+            density, grid_feats, _ = call(vox_prof, leaves)
+            return grads(density, grid_feats, leaves)
+    else:
+        prof_step = step
     _lib.profile_enable(True)
     for _ in range(args.steps):
-        step()
+        prof_step()
     torch.cuda.synchronize()
     prof = _lib.profile_read()
     _lib.profile_enable(False)
