@@ -181,11 +181,15 @@ def run_ours(args, rank, world, dev):
     if args.density_only:  # features=None: the density-only kernels
         host_in = host_in[:-1]
     leaves = [t.to(dev).requires_grad_() for t in host_in]
-    if args.graph:
-        from CudaGaussianVoxelizer import GraphedGaussianVoxelizer
+    if args.graph:  # whole step captured in one CUDA graph: capacity-capped module, no host synchronisation
         if sr:
             raise SystemExit("--graph takes covariance inputs")
-        vox = GraphedGaussianVoxelizer(voxel_size=size, voxel_range=rng)
+        out0, mb0 = _C._forward_impl(*[t.detach() for t in leaves[:3]], size, rng,
+                                     None if args.density_only else leaves[3].detach(), False, plan=True)
+        caps = (int(out0[7].numel() * 1.25) + 1024, int(mb0 * 1.25) + 1024 if c > 0 else 0)
+        del out0
+        vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False, max_pairs=caps[0],
+                                      max_block_pairs=caps[1])
     else:
         vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
 
@@ -203,6 +207,24 @@ def run_ours(args, rank, world, dev):
     def step():
         density, grid_feats, _ = call(vox, leaves)
         return grads(density, grid_feats, leaves)
+
+    if args.graph:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+            graph_out = step()  # noqa: F841  (static outputs of the captured step)
+        eager_step = step
+
+        def step():
+            graph.replay()
+    else:
+        eager_step = step
 
     def barrier():
         if world > 1:
@@ -231,14 +253,7 @@ def run_ours(args, rank, world, dev):
 
     # per-kernel device time (CUDA events on the launch stream, inside the library) over K steps; graph
     # replays launch nothing from the host, so --graph profiles the same kernels through the eager module
-    if args.graph:
-        vox_prof = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
-
-        def prof_step():
-            density, grid_feats, _ = call(vox_prof, leaves)
-            return grads(density, grid_feats, leaves)
-    else:
-        prof_step = step
+    prof_step = eager_step
     _lib.profile_enable(True)
     for _ in range(args.steps):
         prof_step()
@@ -280,11 +295,17 @@ def run_ours(args, rank, world, dev):
     host = [t.pin_memory() for t in host_in]
     h2d = sum(t.numel() * t.element_size() for t in host)
     # stats timing off: the reference-style per-call timing synchronisations are optional
-    vox_e2e = vox if args.graph else PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+    vox_e2e = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
 
     def e2e_step():
         # H2D of the inputs, forward, backward with the same upstream gradients as the device-timed step,
         # and a D2H read of one element of the result (4 bytes)
+        if args.graph:  # into the captured step's static inputs, then replay
+            with torch.no_grad():
+                for t, h in zip(leaves, host):
+                    t.copy_(h, non_blocking=True)
+            graph.replay()
+            return graph_out[0].reshape(-1)[:1].to("cpu").item()
         ls = [t.to(dev, non_blocking=True).requires_grad_() for t in host]
         density, grid_feats, _ = call(vox_e2e, ls)
         gr = grads(density, grid_feats, ls)
@@ -318,8 +339,8 @@ def run_ours(args, rank, world, dev):
                                f"fwd+bwd with randn upstream grads"
                                + (", Gaussians as scales + rotation quaternions (grads to both)" if sr else "")
                                + (", density only (features=None)" if args.density_only else "")
-                               + (", forward and backward replayed from CUDA graphs (capacity-capped, no host "
-                                  "sync)" if args.graph else ""),
+                               + (", the whole step replayed from one CUDA graph (capacity-capped module, no "
+                                  "host sync)" if args.graph else ""),
                    "global_batch": world,
                    "scenes_per_rank": 1, "l2": "inputs larger than L2 (grid_feats 4*V*C bytes)",
                    "pairs_M": M, "block_pairs": MB, "parallelism": f"dp{world} (independent scenes)",
@@ -896,7 +917,7 @@ def main():
     ap.add_argument("--loss-channels", type=int, default=0, help="channels of the loss workload (default: config C)")
     ap.add_argument("--density-only", action="store_true", help="features=None (the density-only kernels)")
     ap.add_argument("--graph", action="store_true",
-                    help="GraphedGaussianVoxelizer: forward and backward replayed from CUDA graphs")
+                    help="capture the whole step (capacity-capped module) in one CUDA graph and replay it")
     ap.add_argument("--scenes", type=int, default=1,
                     help="scenes per rank per step, splatted in one batched call (compared with a loop of calls)")
     ap.add_argument("--cov-input", default="cov", choices=["cov", "sr"],

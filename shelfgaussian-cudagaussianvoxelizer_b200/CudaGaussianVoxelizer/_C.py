@@ -107,11 +107,14 @@ def _scene_offsets(scene_sizes, n, dev):
 
 
 def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False,
-                  plan=False, scale_rot=None, scenes=None):
+                  plan=False, scale_rot=None, scenes=None, caps=None):
     """The forward; ``scale_rot=(scales, rotations)`` replaces ``covariances`` (then ``plan`` is implied and
     the covariances are formed inside the preparation kernel).  ``scenes=(scene_offsets (B+1) device int32,
     B)``: the Gaussians are a ragged batch of B scenes, splatted in one call into (B, X, Y, Z[, C]) volumes
-    (boxes and tile ids in the coordinates of the scenes stacked along x; ``plan`` implied)."""
+    (boxes and tile ids in the coordinates of the scenes stacked along x; ``plan`` implied).
+    ``caps=(max_pairs, max_block_pairs)``: capacity-capped, with no host synchronisation at all (the pair
+    buffers are sized by the capacities; ``plan`` implied and the returned block-pair count is the cap), so
+    the call can be captured in a CUDA graph; overflow is reported through the device error word."""
     lib = _lib.load()
     size_h = _host_values(voxel_size, 3, "voxel_size")
     range_h = _host_values(voxel_range, 6, "voxel_range")
@@ -144,6 +147,10 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
         scene_off, nsc = scenes
         if keep_t2g:
             raise RuntimeError("t2g maps are not exposed for batched scenes")
+    if caps is not None:
+        plan = True
+        if scenes is not None or scale_rot is not None or keep_t2g or timing:
+            raise RuntimeError("capacity-capped calls take covariances, one scene and timing=False")
     XS = X * nsc  # x rows of the stacked volume arrays
     i32 = dict(dtype=torch.int32, device=dev)
     f32 = dict(dtype=torch.float32, device=dev)
@@ -169,7 +176,14 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
             ev0.record(stream)
         m = ctypes.c_int64()
         mb = ctypes.c_int64()
-        if scenes is not None:
+        if caps is not None:  # no readback: the capacities size the pair buffers
+            _lib.check(lib.g2v_forward_prepare_capped(_ptr(means3D), _ptr(covariances), n, _lib.f3(size_h),
+                                                      _lib.f6(range_h), int(caps[0]), _ptr(cov_inv), _ptr(lb),
+                                                      _ptr(ub), _ptr(nvox), _ptr(g2t_offsets), _ptr(ws1),
+                                                      ws1.numel(), sptr), "g2v_forward_prepare_capped")
+            m.value = int(caps[0])
+            mb.value = int(caps[1]) if c > 0 else 0
+        elif scenes is not None:
             _lib.check(lib.g2v_forward_prepare_plan_batched(
                 _ptr(means3D), _ptr(covariances) if scale_rot is None else None,
                 _ptr(scales) if scale_rot is not None else None, _ptr(rotations) if scale_rot is not None else None,

@@ -33,11 +33,13 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
     """Autograd function of the splat (reference CudaGaussianVoxelizer/__init__.py:10-47)."""
 
     @staticmethod
-    def forward(ctx, means3D, opacity, covariances, voxel_size, voxel_range, features, timing=True, scenes=None):
-        # the forward also counts the backward's (Gaussian, block) pairs in its one synchronisation
+    def forward(ctx, means3D, opacity, covariances, voxel_size, voxel_range, features, timing=True, scenes=None,
+                caps=None):
+        # the forward also counts the backward's (Gaussian, block) pairs in its one synchronisation (or, with
+        # capacities, synchronises not at all)
         ((density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, fwd_sec),
          num_block_pairs) = _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing,
-                                          plan=True, scenes=scenes)
+                                          plan=True, scenes=scenes, caps=caps)
         ctx.num_scenes = 1 if scenes is None else scenes[1]
         stats = torch.zeros(2, dtype=torch.float32, device="cpu")
         stats[0] = fwd_sec
@@ -62,7 +64,8 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
             g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs,
             num_scenes=ctx.num_scenes)
         stats[1] = bwd_sec
-        return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None, None)
+        return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None, None,
+                None)
 
 
 class _CudaGaussianVoxelizeSRFunction(torch.autograd.Function):
@@ -135,14 +138,22 @@ class PyCudaGaussianVoxelizer(nn.Module):
     scale and rotation quaternion (the covariance is formed and differentiated inside the kernels).
     ``stats[0]`` is the forward device time in seconds, ``stats[1]`` the backward's (filled by
     ``.backward()``).  ``timing=False`` skips the two end-of-call synchronisations that fill them
-    (stats stay 0).  Reference: CudaGaussianVoxelizer/__init__.py:69-82.
+    (stats stay 0).  ``max_pairs`` (and ``max_block_pairs`` with features), with ``timing=False``: the
+    pair buffers are sized by these capacities instead of the forward's one synchronisation, so a whole
+    training step through this module can be captured in a CUDA graph (overflow is flagged in the device
+    error word; see ``GraphedGaussianVoxelizer.check``).  Reference: CudaGaussianVoxelizer/__init__.py:69-82.
     """
 
-    def __init__(self, voxel_size=[0.4, 0.4, 0.4], voxel_range=[-40, -40, -1, 40, 40, 5.4], timing: bool = True):
+    def __init__(self, voxel_size=[0.4, 0.4, 0.4], voxel_range=[-40, -40, -1, 40, 40, 5.4], timing: bool = True,
+                 max_pairs: int | None = None, max_block_pairs: int | None = None):
         super().__init__()
         self.voxel_size = torch.tensor(voxel_size, dtype=torch.float32, device="cuda")
         self.voxel_range = torch.tensor(voxel_range, dtype=torch.float32, device="cuda")
         self.timing = timing
+        # capacities: forward and backward without any host synchronisation (capturable in a CUDA graph)
+        self.caps = None if max_pairs is None else (int(max_pairs), int(max_block_pairs or 0))
+        if self.caps is not None and timing:
+            raise RuntimeError("PyCudaGaussianVoxelizer: max_pairs needs timing=False (no synchronisation)")
         # host copies: the C ABI takes the geometry by value, so no device read-back is needed
         _C._host_values(self.voxel_size, 3, "voxel_size")
         _C._host_values(self.voxel_range, 6, "voxel_range")
@@ -176,7 +187,7 @@ class PyCudaGaussianVoxelizer(nn.Module):
         if scales is not None or rotations is not None:
             raise RuntimeError("PyCudaGaussianVoxelizer: pass covariances or scales/rotations, not both")
         return _CudaGaussianVoxelizeFunction.apply(means3D, opacity, covariances, self.voxel_size, self.voxel_range,
-                                                   features, self.timing, scenes)
+                                                   features, self.timing, scenes, self.caps)
 
 
 class _CudaFeatsCosinelossFunction(torch.autograd.Function):

@@ -96,3 +96,45 @@ def test_capped_prepare_matches_prepare():
     torch.cuda.synchronize()
     for x, y in ((cov_inv, ref[1]), (lb, ref[2]), (ub, ref[3]), (nvox, ref[4]), (off, ref[6])):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("c", [0, 16])
+def test_whole_step_capture_with_capped_module(c):
+    """A training step (forward, loss, backward) through PyCudaGaussianVoxelizer(max_pairs=...) captured in
+    one torch CUDA graph reproduces the eager step bit for bit, and keeps doing so for new inputs copied
+    into the static tensors."""
+    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer, _C
+    m, o, cov, f = _inputs(500, c, 21)
+    out0, mb0 = _C._forward_impl(m, o, cov, SIZE, RNG, f, False, plan=True)
+    caps = (2 * int(out0[7].numel()) + 64, 2 * mb0 + 64)
+    capped = PyCudaGaussianVoxelizer(voxel_size=SIZE, voxel_range=RNG, timing=False, max_pairs=caps[0],
+                                     max_block_pairs=caps[1])
+    eager = PyCudaGaussianVoxelizer(voxel_size=SIZE, voxel_range=RNG)
+    static = [t.clone().requires_grad_(True) for t in (m, o, cov)] + ([f.clone().requires_grad_(True)] if c else [])
+
+    def step(vox, ls):
+        density, grid_feats, _ = vox(*ls[:3], ls[3] if c else None)
+        loss = (density * density).sum() + (grid_feats.sum() if c else 0.0)
+        return torch.autograd.grad(loss, ls)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step(capped, static)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="relaxed"):
+        out = step(capped, static)
+    for seed in (21, 22):
+        m, o, cov, f = _inputs(500, c, seed)
+        with torch.no_grad():
+            for t, v in zip(static, (m, o, cov, f)):
+                t.copy_(v)
+        g.replay()
+        ref = step(eager, [t.detach().clone().requires_grad_(True) for t in static])
+        torch.cuda.synchronize()
+        for i, (x, y) in enumerate(zip(out, ref)):
+            assert torch.equal(x, y), f"seed {seed}: grad {i}"
+    from CudaGaussianVoxelizer import GraphedGaussianVoxelizer
+    GraphedGaussianVoxelizer(voxel_size=SIZE, voxel_range=RNG).check()
