@@ -141,11 +141,11 @@ bool use_tensor_cores() {
     return !(v && strcmp(v, "simt") == 0);
 }
 
-// Feature-gradient pass: the cluster kernel (weights shared across the channel groups of a block, one
-// pass of up to 512 slots) unless G2V_FPASS=single selects the single-CTA kernel (256 slots per pass).
+// Feature-gradient pass: the single-CTA kernel (256 slots per pass) unless G2V_FPASS=cluster selects the
+// cluster kernel (weights shared across the channel groups of a block, one pass of up to 512 slots).
 bool use_fpass_cluster() {
     const char* v = getenv("G2V_FPASS");
-    return !(v && strcmp(v, "single") == 0);
+    return v && strcmp(v, "cluster") == 0;
 }
 
 int make_grid(const float size[3], const float range[6], Grid& G) {
