@@ -38,7 +38,6 @@ SOURCES = {
     "g2v_selftest.cu": [],
     "g2v_loss.cu": [],
     "g2v_cov.cu": [],
-    "g2v_fpass_cl.cu": [],
 }
 HEADERS_TC = ["g2v_tc.cuh"]
 HEADERS = [os.path.join(HERE, "g2v_internal.cuh"), os.path.join(HERE, "g2v_tc.cuh"), os.path.join(HERE, "g2v_cov.cuh"),

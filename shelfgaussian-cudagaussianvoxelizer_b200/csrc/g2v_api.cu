@@ -56,10 +56,6 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
                     const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
                     int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
                     int64_t block_pair_cap, int* err, cudaStream_t s);
-int launch_fpass_cl(const float* grad_feats, int C, const float* density, const GParams* gparams,
-                    const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
-                    int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
-                    int64_t block_pair_cap, int* err, cudaStream_t s);
 size_t spass_tc_split_bytes(int64_t n, int64_t C);
 void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]);
 int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
@@ -139,13 +135,6 @@ int report_device_error(int word, cudaStream_t s) {
 bool use_tensor_cores() {
     const char* v = getenv("G2V_VARIANT");
     return !(v && strcmp(v, "simt") == 0);
-}
-
-// Feature-gradient pass: the single-CTA kernel (256 slots per pass) unless G2V_FPASS=cluster selects the
-// cluster kernel (weights shared across the channel groups of a block, one pass of up to 512 slots).
-bool use_fpass_cluster() {
-    const char* v = getenv("G2V_FPASS");
-    return v && strcmp(v, "cluster") == 0;
 }
 
 int make_grid(const float size[3], const float range[6], Grid& G) {
@@ -892,12 +881,7 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
         if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s,
                                         num_block_pairs, err)))
             return rc;
-        if (tcore && use_fpass_cluster()) {
-            if ((rc = launch_fpass_cl(grad_grid_feats, C, density, w.gparams, w.block_offsets, w.block_lists,
-                                      w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1], nb[2], B, tile_x_begin,
-                                      tile_x_end, G, w.partialF, num_block_pairs, err, s)))
-                return rc;
-        } else if (tcore) {
+        if (tcore) {
             if ((rc = launch_fpass_tc(grad_grid_feats, C, density, w.gparams, w.block_offsets, w.block_lists,
                                       w.g2b_offsets, bx_begin, bx_end - bx_begin, nb[1], nb[2], B, tile_x_begin,
                                       tile_x_end, G, w.partialF, num_block_pairs, err, s)))

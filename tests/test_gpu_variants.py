@@ -69,18 +69,23 @@ def test_device_error_word_is_clear():
     assert w.value == 0
 
 
-def _with_variant(variant, fn):
-    old = os.environ.get("G2V_VARIANT")
-    os.environ["G2V_VARIANT"] = variant
+def _with_env(env, fn):
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
     try:
         out = fn()
         torch.cuda.synchronize()
     finally:
-        if old is None:
-            del os.environ["G2V_VARIANT"]
-        else:
-            os.environ["G2V_VARIANT"] = old
+        for k, v in old.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
     return out
+
+
+def _with_variant(variant, fn):
+    return _with_env({"G2V_VARIANT": variant}, fn)
 
 
 @pytest.mark.parametrize("n,c,seed,half,var_max,xt", [
@@ -113,6 +118,7 @@ def test_tensor_core_backward_matches_oracle_and_fp32_variant(n, c, seed, half, 
     names = ("grad_means", "grad_cov", "grad_opacity", "grad_features")
     for name, a, b in zip(names, tc, fp):
         assert_close(f"{name} tc vs simt", a, b)
+
     xr = None if xt is None else (xt[0] * 4, min(xt[1] * 4, dims[0]))
     lb_h, ub_h = lb.cpu().numpy(), ub.cpu().numpy()
     dref, fref = oracle.forward(m, o, cv, f, lb_h, ub_h, size, rng, dims, x_range=xr)
