@@ -64,51 +64,102 @@ def load_peaks():
 
 # ------------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms around the timed region.
+
+    The sampler is started and waited for (first sample written) before the timed region begins, so a
+    short timed region still has samples; ``stop()`` keeps the samples whose timestamps fall inside the
+    region (begin = end of the constructor, end = the call of ``stop()``) and, when the region was shorter
+    than the sampling interval, the first sample after it began ("window": "nearest")."""
+    FIELDS = ("timestamp,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
 
     def __init__(self, gpu_id):
         self.proc = None
+        self.gpu_id = str(gpu_id) if gpu_id is not None else None
         self.path = tempfile.mktemp(prefix="g2v_clocks_", suffix=".csv")
+        for select in ((True, False) if self.gpu_id else (False,)):
+            if self._start(select):
+                break
+        self.t_begin = time.time()
+
+    def _start(self, select):
         try:
             self.fh = open(self.path, "w")
-            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
-            if gpu_id is not None:
-                cmd += ["-i", str(gpu_id)]
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                   str(self.INTERVAL_MS)]
+            if select:
+                cmd += ["-i", self.gpu_id]
             self.proc = subprocess.Popen(cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return False
+        t0 = time.time()
+        while time.time() - t0 < 10.0:  # wait for the first sample (nvidia-smi start-up)
+            if self.proc.poll() is not None:
+                break
+            if os.path.getsize(self.path) > 0:
+                return True
+            time.sleep(0.02)
+        self._kill()
+        return False
 
-    def stop(self):
+    def _kill(self):
         if self.proc is None:
-            return None
+            return
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
         self.fh.close()
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        self.proc = None
+
+    @staticmethod
+    def _stamp(s):
+        import datetime
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
+            try:
+                return datetime.datetime.strptime(s, fmt).timestamp()
+            except ValueError:
+                pass
+        return None
+
+    def stop(self):
+        t_end = time.time()
+        if self.proc is None:
+            return None
+        time.sleep(2.0 * self.INTERVAL_MS / 1000.0)  # the sample that follows the region's end
+        self._kill()
+        rows = []
+        want = self.gpu_id.lower().replace("gpu-", "") if self.gpu_id else None
         with open(self.path) as fh:
             for line in fh:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) < 9:
+                if len(parts) < 10:
+                    continue
+                if want and want.count("-") >= 4 and parts[1].lower().replace("gpu-", "") != want:
                     continue
                 try:
-                    sm.append(float(parts[1]))
-                    smax = float(parts[2])
+                    rows.append((self._stamp(parts[0]), float(parts[2]), float(parts[3]), parts[6:10]))
                 except ValueError:
                     continue
-                for nm, v in zip(names, parts[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(nm)
         os.unlink(self.path)
-        if not sm:
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        slack = self.INTERVAL_MS / 1000.0
+        inside = [r for r in rows if r[0] is not None and self.t_begin - slack <= r[0] <= t_end + slack]
+        window = "timed region"
+        if not inside:
+            after = [r for r in rows if r[0] is not None and r[0] >= self.t_begin]
+            inside = after[:1] or rows[-1:]
+            window = "nearest"
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({nm for r in inside for nm, v in zip(names, r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median([r[1] for r in inside]), "sm_max_mhz": inside[-1][2],
+                "reasons": reasons, "samples": len(inside), "window": window,
+                "interval_ms": self.INTERVAL_MS}
 
 
 def gpu_id_for(dev_index):
@@ -904,7 +955,7 @@ def run_loss_reference(args, rank, world, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="cfg3", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
