@@ -339,7 +339,8 @@ def run_ours(args, rank, world, dev):
                 "frac": (achieved / peak) if achieved else None, "traffic": traffic,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": avg_ms,
-                "kernel_share": {k: round(v[0] / sum(x[0] for x in prof.values()), 4) for k, v in prof.items()}}
+                "kernel_share": {k: round(v[0] / sum(x[0] for x in prof.values()), 4) for k, v in prof.items()},
+                "kernel_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in prof.items()}}
     sb = step_bytes(n, c, V, M)
 
     # end-to-end through the public API with pinned host inputs (H2D inside the timed region)

@@ -22,13 +22,18 @@
 //       row by row from the split features with 16-byte cp.async (L2 evict_last);
 //   B = w slice (128 voxels x 16 Gaussians) MN-major, 128-byte swizzle, same atom geometry: one thread
 //       writes the 8 z-voxels of a line for one Gaussian as one 16-byte store (conflict-free).
-// Roles (544 threads): warps 0-3 gather feature rows and stage the step's Gaussian records; warps 4-7
-// evaluate the weights (thread = z-line of 8 voxels x Gaussian pair; along z the exponent is a
-// quadratic, so each weight is two FMAs and one exp2) and, in a unit's first job, the density; warp 8
-// (one thread) issues the 6 MMAs of a step; warps 9-16 run the epilogue (thread = channel): the scaled
+// Roles (544 threads with 4 weight warps): warps 0-3 gather feature rows and stage the step's Gaussian
+// records; warps 4-7 evaluate the weights (thread = z-line of 8 voxels x Gaussian pair; along z the
+// exponent is a quadratic, so each weight is two FMAs and one exp2) and, in a unit's first job, the
+// density; warp 8 (one thread) issues the 6 MMAs of a step; warps 9-16 run the epilogue (thread = channel): the scaled
 // values of 16 voxels x 256 channels go to a shared-memory tile that one tiled TMA store writes out
 // (L2 evict_first; the store clips the grid edges), double-buffered, or -- when the tensor map cannot be
 // built (C % 4 != 0, unaligned output) -- straight to global memory with streaming stores.
+// Weight cache: the weights of a unit do not depend on the channel group, so only its first job
+// evaluates them; every weight thread also stores its 16-byte words to the CTA's region of a workspace
+// buffer (the B stage's layout, kWcSteps steps per CTA; the working set of all CTAs stays in L2) and the
+// unit's later jobs copy them back with cp.async.  Steps beyond kWcSteps (units of more than 512
+// Gaussians) are evaluated in every job.
 // Seven stages; every mbarrier wait is bounded.
 #include <cstddef>
 
@@ -41,7 +46,6 @@
 namespace g2v {
 
 namespace {
-constexpr int kThreads = 544;             // 17 warps
 constexpr int kKStep = 16;                // Gaussians per pipeline step
 constexpr int kCG = 256;                  // channels per job (two M-blocks)
 constexpr int kUV = 128;                  // voxels per unit
@@ -52,10 +56,21 @@ constexpr int kBHalf = 4096;              // 128 voxels x 16 Gaussians, one half
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kBufCols = 256;             // one job: 2 M-blocks x 128 voxel columns
-constexpr int kWarpW0 = 4;                // first weight warp (4 of them)
-constexpr int kNWW = 4;
-constexpr int kMmaWarp = 8;
-constexpr int kEpiWarp0 = 9;
+constexpr int kWarpW0 = 4;                // first weight warp
+// Weight-cache capacity: steps (16 Gaussians each) of a unit whose weights are kept for the unit's later
+// channel groups, per CTA, and the CTA count the cache is sized for.
+constexpr int kWcSteps = 32;
+constexpr int kMaxSplatCtas = 148;
+constexpr size_t kWcStepBytes = 2 * (size_t)kBHalf;
+// Roles for NW weight warps: warps 0-3 producers, 4 .. 4+NW-1 weights, then the MMA warp and 8 epilogue warps.
+template <int NW>
+struct Roles {
+    static constexpr int kMmaWarp = kWarpW0 + NW;
+    static constexpr int kEpiWarp0 = kMmaWarp + 1;
+    static constexpr int kThreads = (kEpiWarp0 + 8) * 32;
+    static constexpr int kGpt = kKStep * 16 / (NW * 32);  // Gaussians per weight thread and step
+    static_assert(kGpt * NW * 32 == kKStep * 16, "weight threads must tile 16 Gaussians x 16 z-lines");
+};
 constexpr uint32_t kIdesc = tc::idesc_f16_f32(128, kUV, /*A MN-major*/ 1, /*B MN-major*/ 1);
 
 // The Gaussian records of the 16 Gaussians of a step, staged with the step's features.
@@ -74,10 +89,11 @@ struct TcMisc {
     uint32_t tmem_base;
     float red[8];
     alignas(16) float vscale[2][kUV];  // per unit: 2^-kt / max(D_v, eps)
-    alignas(16) float dpart[kKStep / 2][kUV];  // density partials [Gaussian pair][voxel], scaled by 2^kt
+    alignas(16) float dpart[kKStep][kUV];  // density partials [Gaussian group of a thread][voxel], scaled by 2^kt
     alignas(16) StepParams prm[kStages];
 };
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 2 * (size_t)kOutBytes + sizeof(TcMisc);
+static_assert(kSmemBytes % 16 == 0, "dynamic shared memory size");
 static_assert(kSmemBytes <= 227 * 1024, "splat_tc_kernel shared memory");
 static_assert(offsetof(TcMisc, vscale) % 16 == 0 && offsetof(TcMisc, prm) % 16 == 0,
               "vector-accessed shared fields must be 16-byte aligned");
@@ -147,8 +163,11 @@ __global__ void __launch_bounds__(256) pack_params_kernel(const float* __restric
     out[g] = r;
 }
 
-// Named barrier of the 4 weight warps (barrier 0 is __syncthreads).
-__device__ __forceinline__ void weight_barrier() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+// Named barrier of the NW weight warps (barrier 0 is __syncthreads).
+template <int NW>
+__device__ __forceinline__ void weight_barrier() {
+    asm volatile("bar.sync 2, %0;" ::"n"(NW * 32) : "memory");
+}
 
 struct UnitGeom {
     int tx, ty, tzp;
@@ -166,12 +185,14 @@ __device__ __forceinline__ UnitGeom unit_geom(int u, int ty_n, int tzp_n, int tx
 // Named barrier of the 8 epilogue warps.
 __device__ __forceinline__ void epi_barrier() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-template <bool kTmaStore>
-__global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
+template <bool kTmaStore, int NW>
+__global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
     const __grid_constant__ CUtensorMap omap, const __half* __restrict__ Fhi, const __half* __restrict__ Flo, const float* __restrict__ unscale, int C, int Cp,
     const GParams* __restrict__ gparams, const int32_t* __restrict__ unit_offsets,
     const int32_t* __restrict__ unit_lists, int num_units, int tx_begin, Grid G, float* __restrict__ density,
-    float* __restrict__ grid_feats, int* __restrict__ err) {
+    float* __restrict__ grid_feats, unsigned char* __restrict__ wcache, int wc_steps, int* __restrict__ err) {
+    constexpr int kNWW = NW;
+    constexpr int kMmaWarp = Roles<NW>::kMmaWarp, kEpiWarp0 = Roles<NW>::kEpiWarp0, kGpt = Roles<NW>::kGpt;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
     unsigned char* ostage = base + kStages * kStageBytes;  // 2 epilogue staging tiles
@@ -187,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(&ms.full_a[i], 128);
-            tc::mbar_init(&ms.full_w[i], kNWW);
+            tc::mbar_init(&ms.full_w[i], kNWW * 32);
             tc::mbar_init(&ms.empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -260,12 +281,17 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
         }
         tc::cp_async_wait<0>();  // no copy in flight when the shared memory is released
     } else if (warp < kMmaWarp) {
-        // ============ weight warps: thread = (z-line o of 8 voxels, Gaussian pair kp of the step) ============
+        // ============ weight warps: thread = (z-line o of 8 voxels, kGpt Gaussians kq*kGpt.. of the step) ============
+        // With a weight cache, a unit's weights are evaluated in its first channel group only: each thread
+        // also writes its 16-byte words to the CTA's region of the cache (same layout as the B stage) and,
+        // in the later channel groups, copies them back with cp.async instead of evaluating them again.
+        // A thread reads back only the words it wrote itself.
         const int t = tid - kWarpW0 * 32;
-        const int o = t & 15, kp = t >> 4;
+        const int o = t & 15, kq = t >> 4;
         const int lx = o >> 2, ly = o & 3;
         const float k2 = tc::kNegHalfLog2e;
         const float hz = G.h[2];
+        unsigned char* wregion = wcache ? wcache + (size_t)blockIdx.x * wc_steps * kWcStepBytes : nullptr;
         // The named barriers below are reached the same number of times by every weight thread whatever
         // `ok` says (a wait that gave up only skips work), so a failed wait cannot split the barrier.
         int it = 0, nu = 0;
@@ -277,17 +303,19 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
             const int x0 = ug.tx * kTile, y0 = ug.ty * kTile, z0 = ug.tzp * 8;
             const int vx = x0 + lx, vy = y0 + ly;
             const float cx = voxel_centre(G, 0, vx), cy = voxel_centre(G, 1, vy), cz0 = voxel_centre(G, 2, z0);
+            // this thread's cache reads of the previous unit are complete before its words are rewritten
+            tc::cp_async_wait<0>();
             // unit weight scale 2^kt from the largest |opacity| (w <= |opacity|)
             float om = 0.0f;
             for (int i = t; i < K; i += kNWW * 32) om = fmaxf(om, fabsf(gparams[list[i]].w[0].w));
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, off));
             if (lane == 0) ms.red[warp - kWarpW0] = om;
-            weight_barrier();
+            weight_barrier<NW>();
             om = 0.0f;
 #pragma unroll
             for (int w8 = 0; w8 < kNWW; ++w8) om = fmaxf(om, ms.red[w8]);
-            weight_barrier();
+            weight_barrier<NW>();
             int kt = 0;
             if (om > 0.0f) {
                 int e2;
@@ -302,13 +330,28 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
             for (int cg = 0; cg < ngroups; ++cg) {
                 for (int i = 0; i < nsteps && ok; ++i, ++it) {
                     const int st = it % kStages;
+                    const bool cached = wregion != nullptr && i < wc_steps;
+                    const bool reuse = cached && cg > 0;
                     if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
-                    ok = ok && tc::mbar_wait(&ms.full_a[st], (it / kStages) & 1, err);
+                    if (!reuse) ok = ok && tc::mbar_wait(&ms.full_a[st], (it / kStages) & 1, err);
                     if (!ok) break;
+                    unsigned char* bst = base + st * kStageBytes + 2 * kAHalf;
+                    unsigned char* wstep = cached ? wregion + (size_t)i * kWcStepBytes : nullptr;
+                    if (reuse) {
+#pragma unroll
+                        for (int u2 = 0; u2 < kGpt; ++u2) {
+                            const int k = kq * kGpt + u2, r = k & 7;
+                            const uint32_t off = (k >> 3) * 2048 + (o >> 3) * 1024 + r * 128 + (((o & 7) ^ r) << 4);
+                            tc::cp_async16(tc::smem_u32(bst + off), wstep + off, 16u);
+                            tc::cp_async16(tc::smem_u32(bst + kBHalf + off), wstep + kBHalf + off, 16u);
+                        }
+                        tc::cp_async_mbar_arrive_noinc(&ms.full_w[st]);
+                        continue;
+                    }
                     const int k0 = i * kKStep;
 #pragma unroll
-                    for (int u2 = 0; u2 < 2; ++u2) {
-                        const int k = 2 * kp + u2;
+                    for (int u2 = 0; u2 < kGpt; ++u2) {
+                        const int k = kq * kGpt + u2;
                         const GParams& gp = ms.prm[st].g[k];
                         const float4 A = gp.w[0], P0 = gp.w[1], P1 = gp.w[2], P2 = gp.w[3], U = gp.w[4];
                         const bool live = k0 + k < K && vx >= __float_as_int(P2.y) && vx <= __float_as_int(U.x) &&
@@ -337,25 +380,28 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
                         tc::split_half2(w[6], w[7], h.w, l.w);
                         const int r = k & 7;
                         const uint32_t off = (k >> 3) * 2048 + (o >> 3) * 1024 + r * 128 + (((o & 7) ^ r) << 4);
-                        *reinterpret_cast<uint4*>(base + st * kStageBytes + 2 * kAHalf + off) = h;
-                        *reinterpret_cast<uint4*>(base + st * kStageBytes + 2 * kAHalf + kBHalf + off) = l;
+                        *reinterpret_cast<uint4*>(bst + off) = h;
+                        *reinterpret_cast<uint4*>(bst + kBHalf + off) = l;
+                        if (cached) {
+                            *reinterpret_cast<uint4*>(wstep + off) = h;
+                            *reinterpret_cast<uint4*>(wstep + kBHalf + off) = l;
+                        }
                     }
                     tc::fence_async_smem();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
+                    tc::mbar_arrive(&ms.full_w[st]);
                 }
                 if (cg == 0) {
-                    // density of the unit: sum over the 8 Gaussian pairs; vscale for the epilogue
+                    // density of the unit: sum over the thread groups; vscale for the epilogue
 #pragma unroll
-                    for (int lz = 0; lz < 8; ++lz) ms.dpart[kp][o * 8 + lz] = dsum[lz];
-                    weight_barrier();
+                    for (int lz = 0; lz < 8; ++lz) ms.dpart[kq][o * 8 + lz] = dsum[lz];
+                    weight_barrier<NW>();
                     const int b = nu & 1;
                     if (nu >= 2 && ok) ok = tc::mbar_wait(&ms.dfree[b], ((nu / 2) + 1) & 1, err);
                     if (t < kUV) {
                         const int v = t;  // voxel of the unit: (v >> 5, (v >> 3) & 3, v & 7)
                         float Ds = 0.0f;
 #pragma unroll
-                        for (int q = 0; q < kKStep / 2; ++q) Ds += ms.dpart[q][v];
+                        for (int q = 0; q < kNWW * 2; ++q) Ds += ms.dpart[q][v];
                         const float D = ldexpf(Ds, -kt);
                         ms.vscale[b][v] = ldexpf(1.0f, -kt) / fmaxf(D, kEps);
                         const int x = x0 + (v >> 5), y = y0 + ((v >> 3) & 3), z = z0 + (v & 7);
@@ -363,11 +409,12 @@ __global__ void __launch_bounds__(kThreads, 1) splat_tc_kernel(
                             density[grid_row(G, x, y, z)] = D;
                     }
                     tc::mbar_arrive(&ms.dready[b]);
-                    weight_barrier();  // dpart is reused by the next unit
+                    weight_barrier<NW>();  // dpart is reused by the next unit
                 }
             }
             ++nu;
         }
+        tc::cp_async_wait<0>();  // no copy in flight when the shared memory is released
     } else if (warp == kMmaWarp) {
         // ============ MMA thread ============
         if (lane == 0) {
@@ -529,8 +576,41 @@ int launch_pack_params(const float* means, const float* opacity, const float* co
 size_t splat_tc_split_bytes(int64_t n, int64_t C) {
     const int64_t Cp = (C + 7) / 8 * 8;
     return 2 * ((size_t)n * Cp * sizeof(__half) + 256) + 2 * ((size_t)Cp * 4 + 256) +
-           ((size_t)(n > 0 ? n : 1) * sizeof(GParams) + 256);
+           ((size_t)(n > 0 ? n : 1) * sizeof(GParams) + 256) + ((size_t)kMaxSplatCtas * kWcSteps * kWcStepBytes + 256);
 }
+
+namespace {
+// Weight warps of the splat kernel (G2V_SPLAT_WW=4 or 8, default 4: measured at cfg3 with the weight
+// cache, 1.16 ms with 4 and 1.22 ms with 8) and whether the weight cache is used (G2V_SPLAT_WCACHE=0
+// turns it off: 1.60 / 1.46 ms).
+int splat_weight_warps() {
+    const char* e = getenv("G2V_SPLAT_WW");
+    return (e && atoi(e) == 8) ? 8 : 4;
+}
+bool splat_weight_cache() {
+    const char* e = getenv("G2V_SPLAT_WCACHE");
+    return !(e && e[0] == '0');
+}
+template <int NW>
+int launch_splat_kernel(bool tma, const CUtensorMap& omap, const __half* hi, const __half* lo, const float* unscale,
+                        int C, int Cp, const GParams* gp, const int32_t* unit_offsets, const int32_t* unit_lists,
+                        int num_units, int tile_x_begin, const Grid& G, float* density, float* grid_feats,
+                        unsigned char* wcache, int* err, cudaStream_t s) {
+    auto kern = tma ? splat_tc_kernel<true, NW> : splat_tc_kernel<false, NW>;
+    G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    int dev = 0, sms = 148;
+    G2V_CUDA(cudaGetDevice(&dev));
+    G2V_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    int grid = num_units < sms ? num_units : sms;
+    if (grid > kMaxSplatCtas) grid = kMaxSplatCtas;  // the weight cache holds kMaxSplatCtas regions
+    G2V_TIMED("splat_tc_kernel", s,
+              kern<<<(unsigned)grid, Roles<NW>::kThreads, kSmemBytes, s>>>(
+                  omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units, tile_x_begin, G, density,
+                  grid_feats, wcache, kWcSteps, err));
+    G2V_LAUNCH_CHECK("splat_tc_kernel");
+    return 0;
+}
+}  // namespace
 
 // Splits the features (per-channel power-of-two scale) into `split` (splat_tc_split_bytes) and runs the
 // tensor-core splat over the units (z pairs of tiles) of the slab [tile_x_begin, tile_x_end).
@@ -559,24 +639,20 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
         G2V_LAUNCH_CHECK("feature_split_kernel");
     }
     GParams* gp = cv.take<GParams>((size_t)(n > 0 ? n : 1));
+    unsigned char* wcache = cv.take<unsigned char>((size_t)kMaxSplatCtas * kWcSteps * kWcStepBytes);
     int rc = launch_pack_params(means, opacity, cov_inv, lb, ub, n, gp, s);
     if (rc) return rc;
     CUtensorMap omap;
     memset(&omap, 0, sizeof(omap));
     const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
     const bool tma = C > 0 && encode_grid_rows_f32(&omap, grid_feats, ldims, C, kCG, 8, 2, 1);
-    auto kern = tma ? splat_tc_kernel<true> : splat_tc_kernel<false>;
-    G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    int dev = 0, sms = 148;
-    G2V_CUDA(cudaGetDevice(&dev));
-    G2V_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int grid = num_units < sms ? num_units : sms;
-    G2V_TIMED("splat_tc_kernel", s,
-              kern<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(omap, hi, lo, unscale, C, Cp, gp, unit_offsets,
-                                                                            unit_lists, num_units, tile_x_begin, G,
-                                                                            density, grid_feats, err));
-    G2V_LAUNCH_CHECK("splat_tc_kernel");
-    return 0;
+    unsigned char* wc = splat_weight_cache() ? wcache : nullptr;
+    if (splat_weight_warps() == 4)
+        return launch_splat_kernel<4>(tma, omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units,
+                                      tile_x_begin, G, density, grid_feats, wc, err, s);
+    return launch_splat_kernel<8>(tma, omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units,
+                                  tile_x_begin, G, density, grid_feats, wc, err, s);
 }
 
 }  // namespace g2v
+
