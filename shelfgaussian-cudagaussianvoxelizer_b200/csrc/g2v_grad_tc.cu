@@ -250,51 +250,79 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             }
         } else if (warp < 16) {
             // ---------------- weight warps: thread = slot t, the 16 voxels of the step's x-slice -----------
+            // Over a tile the base-2 exponent of the weight is a quadratic in the local voxel (ks, ly, lz):
+            //   k (d0 + h l)^T P (d0 + h l),  k = -log2(e) / 2,  d0 = tile-origin voxel centre - mean,
+            // so its 10 coefficients are formed once per tile (the first of its 4 x-slice steps) and each
+            // step only adds the ks terms.  The y / z box masks of the tile are 0 / -inf terms added per
+            // (ly, lz), the x mask decides the whole slice.  Voxel centres are linear within a tile (a tile
+            // never spans two stacked scenes).
             const int t = tid - 256;
+            const bool trow = t < nn;  // rows >= N are not read by the MMAs
+            const bool slot = t < ns;
+            const float k = tc::kNegHalfLog2e;
+            const float hx = G.h[0], hy = G.h[1], hz = G.h[2];
+            float opa = 0.0f, A0 = 0.0f, Bx = 0.0f, By = 0.0f, Bz = 0.0f;
+            float Qxx = 0.0f, Qyy = 0.0f, Qzz = 0.0f, Qxy = 0.0f, Qxz = 0.0f, Qyz = 0.0f;
+            float my[4], mz[4];
+            int xlo = 1, xhi = 0;
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
-                int x0, y0, z0, ks;
-                step_geom(j, x0, y0, z0, ks);
+                const int ks = j & 3;
+                if (ks == 0 && trow) {
+                    const int4 o = ms.org[j >> 2];
+                    const GParams& gp = ms.prm[t];
+                    const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
+                    // P = [[b.x b.y b.z] [b.w c.x c.y] [c.z c.w d.x]]
+                    const float dx = voxel_centre(G, 0, o.x) - a.x, dy = voxel_centre(G, 1, o.y) - a.y;
+                    const float dz = voxel_centre(G, 2, o.z) - a.z;
+                    const float qx = b.x * dx + b.y * dy + b.z * dz;    // (P d0)
+                    const float qy = b.w * dx + c.x * dy + c.y * dz;
+                    const float qz = c.z * dx + c.w * dy + d.x * dz;
+                    const float ptx = b.x * dx + b.w * dy + c.z * dz;   // (P^T d0)
+                    const float pty = b.y * dx + c.x * dy + c.w * dz;
+                    const float ptz = b.z * dx + c.y * dy + d.x * dz;
+                    opa = a.w;
+                    A0 = k * (dx * qx + dy * qy + dz * qz);
+                    Bx = k * hx * (qx + ptx);
+                    By = k * hy * (qy + pty);
+                    Bz = k * hz * (qz + ptz);
+                    Qxx = k * hx * hx * b.x;
+                    Qyy = k * hy * hy * c.x;
+                    Qzz = k * hz * hz * d.x;
+                    Qxy = k * hx * hy * (b.y + b.w);
+                    Qxz = k * hx * hz * (b.z + c.z);
+                    Qyz = k * hy * hz * (c.y + c.w);
+                    xlo = __float_as_int(d.y) - o.x;
+                    xhi = __float_as_int(e4.x) - o.x;
+                    const int ylo = __float_as_int(d.z) - o.y, yhi = __float_as_int(e4.y) - o.y;
+                    const int zlo = __float_as_int(d.w) - o.z, zhi = __float_as_int(e4.z) - o.z;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        my[i] = (i >= ylo && i <= yhi) ? 0.0f : -INFINITY;
+                        mz[i] = (i >= zlo && i <= zhi) ? 0.0f : -INFINITY;
+                    }
+                }
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                 if (!ok) break;
-                const int x = x0 + ks;
-                if (t < nn) {  // rows >= N are not read by the MMAs
+                if (trow) {
                 float w[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) w[e] = 0.0f;
-                const GParams& gp = ms.prm[t];
-                const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
-                const bool live = t < ns && x >= __float_as_int(d.y) && x <= __float_as_int(e4.x);
-                if (live) {
-                    const float cx = voxel_centre(G, 0, x), cy0 = voxel_centre(G, 1, y0), cz0 = voxel_centre(G, 2, z0);
-                    const float hy = G.h[1], hz = G.h[2];
-                    const int ylo = __float_as_int(d.z) - y0, yhi = __float_as_int(e4.y) - y0;
-                    const int zlo = __float_as_int(d.w) - z0, zhi = __float_as_int(e4.z) - z0;
-                    const float dx = cx - a.x, dy = cy0 - a.y, dz = cz0 - a.z;
-                    const float qx = b.x * dx + b.y * dy + b.z * dz;
-                    const float qy = b.w * dx + c.x * dy + c.y * dz;
-                    const float qz = c.z * dx + c.w * dy + d.x * dz;
-                    const float pty = b.y * dx + c.x * dy + c.w * dz;  // (P^T d)_y
-                    const float ptz = b.z * dx + c.y * dy + d.x * dz;  // (P^T d)_z
-                    // base-2 exponent of voxel (ly, lz):
-                    //   k (A + By ly + Qyy ly^2 + (Bz + Qyz ly) lz + Qzz lz^2) + log2(1 / den_v),  k = -log2(e) / 2
-                    const float k = tc::kNegHalfLog2e;
-                    const float A = k * (dx * qx + dy * qy + dz * qz);
-                    const float By = k * hy * (qy + pty), Bz = k * hz * (qz + ptz);
-                    const float Qyy = k * hy * hy * c.x, Qzz = k * hz * hz * d.x, Qyz = k * hy * hz * (c.y + c.w);
+                if (slot && ks >= xlo && ks <= xhi) {
+                    const float fk = (float)ks;
+                    const float Ak = fmaf(fmaf(Qxx, fk, Bx), fk, A0);
+                    const float Byk = fmaf(Qxy, fk, By), Bzk = fmaf(Qxz, fk, Bz);
                     const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[(j >> 2) * kVoxPerTile + ks * 16]);
 #pragma unroll
                     for (int ly = 0; ly < 4; ++ly) {
-                        const float4 L = L4[ly];  // the 4 voxels (ly, 0..3); box mask: -inf outside
-                        const float my = (ly >= ylo && ly <= yhi) ? 0.0f : -INFINITY;
-                        const float Ay = fmaf(fmaf(Qyy, (float)ly, By), (float)ly, A) + my;
-                        const float By2 = fmaf(Qyz, (float)ly, Bz);
-                        const float Lz[4] = {L.x, L.y, L.z, L.w};
+                        const float4 L = L4[ly];  // log2(1 / den) of the 4 voxels (ly, 0..3); -inf outside the grid
+                        const float Ay = fmaf(fmaf(Qyy, (float)ly, Byk), (float)ly, Ak) + my[ly];
+                        const float Bz2 = fmaf(Qyz, (float)ly, Bzk);
+                        const float Lz[4] = {L.x + mz[0], L.y + mz[1], L.z + mz[2], L.w + mz[3]};
 #pragma unroll
                         for (int lz = 0; lz < 4; ++lz) {
-                            const float mz = (lz >= zlo && lz <= zhi) ? Lz[lz] : -INFINITY;
-                            const float m = fmaf(fmaf(Qzz, (float)lz, By2), (float)lz, Ay) + mz;
-                            w[ly * 4 + lz] = a.w * tc::exp2_approx(m);
+                            const float m = fmaf(fmaf(Qzz, (float)lz, Bz2), (float)lz, Ay) + Lz[lz];
+                            w[ly * 4 + lz] = opa * tc::exp2_approx(m);
                         }
                     }
                 }
@@ -393,10 +421,22 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
 }
 }  // namespace
 
+int launch_fpass_tc_pair(const float* grad_feats, int C, const float* density, const GParams* gparams,
+                         const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets,
+                         int bx_begin, int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end,
+                         const Grid& G, float* partialF, int64_t block_pair_cap, int* err, cudaStream_t s);
+
+// The feature-gradient pass: one CTA per (block, 256-channel group) with passes of 256 slots (the
+// kernel above, the default) or, with G2V_FPASS=pair, on CTA pairs with passes of 512 slots
+// (g2v_fpass_pair.cu; correct, measured slower at cfg3: 2.24 vs 1.81 ms).
 int launch_fpass_tc(const float* grad_feats, int C, const float* density, const GParams* gparams,
                     const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
                     int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
                     int64_t block_pair_cap, int* err, cudaStream_t s) {
+    const char* mode = getenv("G2V_FPASS");
+    if (mode && strcmp(mode, "pair") == 0)
+        return launch_fpass_tc_pair(grad_feats, C, density, gparams, block_offsets, block_lists, g2b_offsets, bx_begin,
+                                    nbx, nby, nbz, B, tx_begin, tx_end, G, partialF, block_pair_cap, err, s);
     const int64_t nblocks = (int64_t)nbx * nby * nbz;
     if (nblocks <= 0 || C <= 0) return 0;
     const int ngroups = (C + kCG - 1) / kCG;
