@@ -59,14 +59,14 @@ struct FMisc {
     int fail;
     uint64_t gfull[kGS];   // TMA bytes of a staged step
     uint64_t gempty[kGS];  // 8 converter-warp arrivals
-    alignas(16) GParams prm[kSlots];
+    alignas(16) GParams prm[kSlots];  // slot records of the pass (each weight thread stages its own)
     int64_t rowoff[kSlots];
     alignas(16) float lrd[kMaxBlockTiles * kVoxPerTile];  // log2(1 / max(D, eps)), -inf outside the grid
     int4 org[kMaxBlockTiles];  // voxel origin of each tile of the block, in step order
 };
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(FMisc);
 static_assert(kSmemBytes <= 227 * 1024, "fpass_tc_kernel shared memory");
-static_assert(offsetof(FMisc, prm) % 16 == 0, "GParams records are read as float4");
+static_assert(offsetof(FMisc, lrd) % 16 == 0, "lrd is read as float4");
 
 template <bool kTma>
 __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
@@ -115,18 +115,6 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         if (tid == 0) atomicOr(err, 4);
         return;
     }
-    // log2(1 / max(D, eps)) of every voxel of the block's tiles (tile order of the steps)
-    for (int i = tid; i < ntiles * kVoxPerTile; i += kThreads) {
-        const int t = i >> 6;
-        int lx, ly, lz;
-        local_voxel(i & 63, lx, ly, lz);
-        const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
-        const int x = (txa + txi) * kTile + lx, y = (tya + tyi) * kTile + ly, z = (tza + tzi) * kTile + lz;
-        float r = -INFINITY;
-        if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
-            r = -log2f(fmaxf(density[grid_row(G, x, y, z)], kEps));
-        ms.lrd[i] = r;
-    }
     for (int t = tid; t < ntiles; t += kThreads) {
         const int tzi = t % ntz, tyi = (t / ntz) % nty, txi = t / (ntz * nty);
         ms.org[t] = make_int4((txa + txi) * kTile, (tya + tyi) * kTile, (tza + tzi) * kTile, 0);
@@ -173,29 +161,6 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         const int p0 = pass * kSlots, ns = min(kSlots, Kb - p0);
         const int nn = (ns + 15) & ~15;  // MMA N of this pass
         const uint32_t idesc = tc::idesc_bf16_f32(128, nn, /*A MN-major*/ 1, /*B K-major*/ 0);
-        // slot parameters and partial-row offsets for this pass
-        for (int i = tid; i < kSlots * 5; i += kThreads) {
-            const int sl = i / 5, wq = i - sl * 5;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (sl < ns) v = gparams[block_lists[s0 + p0 + sl]].w[wq];
-            ms.prm[sl].w[wq] = v;
-        }
-        for (int sl = tid; sl < kSlots; sl += kThreads) {
-            int64_t ro = -1;
-            if (sl < ns) {
-                const int g = block_lists[s0 + p0 + sl];
-                const GParams& gp = gparams[g];
-                const int lbx = __float_as_int(gp.w[3].y), lby = __float_as_int(gp.w[3].z), lbz = __float_as_int(gp.w[3].w);
-                const int ubx = __float_as_int(gp.w[4].x), uby = __float_as_int(gp.w[4].y), ubz = __float_as_int(gp.w[4].z);
-                const int blx = (lbx / kTile) / BX, bly = (lby / kTile) / BY, blz = (lbz / kTile) / BZ;
-                const int ey = (uby / kTile) / BY - bly + 1, ez = (ubz / kTile) / BZ - blz + 1;
-                ro = (int64_t)g2b_offsets[g] + ((bx - blx) * ey + (by - bly)) * ez + (bz - blz);
-                if (ro >= block_pair_cap) ro = -1;  // offsets come from the caller
-            }
-            ms.rowoff[sl] = ro;
-        }
-        __syncthreads();
-
         if (warp < 8) {
             // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 2 voxel rows) ----------
             const int jc = lane;                                     // channels c0 + 8 jc .. + 7
@@ -248,6 +213,22 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
                 }
             }
+            // partial-row offsets of the pass's slots for the epilogue, while the last MMAs run
+            {
+                const int sl = tid;  // 256 converter threads, one slot each
+                int64_t ro = -1;
+                if (sl < ns) {
+                    const int g = block_lists[s0 + p0 + sl];
+                    const GParams& gp = gparams[g];
+                    const int lbx = __float_as_int(gp.w[3].y), lby = __float_as_int(gp.w[3].z), lbz = __float_as_int(gp.w[3].w);
+                    const int uby = __float_as_int(gp.w[4].y), ubz = __float_as_int(gp.w[4].z);
+                    const int blx = (lbx / kTile) / BX, bly = (lby / kTile) / BY, blz = (lbz / kTile) / BZ;
+                    const int ey = (uby / kTile) / BY - bly + 1, ez = (ubz / kTile) / BZ - blz + 1;
+                    ro = (int64_t)g2b_offsets[g] + ((bx - blx) * ey + (by - bly)) * ez + (bz - blz);
+                    if (ro >= block_pair_cap) ro = -1;  // offsets come from the caller
+                }
+                ms.rowoff[sl] = ro;
+            }
         } else if (warp < 16) {
             // ---------------- weight warps: thread = slot t, the 16 voxels of the step's x-slice -----------
             // Over a tile the base-2 exponent of the weight is a quadratic in the local voxel (ks, ly, lz):
@@ -259,6 +240,27 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             const int t = tid - 256;
             const bool trow = t < nn;  // rows >= N are not read by the MMAs
             const bool slot = t < ns;
+            if (pass == 0) {
+                // log2(1 / max(D, eps)) of every voxel of the block's tiles (tile order of the steps); only
+                // the weight warps read it, so only they wait for it (named barrier 2)
+                for (int i = t; i < ntiles * kVoxPerTile; i += 256) {
+                    const int ti = i >> 6;
+                    int lx, ly, lz;
+                    local_voxel(i & 63, lx, ly, lz);
+                    const int tzi = ti % ntz, tyi = (ti / ntz) % nty, txi = ti / (ntz * nty);
+                    const int x = (txa + txi) * kTile + lx, y = (tya + tyi) * kTile + ly, z = (tza + tzi) * kTile + lz;
+                    float r = -INFINITY;
+                    if (x < G.dims[0] && y < G.dims[1] && z < G.dims[2])
+                        r = -log2f(fmaxf(density[grid_row(G, x, y, z)], kEps));
+                    ms.lrd[i] = r;
+                }
+                asm volatile("bar.sync 2, 256;" ::: "memory");
+            }
+            if (trow) {  // this thread's slot record, read at each tile of the pass
+                const GParams& src = gparams[slot ? block_lists[s0 + p0 + t] : 0];
+#pragma unroll
+                for (int wq = 0; wq < 5; ++wq) ms.prm[t].w[wq] = src.w[wq];
+            }
             const float k = tc::kNegHalfLog2e;
             const float hx = G.h[0], hy = G.h[1], hz = G.h[2];
             float opa = 0.0f, A0 = 0.0f, Bx = 0.0f, By = 0.0f, Bz = 0.0f;
@@ -392,19 +394,30 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         tc::tc_fence_before();
         __syncthreads();
         tc::tc_fence_after();
-        // epilogue: warp w < 8 reads lanes 32*(w%4).. (channels) of M-block w/4, 256 slot columns
-        if (warp < 8 && !ms.fail) {
-            const int q = warp & 3, mb = warp >> 2;
+        // epilogue: warp w < 16 reads lanes 32*(w%4).. (channels) of M-block (w/4)%2, slot columns
+        // 128*(w/8) .. +127; the next 16 columns load from TMEM while the current ones are stored
+        if (warp < 16 && !ms.fail) {
+            const int q = warp & 3, mb = (warp >> 2) & 1, half = warp >> 3;
             const int c = c0 + mb * 128 + q * 32 + lane;
-            for (int jc = 0; jc < kSlots / 16; ++jc) {
-                if (jc * 16 >= ns) break;  // warp-uniform
-                float vals[16];
-                tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + mb * kSlots + jc * 16, vals);
-                if (c < C) {
+            const int jc0 = half * 8, jc1 = min(half * 8 + 8, (ns + 15) >> 4);  // warp-uniform
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + mb * kSlots;
+            if (jc0 < jc1) {
+                float va[16], vb[16];
+                tc::tmem_ld16(tbase + jc0 * 16, va);
+                for (int jc = jc0; jc < jc1; ++jc) {
+                    const bool more = jc + 1 < jc1;
+                    if (more) tc::tmem_ld16_nowait(tbase + (jc + 1) * 16, vb);
+                    if (c < C) {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int64_t ro = ms.rowoff[jc * 16 + e];
-                        if (ro >= 0) partialF[ro * C + c] = vals[e];
+                        for (int e = 0; e < 16; ++e) {
+                            const int64_t ro = ms.rowoff[jc * 16 + e];
+                            if (ro >= 0) partialF[ro * C + c] = va[e];
+                        }
+                    }
+                    if (more) {
+                        tc::tmem_wait_ld16(vb);
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) va[e] = vb[e];
                     }
                 }
             }
