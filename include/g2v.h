@@ -346,12 +346,19 @@ G2V_API int g2v_cosine_loss_backward(const float* grad_loss, const int32_t* coun
                                      float* grad_grid_feats, void* stream);
 
 /*
- * Debug / parity hook: the Tile->Gaussian CSR built by g2v_forward_splat for the whole grid, copied
- * out of the splat workspace after the call: tile_offsets (num_tiles+1, int32) and t2g_gaussians
- * (M, int32).  No reference counterpart (the reference keeps this map internal, cu:1675-1772).
+ * The reference's Tile->Gaussian CSR over the whole grid, built from the forward's boxes: the stable
+ * sort of the (tile id, Gaussian id) pairs by tile, run-length encoding and scan of
+ * src/cuda_gaussian_voxelizer.cu:1675-1772 (CUB there; the reference keeps the map internal).
+ * tile_offsets (num_tiles+1, int32, all tiles), t2g_gaussians (num_pairs, int32, Gaussian ids ascending
+ * within each tile).  The tensor-core splat does not need this map (it lists z pairs of tiles), so the
+ * forward no longer builds it; this call exposes it.  workspace: g2v_build_t2g_workspace_size.
  */
-G2V_API int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs,
-                       const int dims[3], int32_t* tile_offsets, int32_t* t2g_gaussians, void* stream);
+G2V_API int g2v_build_t2g_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3],
+                                         size_t* bytes);
+G2V_API int g2v_build_t2g(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, int64_t num_gaussians,
+                          const float voxel_size[3], const float voxel_range[6], int64_t num_pairs,
+                          int32_t* tile_offsets, int32_t* t2g_gaussians, void* workspace, size_t workspace_bytes,
+                          void* stream);
 
 /*
  * Device error word (no reference counterpart): the tensor-core kernels never spin without a bound;

@@ -240,8 +240,12 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
             nt = tiles[0] * tiles[1] * tiles[2]
             toff = torch.empty((nt + 1,), **i32)
             t2g = torch.empty((max(m, 1),), **i32)
-            _lib.check(lib.g2v_debug_copy_t2g(_ptr(ws2), n, m, _lib.i3((X, Y, Z)), _ptr(toff), _ptr(t2g), sptr),
-                       "g2v_debug_copy_t2g")
+            tb = ctypes.c_size_t()
+            _lib.check(lib.g2v_build_t2g_workspace_size(n, m, _lib.i3((X, Y, Z)), ctypes.byref(tb)),
+                       "g2v_build_t2g_workspace_size")
+            ws3 = _workspace(tb.value, dev)
+            _lib.check(lib.g2v_build_t2g(_ptr(lb), _ptr(ub), n, _lib.f3(size_h), _lib.f6(range_h), m, _ptr(toff),
+                                         _ptr(t2g), _ptr(ws3), ws3.numel(), sptr), "g2v_build_t2g")
             return out, (toff, t2g[:m])
         return out
 
@@ -259,7 +263,8 @@ def gaussian_voxelizer_forward(means3D, opacity, covariances, voxel_size, voxel_
 
 
 def t2g_maps(means3D, opacity, covariances, voxel_size, voxel_range, features=None):
-    """Forward outputs plus the Tile->Gaussian CSR built by the splat: (outputs, (tile_offsets, t2g_gaussians))."""
+    """Forward outputs plus the reference's Tile->Gaussian CSR (g2v_build_t2g on the forward's boxes):
+    (outputs, (tile_offsets, t2g_gaussians))."""
     return _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, False, keep_t2g=True)
 
 

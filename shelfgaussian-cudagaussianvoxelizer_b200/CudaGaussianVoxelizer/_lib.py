@@ -58,7 +58,8 @@ SIGNATURES = {
     "g2v_cosine_loss_workspace_size": (I32, [I64, ctypes.POINTER(SZ)]),
     "g2v_cosine_loss_forward": (I32, [P, P, P, P, I64, I64, P, P, P, SZ, P]),
     "g2v_cosine_loss_backward": (I32, [P, P, I32, P, P, P, P, I64, I64, P, P]),
-    "g2v_debug_copy_t2g": (I32, [P, I64, I64, I3, P, P, P]),
+    "g2v_build_t2g_workspace_size": (I32, [I64, I64, I3, ctypes.POINTER(SZ)]),
+    "g2v_build_t2g": (I32, [P, P, I64, F3, F6, I64, P, P, P, SZ, P]),
     "g2v_device_error": (I32, [P, ctypes.POINTER(I32)]),
     "g2v_debug_wait_timeout": (I32, [P, ctypes.POINTER(I32)]),
     "g2v_profile_enable": (I32, [I32]),

@@ -33,6 +33,8 @@ int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid
                      int64_t list_cap, int* err);
 int count_gaussian_cells(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                          int32_t* per_gaussian, int32_t* dummy_counts, cudaStream_t s);
+int fill_g2t(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int32_t* g2t_offsets,
+             int32_t* g2t_tile_ids, int64_t g2t_cap, cudaStream_t s);
 int launch_splat_simt(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
                       const int32_t* ub, const float* features, int C, const int32_t* tile_offsets,
                       const int32_t* tile_lists, int first_tile, int num_tiles, const Grid& G, float* density,
@@ -476,13 +478,20 @@ static int forward_splat_impl(const float* means3d, const float* opacity, const 
     int* err = nullptr;
     if ((rc = device_error_ptr(&err))) return rc;
     const int one[3] = {1, 1, 1};
-    if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
-                               tile_x_end, g2t_offsets, g2t_tile_ids, num_pairs, nullptr, w.counts, w.tile_offsets, w.unsorted,
-                               w.lists, w.scan, w.total, s, num_pairs, err)))
+    const bool tcore = features != nullptr && C > 0 && use_tensor_cores();
+    // the reference's G2T tile ids; the per-tile Gaussian lists only for the FP32-FMA splat (the
+    // tensor-core splat lists z pairs of tiles; g2v_build_t2g builds the per-tile map on request)
+    if (tcore) {
+        if ((rc = fill_g2t(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, g2t_offsets, g2t_tile_ids, num_pairs, s)))
+            return rc;
+    } else if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, tile_x_begin,
+                                      tile_x_end, g2t_offsets, g2t_tile_ids, num_pairs, nullptr, w.counts,
+                                      w.tile_offsets, w.unsorted, w.lists, w.scan, w.total, s, num_pairs, err))) {
         return rc;
+    }
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
-    if (features != nullptr && C > 0 && use_tensor_cores()) {
+    if (tcore) {
         // unit lists: z pairs of tiles, Gaussian ids ascending (at most M entries over fewer cells)
         int cell[3], ncells[3];
         spass_tc_unit_shape(G, cell, ncells);
@@ -521,24 +530,44 @@ int g2v_forward_splat_local(const float* means3d, const float* opacity, const fl
                               grid_feats, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream, true);
 }
 
-int g2v_debug_copy_t2g(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs, const int dims[3],
-                       int32_t* tile_offsets, int32_t* t2g_gaussians, void* stream) {
-    (void)num_gaussians;
-    if (!splat_workspace || !dims || !tile_offsets || (num_pairs > 0 && !t2g_gaussians)) {
+int g2v_build_t2g_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3], size_t* bytes) {
+    if (!bytes || !dims || num_gaussians < 0 || num_pairs < 0) {
         set_error("invalid argument");
         return G2V_ERROR_INVALID_VALUE;
     }
     const int64_t ntiles = (int64_t)((dims[0] + 3) / 4) * ((dims[1] + 3) / 4) * ((dims[2] + 3) / 4);
-    Carver c(const_cast<void*>(splat_workspace));
+    Carver c(nullptr);
     T2GWs w;
     carve_t2g(c, ntiles, num_pairs, w);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    G2V_CUDA(cudaMemcpyAsync(tile_offsets, w.tile_offsets, sizeof(int32_t) * (size_t)(ntiles + 1),
-                             cudaMemcpyDeviceToDevice, s));
-    if (num_pairs > 0)
-        G2V_CUDA(cudaMemcpyAsync(t2g_gaussians, w.lists, sizeof(int32_t) * (size_t)num_pairs,
-                                 cudaMemcpyDeviceToDevice, s));
+    *bytes = c.bytes();
     return G2V_SUCCESS;
+}
+
+int g2v_build_t2g(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, int64_t num_gaussians,
+                  const float voxel_size[3], const float voxel_range[6], int64_t num_pairs, int32_t* tile_offsets,
+                  int32_t* t2g_gaussians, void* workspace, size_t workspace_bytes, void* stream) {
+    g_msg[0] = 0;
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if (num_gaussians < 0 || num_pairs < 0 || !tile_offsets || (num_pairs > 0 && !t2g_gaussians) ||
+        (num_gaussians > 0 && (!valid_voxel_lb || !valid_voxel_ub))) {
+        set_error("g2v_build_t2g: invalid pointer or size");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    size_t need = 0;
+    g2v_build_t2g_workspace_size(num_gaussians, num_pairs, G.dims, &need);
+    if ((rc = need_ws(need, workspace_bytes, workspace))) return rc;
+    Carver c(workspace);
+    T2GWs w;
+    const int64_t ntiles = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
+    carve_t2g(c, ntiles, num_pairs, w);
+    int* err = nullptr;
+    if ((rc = device_error_ptr(&err))) return rc;
+    const int one[3] = {1, 1, 1};
+    return build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, one, G.tiles, 0, G.tiles[0], nullptr,
+                            nullptr, 0, nullptr, w.counts, tile_offsets, w.unsorted, t2g_gaussians, w.scan, w.total,
+                            static_cast<cudaStream_t>(stream), num_pairs, err);
 }
 
 int g2v_debug_wait_timeout(void* stream, int* gave_up) {

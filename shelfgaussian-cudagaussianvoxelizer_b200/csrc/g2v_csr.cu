@@ -250,6 +250,20 @@ int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid
     return 0;
 }
 
+// The reference's G2T tile ids only (FillG2TKernel, cu:228-286), without the Tile->Gaussian lists:
+// the tensor-core splat works on its own unit lists.  Nothing is counted (empty listing range).
+int fill_g2t(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int32_t* g2t_offsets,
+             int32_t* g2t_tile_ids, int64_t g2t_cap, cudaStream_t s) {
+    if (n == 0) return 0;
+    const int64_t threads = n * 32;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    G2V_TIMED("cells_count_kernel", s, cells_count_kernel<<<blocks, 256, 0, s>>>(lb, ub, n, G, 1, 1, 1, 1, 1, 0, 0,
+                                                                              g2t_offsets, g2t_tile_ids, g2t_cap,
+                                                                              nullptr, nullptr));
+    G2V_LAUNCH_CHECK("cells_count_kernel");
+    return 0;
+}
+
 // Per-Gaussian cell counts only (for sizing the backward's block partial rows).
 int count_gaussian_cells(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                          int32_t* per_gaussian, int32_t* dummy_counts, cudaStream_t s) {
