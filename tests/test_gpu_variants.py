@@ -125,3 +125,54 @@ def test_tensor_core_backward_matches_oracle_and_fp32_variant(n, c, seed, half, 
     ref = oracle.backward(m, o, cv, f, lb_h, ub_h, size, rng, dims, gD.numpy(), gF.numpy(), dref, fref, x_range=xr)
     for name, a, b in zip(names, tc, ref):
         assert_close(name, a, b)
+
+
+@pytest.mark.parametrize("n,c,seed,half,var_max", [
+    (300, 24, 1, 6.0, 2.5),      # one pair pass, the peer CTA's channels all beyond C
+    (3000, 300, 3, 6.0, 8.0),    # blocks of > 256 and > 512 Gaussians (two slot ranges, several passes)
+    (2000, 37, 2, 8.0, 2.5),     # C not a multiple of 4 (converters load the gradient rows themselves)
+])
+def test_feature_gradient_pair_variant_matches_default(n, c, seed, half, var_max):
+    """G2V_FPASS=pair (CTA pairs sharing each MMA, cta_group::2) gives the default kernel's gradients."""
+    from CudaGaussianVoxelizer import _C
+    size, rng = [0.4] * 3, [-half, -half, -1.0, half, half, 5.4]
+    m, o, cv, f = oracle.generate_inputs(n, c, rng, seed=seed, num_outside=n // 20, var_max=var_max)
+    dims = oracle.grid_shape(size, rng)[0]
+    g = torch.Generator().manual_seed(seed + 7)
+    gD, gF = torch.randn(*dims, generator=g).cuda(), torch.randn(*dims, c, generator=g).cuda()
+    mt, ot, ct, ft = dev(m.numpy(), o.numpy(), cv.numpy(), f.numpy())
+    density, cov_inv, lb, ub, nvox, grid_feats, off, ids, _ = _C.gaussian_voxelizer_forward(mt, ot, ct, size, rng, ft)
+
+    def bwd():
+        return [t.cpu().numpy() for t in _C.gaussian_voxelizer_backward(
+            gD, gF, mt, ot, cov_inv, size, rng, lb, ub, nvox, off, ids, density, grid_feats, ft)[:4]]
+
+    single = _with_env({"G2V_FPASS": "single"}, bwd)
+    pair = _with_env({"G2V_FPASS": "pair"}, bwd)
+    for name, a, b in zip(("grad_means", "grad_cov", "grad_opacity"), pair[:3], single[:3]):
+        np.testing.assert_array_equal(a, b, err_msg=name)  # the feature pass does not touch these
+    assert_close("grad_features pair vs single", pair[3], single[3])
+    lb_h, ub_h = lb.cpu().numpy(), ub.cpu().numpy()
+    m, o, cv, f = m.numpy(), o.numpy(), cv.numpy(), f.numpy()
+    dref, fref = oracle.forward(m, o, cv, f, lb_h, ub_h, size, rng, dims)
+    ref = oracle.backward(m, o, cv, f, lb_h, ub_h, size, rng, dims, gD.cpu().numpy(), gF.cpu().numpy(), dref, fref)
+    assert_close("grad_features (pair)", pair[3], ref[3])
+
+
+@pytest.mark.parametrize("env", [{"G2V_SPLAT_WW": "8"}, {"G2V_SPLAT_WCACHE": "0"},
+                                 {"G2V_SPLAT_WW": "8", "G2V_SPLAT_WCACHE": "0"}])
+def test_splat_weight_variants_match_default(env):
+    """The weight cache changes where the weights come from, not their values: bit-identical.  Eight weight
+    warps sum the density over a different grouping of the Gaussians: within the parity bar."""
+    rng = [-10.0, -10.0, -1.0, 10.0, 10.0, 5.4]
+    m, o, cv, f = oracle.generate_inputs(3000, 600, rng, seed=11, num_outside=150)
+    args = (m.numpy(), o.numpy(), cv.numpy(), f.numpy(), [0.4] * 3, rng)
+    ref = _forward("tc", *args)
+    got = _with_env(env, lambda: _forward("tc", *args))
+    if "G2V_SPLAT_WW" in env:
+        assert_close("density", got[0], ref[0], rtol=1e-6)
+        assert_close("grid_feats", got[5], ref[5])
+        same_ww = _with_env({"G2V_SPLAT_WW": env["G2V_SPLAT_WW"]}, lambda: _forward("tc", *args))
+        ref = same_ww
+    np.testing.assert_array_equal(got[0], ref[0])
+    np.testing.assert_array_equal(got[5], ref[5])
