@@ -13,8 +13,8 @@
 //     Gaussians no longer stream and convert their gradient rows a second time.
 // The leader (rank 0) issues the MMAs after both CTAs' producers arrived on its stage barriers (remote
 // arrives through shared::cluster addresses, release/acquire at cluster scope); its commits arrive on
-// the stage-free and accumulator-ready barriers of both CTAs (tcgen05.commit multicast).  The gradient
-// rows are loaded by each CTA into its own staging ring (TMA, no multicast).  Every wait is bounded; the
+// the stage-free and accumulator-ready barriers of both CTAs (one tcgen05.commit for both).  The gradient
+// rows are loaded by each CTA into its own staging ring (a plain per-CTA tiled load).  Every wait is bounded; the
 // pair always reaches its closing cluster barrier, also after a wait gave up.
 #include <cstddef>
 

@@ -349,7 +349,8 @@ namespace tc {
 // (rank 0) issues the MMAs; the A operand's M rows and the B operand's N columns are split between the
 // two CTAs' shared memory at the same offsets, and each CTA's TMEM holds the accumulator rows of its own
 // A rows.  Producers of both CTAs arrive on the leader's mbarriers through shared::cluster addresses;
-// the leader's commits arrive on the same barrier offset in both CTAs (multicast).  No TMA multicast.
+// the leader's commits arrive on the same barrier offset in both CTAs.  Every load of the pair is a plain
+// per-CTA load.
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
