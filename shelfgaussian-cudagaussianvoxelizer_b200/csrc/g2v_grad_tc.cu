@@ -363,20 +363,21 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             }
         } else if (warp == 16 && lane == 0) {
             // ---------------- MMA thread ----------------
+            const uint64_t adesc0 = tc::smem_desc(tc::smem_u32(a_stage(0, 0)), 1024, 2048, tc::kLayoutSw128);
+            const uint64_t bdesc0 = tc::smem_desc(tc::smem_u32(b_stage(0, 0)), 16, 256, tc::kLayoutSw32);
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
                 const uint32_t par = (it / kStages) & 1;
                 ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
                 if (!ok) break;
                 tc::tc_fence_after();
-                const uint64_t bh = tc::smem_desc(tc::smem_u32(b_stage(st, 0)), 16, 256, tc::kLayoutSw32);
-                const uint64_t blo = tc::smem_desc(tc::smem_u32(b_stage(st, 1)), 16, 256, tc::kLayoutSw32);
+                // descriptors of the stage from the stage-0 ones (the start-address field counts 16-byte units)
+                const uint64_t soff = (uint64_t)((st * kStageBytes) >> 4);
+                const uint64_t bh = bdesc0 + soff, blo = bh + (uint64_t)(kBHalf >> 4);
 #pragma unroll
                 for (int mb = 0; mb < kMB; ++mb) {
-                    const uint64_t ah = tc::smem_desc(tc::smem_u32(a_stage(st, 0)) + mb * 4096, 1024, 2048,
-                                                      tc::kLayoutSw128);
-                    const uint64_t al = tc::smem_desc(tc::smem_u32(a_stage(st, 1)) + mb * 4096, 1024, 2048,
-                                                      tc::kLayoutSw128);
+                    const uint64_t ah = adesc0 + soff + (uint64_t)((mb * 4096) >> 4);
+                    const uint64_t al = ah + (uint64_t)(kAHalf >> 4);
                     const uint32_t dcol = tmem + mb * kSlots;
                     tc::mma_f16_ss(dcol, ah, bh, idesc, j > 0);
                     tc::mma_f16_ss(dcol, ah, blo, idesc, true);

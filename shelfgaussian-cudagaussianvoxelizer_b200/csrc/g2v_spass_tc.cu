@@ -297,6 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
         // ============ MMA thread ============
         if (lane == 0) {
             int it = 0, job = 0;
+            const uint64_t adesc0 = tc::smem_desc(a_half(0, 0), 16, kRowGroupBytes, tc::kLayoutSw64);
+            const uint64_t bdesc0 = tc::smem_desc(b_half(0, 0), 16, kRowGroupBytes, tc::kLayoutSw64);
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int K = unit_offsets[u + 1] - unit_offsets[u];
                 if (K == 0) continue;
@@ -316,19 +318,21 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                              tc::mbar_wait(&ms.full_b[sb], (it / kSB) & 1, err);
                         if (!ok) break;
                         tc::tc_fence_after();
+                        // descriptors of the stage: the start-address field counts 16-byte units, so an
+                        // offset within the stage is added to the stage's base descriptors
+                        const uint64_t bh0 = bdesc0 + (uint64_t)((sb * kBStage) >> 4);
+                        const uint64_t bl0 = bh0 + (uint64_t)(kBHalf >> 4);
+                        const uint64_t ah0 = adesc0 + (uint64_t)((sa * kAStage) >> 4);
+                        const uint64_t al0 = ah0 + (uint64_t)(kAHalf >> 4);
 #pragma unroll
                         for (int ks = 0; ks < kKC / 16; ++ks) {
                             // K step ks = channels 16 ks .. 16 ks + 15: 32 bytes into each swizzled row
-                            const uint64_t bh =
-                                tc::smem_desc(b_half(sb, 0) + ks * 32, 16, kRowGroupBytes, tc::kLayoutSw64);
-                            const uint64_t bl =
-                                tc::smem_desc(b_half(sb, 1) + ks * 32, 16, kRowGroupBytes, tc::kLayoutSw64);
+                            const uint64_t bh = bh0 + (uint64_t)(ks * 2);
+                            const uint64_t bl = bl0 + (uint64_t)(ks * 2);
                             for (int mb = 0; mb < nmb; ++mb) {
-                                const uint32_t ao = mb * kMBlockBytes + ks * 32;
-                                const uint64_t ah =
-                                    tc::smem_desc(a_half(sa, 0) + ao, 16, kRowGroupBytes, tc::kLayoutSw64);
-                                const uint64_t al =
-                                    tc::smem_desc(a_half(sa, 1) + ao, 16, kRowGroupBytes, tc::kLayoutSw64);
+                                const uint64_t ao = (uint64_t)((mb * kMBlockBytes + ks * 32) >> 4);
+                                const uint64_t ah = ah0 + ao;
+                                const uint64_t al = al0 + ao;
                                 const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
                                 tc::mma_f16_ss(d, ah, bh, kIdesc, j > 0 || ks > 0);
                                 tc::mma_f16_ss(d, ah, bl, kIdesc, true);

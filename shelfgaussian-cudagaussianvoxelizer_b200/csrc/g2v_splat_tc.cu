@@ -419,6 +419,8 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
         // ============ MMA thread ============
         if (lane == 0) {
             int it = 0, job = 0;
+            const uint64_t adesc0 = tc::smem_desc(a_stage(0, 0), 1024, 2048, tc::kLayoutSw128);
+            const uint64_t bdesc0 = tc::smem_desc(b_stage(0, 0), 1024, 2048, tc::kLayoutSw128);
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int K = unit_offsets[u + 1] - unit_offsets[u];
                 if (K == 0) continue;
@@ -436,12 +438,13 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
                         // the A operand was written by cp.async (generic proxy); the MMA reads it through the async proxy
                         tc::fence_async_smem();
                         tc::tc_fence_after();
-                        const uint64_t bh = tc::smem_desc(b_stage(st, 0), 1024, 2048, tc::kLayoutSw128);
-                        const uint64_t bl = tc::smem_desc(b_stage(st, 1), 1024, 2048, tc::kLayoutSw128);
+                        // descriptors of the stage from the stage-0 ones (start address in 16-byte units)
+                        const uint64_t soff = (uint64_t)((st * kStageBytes) >> 4);
+                        const uint64_t bh = bdesc0 + soff, bl = bh + (uint64_t)(kBHalf >> 4);
 #pragma unroll
                         for (int mb = 0; mb < 2; ++mb) {
-                            const uint64_t ah = tc::smem_desc(a_stage(st, 0) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
-                            const uint64_t al = tc::smem_desc(a_stage(st, 1) + mb * 4096, 1024, 2048, tc::kLayoutSw128);
+                            const uint64_t ah = adesc0 + soff + (uint64_t)((mb * 4096) >> 4);
+                            const uint64_t al = ah + (uint64_t)(kAHalf >> 4);
                             const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
                             tc::mma_f16_ss(d, ah, bh, kIdesc, i > 0);
                             tc::mma_f16_ss(d, ah, bl, kIdesc, true);
