@@ -102,11 +102,17 @@ void run(const char* name, int sms) {
 
 int main() {
     int sms = 0; cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    run<128, 6, 7, 1, 16, 0>("N128 S6 R7 rewritten + 16 KB, 5 warps", sms);
+    run<128, 6, 7, 0, 0, 0>("N128 S6 R7 per-stage operands, static", sms);
+    run<128, 6, 7, 1, 0, 0>("N128 S6 R7 per-stage operands, rewritten (8 KB)", sms);
+    run<128, 6, 7, 1, 16, 0>("N128 S6 R7 rewritten + 16 KB other stores", sms);
     run<128, 6, 7, 1, 16, 1>("N128 S6 R7 rewritten + 16 KB, + 13 busy FMA warps", sms);
-    run<128, 12, 4, 1, 32, 0>("N128 S12 R4 rewritten + 32 KB, 5 warps", sms);
+    run<128, 12, 4, 0, 0, 0>("N128 S12 R4 per-stage (2 M-blocks), static", sms);
+    run<128, 12, 4, 1, 0, 0>("N128 S12 R4 per-stage, rewritten (12 KB)", sms);
+    run<128, 12, 4, 1, 32, 0>("N128 S12 R4 rewritten + 32 KB other stores", sms);
     run<128, 12, 4, 1, 32, 1>("N128 S12 R4 rewritten + 32 KB, + 13 busy FMA warps", sms);
-    run<256, 6, 4, 1, 32, 0>("N256 S6 R4 rewritten + 32 KB, 5 warps", sms);
+    run<256, 6, 4, 0, 0, 0>("N256 S6 R4 per-stage, static", sms);
+    run<256, 6, 4, 1, 0, 0>("N256 S6 R4 per-stage, rewritten (12 KB)", sms);
+    run<256, 6, 4, 1, 32, 0>("N256 S6 R4 rewritten + 32 KB other stores", sms);
     run<256, 6, 4, 1, 32, 1>("N256 S6 R4 rewritten + 32 KB, + 13 busy FMA warps", sms);
     return 0;
 }
