@@ -199,6 +199,25 @@ def algorithmic_bytes(kernel, n, c, V, M, MB, ntiles):
     return None
 
 
+def algorithmic_flops(kernel, c, M):
+    """Contraction FLOPs of one launch (forward 2*64*M*C, backward 4*64*M*C, split here between
+    the tile pass and the feature-gradient pass) and the tensor-core FLOPs that realise them with three
+    bf16/f16 products (hi*hi + hi*lo + lo*hi) per fp32 product."""
+    if kernel in ("splat_tc_kernel", "spass_tc_kernel", "fpass_tc_kernel"):
+        alg = 2.0 * 64 * M * c
+        return alg, 3.0 * alg
+    return None, None
+
+
+def load_bf16_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    return 1590.0, "fallback"
+
+
 def step_bytes(n, c, V, M):
     """Algorithmic bytes of one fwd+bwd step (SURVEY formula, 8.11 GB at cfg3)."""
     fwd = n * 52 + 4 * n * c + 4 * V + 4 * V * c + n * 64 + 4 * (n + 1) + 4 * M
@@ -335,12 +354,23 @@ def run_ours(args, rank, world, dev):
     if os.path.exists(tpath):
         with open(tpath) as fh:
             traffic = json.load(fh).get(args.config, {}).get(kname)
+    # the same launch against the tensor pipe (the contractions are tensor-bound at three split products)
+    alg_flops, tc_flops = algorithmic_flops(kname, c, M)
+    tpeak, tpeak_kind = load_bf16_peak()
+    tensor = None
+    if tc_flops:
+        t_ach = tc_flops / (avg_ms * 1e-3) / 1e12
+        tensor = {"achieved": t_ach, "peak": tpeak, "unit": "TFLOP/s", "frac": t_ach / tpeak,
+                  "flops_per_launch": tc_flops, "algorithmic_flops_per_launch": alg_flops,
+                  "peak_source": tpeak_kind,
+                  "note": "contraction 2*64*M*C per launch executed as three bf16/f16 products"}
     roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": (achieved / peak) if achieved else None, "traffic": traffic,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": avg_ms,
                 "kernel_share": {k: round(v[0] / sum(x[0] for x in prof.values()), 4) for k, v in prof.items()},
-                "kernel_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in prof.items()}}
+                "kernel_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in prof.items()},
+                "tensor": tensor}
     sb = step_bytes(n, c, V, M)
 
     # end-to-end through the public API with pinned host inputs (H2D inside the timed region)
