@@ -255,6 +255,37 @@ G2V_API int g2v_backward(const float* grad_density, const float* grad_grid_feats
                  size_t workspace_bytes, void* stream);
 
 /*
+ * g2v_backward over the whole grid with the tile pass's unit lists supplied by the caller instead of
+ * rebuilt: unit_offsets (num_units + 1) and unit_lists (num_pairs), the z-pairs-of-tiles CSR that
+ * g2v_forward_splat built for the same Gaussians (copied out with g2v_forward_splat_unit_lists).  Used
+ * only by the tensor-core path (the FP32-FMA variant builds its own lists).  Same outputs and workspace as
+ * g2v_backward; a host-side saving of the reference's backward, which rebuilds nothing because it walks
+ * the G2T map per Gaussian (cu:1376-1482).
+ */
+G2V_API int g2v_backward_units(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                               const float* opacity, const float* cov_inv, const float* features,
+                               int64_t num_gaussians, int64_t channels, const float voxel_size[3],
+                               const float voxel_range[6], const int dims[3], const int32_t* valid_voxel_lb,
+                               const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                               const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                               const float* density, const float* grid_feats, float* grad_means3d,
+                               float* grad_covariances, float* grad_opacity, float* grad_features,
+                               const int32_t* unit_offsets, const int32_t* unit_lists, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
+ * Copies the unit lists (Gaussian ids of each z pair of tiles, ascending; the cell->Gaussian CSR the
+ * tensor-core splat and tile pass work on) out of a g2v_forward_splat workspace after the call:
+ * unit_offsets (num_units + 1, int32) and unit_lists (num_pairs, int32; entries beyond
+ * unit_offsets[num_units] unspecified).  With unit_offsets == NULL only *num_units is returned.  Fails
+ * when the splat built no unit lists (channels == 0 or the FP32-FMA variant).  No reference counterpart
+ * (the reference keeps its lists internal, cu:1675-1772).
+ */
+G2V_API int g2v_forward_splat_unit_lists(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs,
+                                         const int dims[3], int64_t channels, int32_t* unit_offsets,
+                                         int32_t* unit_lists, int64_t* num_units, void* stream);
+
+/*
  * g2v_backward for Gaussians parameterised by scales (N,3) and rotations (N,4): the same inputs plus
  * scales/rotations, and grad_scales (N,3) / grad_rotations (N,4) in place of grad_covariances (the chain
  * rule runs in the per-Gaussian gradient reduction, so dL/dSigma is never written).  Workspace: the

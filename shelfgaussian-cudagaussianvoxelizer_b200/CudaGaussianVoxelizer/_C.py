@@ -107,14 +107,17 @@ def _scene_offsets(scene_sizes, n, dev):
 
 
 def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing, keep_t2g=False,
-                  plan=False, scale_rot=None, scenes=None, caps=None):
+                  plan=False, scale_rot=None, scenes=None, caps=None, keep_units=None):
     """The forward; ``scale_rot=(scales, rotations)`` replaces ``covariances`` (then ``plan`` is implied and
     the covariances are formed inside the preparation kernel).  ``scenes=(scene_offsets (B+1) device int32,
     B)``: the Gaussians are a ragged batch of B scenes, splatted in one call into (B, X, Y, Z[, C]) volumes
     (boxes and tile ids in the coordinates of the scenes stacked along x; ``plan`` implied).
     ``caps=(max_pairs, max_block_pairs)``: capacity-capped, with no host synchronisation at all (the pair
     buffers are sized by the capacities; ``plan`` implied and the returned block-pair count is the cap), so
-    the call can be captured in a CUDA graph; overflow is reported through the device error word."""
+    the call can be captured in a CUDA graph; overflow is reported through the device error word.
+    ``keep_units`` (True / False, with ``plan``): a third value is returned, the splat's unit lists
+    ``(unit_offsets, unit_lists)`` when True and the splat built them, else None; they are for
+    ``gaussian_voxelizer_backward(units=...)``, which then skips rebuilding them."""
     lib = _lib.load()
     size_h = _host_values(voxel_size, 3, "voxel_size")
     range_h = _host_values(voxel_range, 6, "voxel_range")
@@ -233,6 +236,18 @@ def _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, featur
             ev1.synchronize()
             sec = ev0.elapsed_time(ev1) / 1000.0
         out = (density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, sec)
+        if keep_units is not None and plan:
+            units = None
+            nu = ctypes.c_int64()
+            if keep_units and scenes is None and caps is None and c > 0 and lib.g2v_forward_splat_unit_lists(
+                    None, n, m, _lib.i3((XS, Y, Z)), c, None, None, ctypes.byref(nu), sptr) == 0:
+                uoff = torch.empty((int(nu.value) + 1,), **i32)
+                ulist = torch.empty((max(m, 1),), **i32)
+                _lib.check(lib.g2v_forward_splat_unit_lists(_ptr(ws2), n, m, _lib.i3((XS, Y, Z)), c, _ptr(uoff),
+                                                            _ptr(ulist), ctypes.byref(nu), sptr),
+                           "g2v_forward_splat_unit_lists")
+                units = (uoff, ulist)
+            return out, int(mb.value), units
         if plan:
             return out, int(mb.value)
         if keep_t2g:
@@ -288,7 +303,7 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
                                 valid_voxel_lb, valid_voxel_ub, num_voxels_per_gaussian, g2t_offsets, g2t_tile_ids,
                                 density, grid_feats, features=None, *, timing: bool = True,
                                 num_block_pairs: int | None = None, tile_x_range=None, scale_rot=None,
-                                num_scenes: int = 1):
+                                num_scenes: int = 1, units=None):
     """Backward of the G2V splat (reference src/bindings.cpp:30-64, cu:1920-2057).
 
     Returns ``(grad_means3D (N,3), grad_cov (N,9), grad_opacity (N,), grad_feats (N,C), bwd_sec)``;
@@ -300,6 +315,9 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
     rule runs inside the gradient reduction).
     ``num_scenes=B``: the state of a batched forward; grad_output / density are (B, X, Y, Z) and
     grad_feats_output / grid_feats (B, X, Y, Z, C).
+    ``units=(unit_offsets, unit_lists)``: the forward splat's unit lists (``_forward_impl(keep_units=True)``)
+    for the same Gaussians; the tile pass then uses them instead of rebuilding them (whole grid, one scene,
+    covariance inputs).
     """
     lib = _lib.load()
     dev = means3D.device
@@ -372,6 +390,14 @@ def gaussian_voxelizer_backward(grad_output, grad_feats_output, means3D, opacity
                                            _ptr(grid_feats), _ptr(grad_means), _ptr(grad_cov), _ptr(grad_rot),
                                            _ptr(grad_op), _ptr(grad_feats), tb, te, _ptr(ws), ws.numel(), sptr),
                        "g2v_backward_sr")
+        elif units is not None and c > 0 and tile_x_range is None:
+            _lib.check(lib.g2v_backward_units(_ptr(grad_output), _ptr(grad_feats_output), _ptr(means3D), _ptr(opacity),
+                                              _ptr(cov_inv), fptr, n, c, _lib.f3(size_h), _lib.f6(range_h),
+                                              _lib.i3(dims), _ptr(valid_voxel_lb), _ptr(valid_voxel_ub),
+                                              _ptr(g2t_offsets), _ptr(g2t_tile_ids), m, int(num_block_pairs),
+                                              _ptr(density), _ptr(grid_feats), _ptr(grad_means), _ptr(grad_cov),
+                                              _ptr(grad_op), _ptr(grad_feats), _ptr(units[0]), _ptr(units[1]),
+                                              _ptr(ws), ws.numel(), sptr), "g2v_backward_units")
         else:
             _lib.check(lib.g2v_backward(_ptr(grad_output), _ptr(grad_feats_output) if c > 0 else None,
                                         _ptr(means3D), _ptr(opacity), _ptr(cov_inv), fptr, n, c, _lib.f3(size_h),

@@ -11,6 +11,8 @@ kernels behind a C ABI, include/g2v.h).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn as nn
 
@@ -19,6 +21,9 @@ from ._C import (CudaFeatsCosinelossBackward, CudaFeatsCosinelossForward, _cosin
                  gaussian_voxelizer_backward, gaussian_voxelizer_forward)
 
 _lib.load()  # fail loudly at import when the native library is missing
+
+# G2V_REUSE_UNITS=0: the backward rebuilds the tile pass's unit lists instead of taking the forward's
+_REUSE_UNITS = os.environ.get("G2V_REUSE_UNITS", "1") != "0"
 
 from .graphs import GraphedGaussianVoxelizer  # noqa: E402
 
@@ -37,9 +42,12 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
                 caps=None):
         # the forward also counts the backward's (Gaussian, block) pairs in its one synchronisation (or, with
         # capacities, synchronises not at all)
+        # the splat's unit lists are kept for the backward's tile pass (it would rebuild the same ones)
         ((density, cov_inv, lb, ub, nvox, grid_feats, g2t_offsets, g2t_tile_ids, fwd_sec),
-         num_block_pairs) = _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features, timing,
-                                          plan=True, scenes=scenes, caps=caps)
+         num_block_pairs, units) = _forward_impl(means3D, opacity, covariances, voxel_size, voxel_range, features,
+                                                 timing, plan=True, scenes=scenes, caps=caps,
+                                                 keep_units=_REUSE_UNITS)
+        ctx.units = units
         ctx.num_scenes = 1 if scenes is None else scenes[1]
         stats = torch.zeros(2, dtype=torch.float32, device="cpu")
         stats[0] = fwd_sec
@@ -62,7 +70,8 @@ class _CudaGaussianVoxelizeFunction(torch.autograd.Function):
         grad_means, grad_cov, grad_op, grad_feats, bwd_sec = gaussian_voxelizer_backward(
             gout, gfeat, means3D, opacity, cov_inv, voxel_size, voxel_range, lb, ub, nvox, g2t_offsets,
             g2t_tile_ids, density, grid_feats, features, timing=ctx.timing, num_block_pairs=ctx.num_block_pairs,
-            num_scenes=ctx.num_scenes)
+            num_scenes=ctx.num_scenes, units=ctx.units)
+        ctx.units = None
         stats[1] = bwd_sec
         return (grad_means, grad_op, grad_cov, None, None, grad_feats if features is not None else None, None, None,
                 None)

@@ -50,6 +50,9 @@ SIGNATURES = {
                                  I32, P, SZ, P]),
     "g2v_backward_sr": (I32, [P, P, P, P, P, P, P, P, I64, I64, F3, F6, I3, P, P, P, P, I64, I64, P, P, P, P, P, P,
                               P, I32, I32, P, SZ, P]),
+    "g2v_backward_units": (I32, [P, P, P, P, P, P, I64, I64, F3, F6, I3, P, P, P, P, I64, I64, P, P, P, P, P, P, P,
+                                 P, P, SZ, P]),
+    "g2v_forward_splat_unit_lists": (I32, [P, I64, I64, I3, I64, P, P, ctypes.POINTER(I64), P]),
     "g2v_backward_plan": (I32, [P, P, I64, I3, I64, P, SZ, P, ctypes.POINTER(I64)]),
     "g2v_backward_plan_workspace_size": (I32, [I64, ctypes.POINTER(SZ)]),
     "g2v_backward_workspace_size": (I32, [I64, I64, I64, I3, I64, ctypes.POINTER(SZ)]),

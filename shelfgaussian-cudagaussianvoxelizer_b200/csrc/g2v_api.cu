@@ -543,6 +543,48 @@ int g2v_build_t2g_workspace_size(int64_t num_gaussians, int64_t num_pairs, const
     return G2V_SUCCESS;
 }
 
+int g2v_forward_splat_unit_lists(const void* splat_workspace, int64_t num_gaussians, int64_t num_pairs,
+                                 const int dims[3], int64_t channels, int32_t* unit_offsets, int32_t* unit_lists,
+                                 int64_t* num_units, void* stream) {
+    g_msg[0] = 0;
+    (void)num_gaussians;
+    if (!dims || !num_units || num_pairs < 0) {
+        set_error("g2v_forward_splat_unit_lists: invalid argument");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    if (channels <= 0 || !use_tensor_cores()) {
+        set_error("g2v_forward_splat_unit_lists: the splat built no unit lists (no features, or the FP32-FMA variant)");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    Grid G{};
+    for (int a = 0; a < 3; ++a) {
+        G.dims[a] = dims[a];
+        G.tiles[a] = (dims[a] + 3) / 4;
+    }
+    int cell[3], ncells[3];
+    spass_tc_unit_shape(G, cell, ncells);
+    const int64_t nu = (int64_t)ncells[0] * ncells[1] * ncells[2];
+    *num_units = nu;
+    if (!unit_offsets) return G2V_SUCCESS;  // size query
+    if (!splat_workspace || (num_pairs > 0 && !unit_lists)) {
+        set_error("g2v_forward_splat_unit_lists: invalid pointer");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    // the splat workspace holds the tile lists, then the unit lists (g2v_forward_splat)
+    const int64_t ntiles = (int64_t)G.tiles[0] * G.tiles[1] * G.tiles[2];
+    Carver c(const_cast<void*>(splat_workspace));
+    T2GWs w, wu;
+    carve_t2g(c, ntiles, num_pairs, w);
+    carve_t2g(c, ntiles, num_pairs, wu);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    G2V_CUDA(cudaMemcpyAsync(unit_offsets, wu.tile_offsets, sizeof(int32_t) * (size_t)(nu + 1), cudaMemcpyDeviceToDevice,
+                             s));
+    if (num_pairs > 0)
+        G2V_CUDA(cudaMemcpyAsync(unit_lists, wu.lists, sizeof(int32_t) * (size_t)num_pairs, cudaMemcpyDeviceToDevice,
+                                 s));
+    return G2V_SUCCESS;
+}
+
 int g2v_build_t2g(const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, int64_t num_gaussians,
                   const float voxel_size[3], const float voxel_range[6], int64_t num_pairs, int32_t* tile_offsets,
                   int32_t* t2g_gaussians, void* workspace, size_t workspace_bytes, void* stream) {
@@ -839,7 +881,8 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
                          float* grad_covariances, float* grad_opacity, float* grad_features, int tile_x_begin,
                          int tile_x_end, void* workspace, size_t workspace_bytes, void* stream, bool local,
                          const float* scales = nullptr, const float* rotations = nullptr,
-                         float* grad_rotations = nullptr, int num_scenes = 1) {
+                         float* grad_rotations = nullptr, int num_scenes = 1,
+                         const int32_t* unit_offsets_in = nullptr, const int32_t* unit_lists_in = nullptr) {
     (void)grid_feats;
     g_msg[0] = 0;
     Grid G;
@@ -874,7 +917,12 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
     if (tcore) spass_tc_unit_shape(G, cell, ncells);
     int* err = nullptr;
     if ((rc = device_error_ptr(&err))) return rc;
-    if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
+    // the tile pass's unit lists: given by the caller (the forward splat built the same ones) or built here
+    const bool given_units = tcore && unit_offsets_in != nullptr && unit_lists_in != nullptr;
+    const int32_t* unit_offsets = given_units ? unit_offsets_in : w.t2g.tile_offsets;
+    const int32_t* unit_lists = given_units ? unit_lists_in : w.t2g.lists;
+    if (!given_units &&
+        (rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
                                tile_x_end, g2t_offsets, nullptr, 0, nullptr, w.t2g.counts, w.t2g.tile_offsets,
                                w.t2g.unsorted, w.t2g.lists, w.t2g.scan, w.t2g.total, s, num_pairs, err)))
         return rc;
@@ -885,7 +933,7 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
                                      w.gparams, s)))
             return rc;
         if ((rc = launch_spass_tc(grad_density, grad_grid_feats, features, num_gaussians, C, density, w.gparams,
-                                  g2t_offsets, w.t2g.tile_offsets, w.t2g.lists, tile_x_begin, tile_x_end, G,
+                                  g2t_offsets, unit_offsets, unit_lists, tile_x_begin, tile_x_end, G,
                                   w.partial10, num_pairs, w.fsplit, err, s)))
             return rc;
     } else if ((rc = launch_spass(grad_density, grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb,
@@ -941,6 +989,26 @@ int g2v_backward(const float* grad_density, const float* grad_grid_feats, const 
                          num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_covariances,
                          grad_opacity, grad_features, tile_x_begin, tile_x_end, workspace, workspace_bytes, stream,
                          false);
+}
+
+int g2v_backward_units(const float* grad_density, const float* grad_grid_feats, const float* means3d,
+                       const float* opacity, const float* cov_inv, const float* features, int64_t num_gaussians,
+                       int64_t channels, const float voxel_size[3], const float voxel_range[6], const int dims[3],
+                       const int32_t* valid_voxel_lb, const int32_t* valid_voxel_ub, const int32_t* g2t_offsets,
+                       const int32_t* g2t_tile_ids, int64_t num_pairs, int64_t num_block_pairs,
+                       const float* density, const float* grid_feats, float* grad_means3d, float* grad_covariances,
+                       float* grad_opacity, float* grad_features, const int32_t* unit_offsets,
+                       const int32_t* unit_lists, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!unit_offsets || !unit_lists) {
+        g_msg[0] = 0;
+        set_error("g2v_backward_units: unit_offsets and unit_lists are required");
+        return G2V_ERROR_INVALID_VALUE;
+    }
+    return backward_impl(grad_density, grad_grid_feats, means3d, opacity, cov_inv, features, num_gaussians, channels,
+                         voxel_size, voxel_range, dims, valid_voxel_lb, valid_voxel_ub, g2t_offsets, g2t_tile_ids,
+                         num_pairs, num_block_pairs, density, grid_feats, grad_means3d, grad_covariances,
+                         grad_opacity, grad_features, 0, 0, workspace, workspace_bytes, stream, false, nullptr,
+                         nullptr, nullptr, 1, unit_offsets, unit_lists);
 }
 
 int g2v_backward_local(const float* grad_density, const float* grad_grid_feats, const float* means3d,
