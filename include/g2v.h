@@ -240,8 +240,10 @@ G2V_API int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs
  * grad_opacity (N) and, when features != NULL, grad_features (N,C).  Every output element is written.
  * Only the voxels of tiles with tile x in [tile_x_begin, tile_x_end) contribute (0 / tiles[0] for the
  * whole grid): on an x-slab the outputs are that slab's partial gradients.
- * grid_feats is accepted for interface parity and not read: sum_c dL/dF_vc F_vc is formed from the
- * per-pair dot products the kernel computes anyway.
+ * e_v = sum_c dL/dF_vc F_vc (the reference's at::bmm) is formed from the per-pair dot products the
+ * tile pass computes anyway; only for the voxels of cells (z pairs of tiles) with more than 256 Gaussians
+ * is it read from grid_feats (the forward's output), which saves running their slot passes twice.
+ * grid_feats may be NULL: then those cells run both passes.
  * Replaces src/cuda_gaussian_voxelizer.cu:1920-2057 (the at::bmm at cu:1996 and
  * ComputeGaussian2VoxelGradientTileWithFeats / ComputeGaussian2VoxelGradientTile).
  */

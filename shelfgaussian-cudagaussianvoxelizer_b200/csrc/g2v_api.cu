@@ -63,7 +63,8 @@ void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]);
 int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
                     const float* density, const GParams* gparams, const int32_t* g2t_offsets,
                     const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
-                    const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s);
+                    const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s,
+                    const float* grid_feats = nullptr, float* ev_buf = nullptr);
 int launch_wait_timeout(int* err, cudaStream_t s, int* gave_up_host);
 // scales / quats / grad_quats non-NULL: grad_cov receives dL/dscales (n,3) and grad_quats dL/dquats (n,4).
 int launch_reduce10(const float* partial10, const int32_t* g2t_offsets, const int32_t* g2t_tile_ids, int64_t n,
@@ -265,6 +266,7 @@ struct BackwardWs {
     float* partialF;
     GParams* gparams;
     void* fsplit;
+    float* ev;  // e_v = sum_c gF_vc F_vc of the voxels of units with more than one slot pass
 };
 size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, int64_t C, BackwardWs& w) {
     Carver c(p);
@@ -286,6 +288,7 @@ size_t carve_backward(void* p, int64_t n, int64_t m, int64_t mb, const Grid& G, 
     w.partialF = c.take<float>((size_t)(feats && mb > 0 ? mb : 1) * (size_t)(feats ? C : 1));
     w.gparams = c.take<GParams>((size_t)(n > 0 ? n : 1));
     w.fsplit = c.take<char>(feats ? spass_tc_split_bytes(n, C) : 1);
+    w.ev = c.take<float>(feats ? (size_t)G.dims[0] * G.dims[1] * G.dims[2] : 1);
     return c.bytes();
 }
 
@@ -883,7 +886,6 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
                          const float* scales = nullptr, const float* rotations = nullptr,
                          float* grad_rotations = nullptr, int num_scenes = 1,
                          const int32_t* unit_offsets_in = nullptr, const int32_t* unit_lists_in = nullptr) {
-    (void)grid_feats;
     g_msg[0] = 0;
     Grid G;
     int rc = make_grid(voxel_size, voxel_range, G);
@@ -934,7 +936,7 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
             return rc;
         if ((rc = launch_spass_tc(grad_density, grad_grid_feats, features, num_gaussians, C, density, w.gparams,
                                   g2t_offsets, unit_offsets, unit_lists, tile_x_begin, tile_x_end, G,
-                                  w.partial10, num_pairs, w.fsplit, err, s)))
+                                  w.partial10, num_pairs, w.fsplit, err, s, grid_feats, w.ev)))
             return rc;
     } else if ((rc = launch_spass(grad_density, grad_grid_feats, means3d, opacity, cov_inv, valid_voxel_lb,
                                   valid_voxel_ub, features, C, density, g2t_offsets, w.t2g.tile_offsets, w.t2g.lists,

@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
     int C, int Cp, const float* __restrict__ density, const GParams* __restrict__ gparams,
     const int32_t* __restrict__ g2t_offsets, const int32_t* __restrict__ unit_offsets,
     const int32_t* __restrict__ unit_lists, int num_units, int tx_begin, Grid G, float* __restrict__ partial10,
-    int64_t pair_cap, int* __restrict__ err) {
+    int64_t pair_cap, const float* __restrict__ ev, int* __restrict__ err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = smem_raw;
     unsigned char* bring = base + kSA * kAStage;
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
             const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
             if (K == 0) continue;
             const int npass = (K + kSlots - 1) / kSlots;
-            const int njobs = npass == 1 ? 1 : 2 * npass;
+            const int njobs = npass == 1 ? 1 : (ev ? npass : 2 * npass);
             for (int jb = 0; jb < njobs && ok; ++jb) {
                 const int p = npass == 1 ? 0 : jb % npass;
                 const int ns = min(kSlots, K - p * kSlots);
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
             const bool vin = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
             const int64_t vrow = vin ? grid_row(G, x, y, z) : -1;
             const int npass = (K + kSlots - 1) / kSlots;
-            const int njobs = npass == 1 ? 1 : 2 * npass;
+            const int njobs = npass == 1 ? 1 : (ev ? npass : 2 * npass);
             for (int jb = 0; jb < njobs && ok; ++jb) {
                 for (int j = 0; j < nsteps && ok; ++j, ++it) {
                     const int sb = it % kSB, gs = it % kGS;
@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                 const int K = unit_offsets[u + 1] - unit_offsets[u];
                 if (K == 0) continue;
                 const int npass = (K + kSlots - 1) / kSlots;
-                const int njobs = npass == 1 ? 1 : 2 * npass;
+                const int njobs = npass == 1 ? 1 : (ev ? npass : 2 * npass);
                 for (int jb = 0; jb < njobs && ok; ++jb, ++job) {
                     const int p = npass == 1 ? 0 : jb % npass;
                     const int ns = min(kSlots, K - p * kSlots);
@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                 if (K == 0) continue;
                 const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
                 const int npass = (K + kSlots - 1) / kSlots;
-                const int njobs = npass == 1 ? 1 : 2 * npass;
+                const int njobs = npass == 1 ? 1 : (ev ? npass : 2 * npass);
                 for (int jb = 0; jb < njobs && ok; ++jb) {
                     for (int j = 0; j < nsteps && ok; ++j, ++it) {
                         const int gs = it % kGS;
@@ -400,15 +400,21 @@ __global__ void __launch_bounds__(kThreads, 1) spass_tc_kernel(
                 ms.rden[et] = in ? 1.0f / den : 0.0f;
                 ms.act[et] = D >= kEps ? 1.0f : 0.0f;
                 ms.e[et] = 0.0f;
+                if (ev && K > kSlots) {  // e_v of a multi-pass unit, formed from grid_feats beforehand
+                    const float e = in ? ev[row] : 0.0f;
+                    ms.e[et] = e;
+                    ms.va[et] = make_float2(ms.rden[et], fmaf(-ms.act[et] * e, ms.rden[et], ms.gD[et]));
+                }
             }
             epi_barrier();
             const float cz0 = voxel_centre(G, 2, z0);
             const int npass = (K + kSlots - 1) / kSlots;
-            const int njobs = npass == 1 ? 1 : 2 * npass;
+            const int njobs = npass == 1 ? 1 : (ev ? npass : 2 * npass);
             for (int jb = 0; jb < njobs; ++jb, ++job) {
                 const int p = npass == 1 ? 0 : jb % npass;
-                const bool do1 = npass == 1 || jb < npass;   // phase 1 of this job
-                const bool do2 = npass == 1 || jb >= npass;  // phase 2 of this job
+                // with e_v given (multi-pass units), every job is phase 2
+                const bool do1 = npass == 1 || (!ev && jb < npass);  // phase 1 of this job
+                const bool do2 = npass == 1 || ev || jb >= npass;    // phase 2 of this job
                 const int buf = job & 1;
                 const bool good = ok && tc::mbar_wait(&ms.tfull[buf], (job / 2) & 1, err);
                 if (!good) ok = false;
@@ -629,10 +635,48 @@ void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]) {
     ncells[2] = (G.tiles[2] + 1) / 2;
 }
 
+namespace {
+// e_v = sum_c gF_vc F_vc (F = grid_feats, the forward's output: the reference's at::bmm, cu:1996) for the
+// voxels of the units with more than kSlots Gaussians, where forming e_v from S would need every slot
+// pass twice.  Block = unit, warp = voxel rows, fixed summation order (deterministic).
+__global__ void __launch_bounds__(256) unit_ev_kernel(const int32_t* __restrict__ unit_offsets, int tzp_n, int tx_begin,
+                                                      Grid G, const float* __restrict__ gF,
+                                                      const float* __restrict__ F, int C, int vec,
+                                                      float* __restrict__ ev) {
+    const int u = blockIdx.x;
+    if (unit_offsets[u + 1] - unit_offsets[u] <= kSlots) return;
+    const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int v = warp; v < kUV; v += 8) {
+        const int x = ug.tx * kTile + (v >> 5), y = ug.ty * kTile + ((v >> 3) & 3), z = ug.tzp * 8 + (v & 7);
+        if (x >= G.dims[0] || y >= G.dims[1] || z >= G.dims[2]) continue;  // warp-uniform
+        const int64_t row = grid_row(G, x, y, z);
+        const float* a = gF + row * C;
+        const float* b = F + row * C;
+        float acc = 0.0f;
+        if (vec) {
+            for (int c = 4 * lane; c < C; c += 128) {
+                const float4 p = *reinterpret_cast<const float4*>(a + c), q = *reinterpret_cast<const float4*>(b + c);
+                acc = fmaf(p.x, q.x, acc);
+                acc = fmaf(p.y, q.y, acc);
+                acc = fmaf(p.z, q.z, acc);
+                acc = fmaf(p.w, q.w, acc);
+            }
+        } else {
+            for (int c = lane; c < C; c += 32) acc = fmaf(a[c], b[c], acc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) ev[row] = acc;
+    }
+}
+}  // namespace
+
 int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
                     const float* density, const GParams* gparams, const int32_t* g2t_offsets,
                     const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
-                    const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s) {
+                    const Grid& G, float* partial10, int64_t pair_cap, void* split, int* err, cudaStream_t s,
+                    const float* grid_feats, float* ev_buf) {
     const int num_units = (tile_x_end - tile_x_begin) * G.tiles[1] * ((G.tiles[2] + 1) / 2);
     if (num_units <= 0 || C <= 0 || n <= 0) return 0;
     const int Cp = (int)spass_tc_padded_channels(C);
@@ -656,11 +700,22 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
     G2V_CUDA(cudaGetDevice(&dev));
     G2V_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int grid = std::min(num_units, sms);
+    // e_v of the multi-pass units from grid_feats (when the caller passed it)
+    const float* ev = nullptr;
+    if (grid_feats != nullptr && ev_buf != nullptr) {
+        const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0) &&
+                        (reinterpret_cast<uintptr_t>(grid_feats) % 16 == 0);
+        G2V_TIMED("unit_ev_kernel", s,
+                  unit_ev_kernel<<<(unsigned)num_units, 256, 0, s>>>(unit_offsets, (G.tiles[2] + 1) / 2, tile_x_begin,
+                                                                     G, grad_feats, grid_feats, C, vec, ev_buf));
+        G2V_LAUNCH_CHECK("unit_ev_kernel");
+        ev = ev_buf;
+    }
     G2V_TIMED("spass_tc_kernel", s,
               kern<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(gmap, grad_density, grad_feats, Fh, Fl, C, Cp,
                                                                   density, gparams, g2t_offsets, unit_offsets,
                                                                   unit_lists, num_units, tile_x_begin, G, partial10,
-                                                                  pair_cap, err));
+                                                                  pair_cap, ev, err));
     G2V_LAUNCH_CHECK("spass_tc_kernel");
     return 0;
 }
