@@ -583,12 +583,15 @@ size_t splat_tc_split_bytes(int64_t n, int64_t C) {
 }
 
 namespace {
-// Weight warps of the splat kernel (G2V_SPLAT_WW=4 or 8, default 4: measured at cfg3 with the weight
-// cache, 1.16 ms with 4 and 1.22 ms with 8) and whether the weight cache is used (G2V_SPLAT_WCACHE=0
-// turns it off: 1.60 / 1.46 ms).
-int splat_weight_warps() {
+// Weight warps of the splat kernel: with one channel group (C <= 256) every step evaluates weights and
+// eight warps hide their latency better (cfg5: splat 32.6 vs 36.7 ms); with several groups the weight
+// cache leaves the evaluation to the first group and four warps are faster (cfg3: 1.16 vs 1.22 ms).
+// G2V_SPLAT_WW=4 or 8 overrides.  G2V_SPLAT_WCACHE=0 turns the weight cache off (cfg3: 1.60 / 1.46 ms).
+int splat_weight_warps(int ngroups) {
     const char* e = getenv("G2V_SPLAT_WW");
-    return (e && atoi(e) == 8) ? 8 : 4;
+    if (e && atoi(e) == 8) return 8;
+    if (e && atoi(e) == 4) return 4;
+    return ngroups == 1 ? 8 : 4;
 }
 bool splat_weight_cache() {
     const char* e = getenv("G2V_SPLAT_WCACHE");
@@ -650,7 +653,7 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
     const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
     const bool tma = C > 0 && encode_grid_rows_f32(&omap, grid_feats, ldims, C, kCG, 8, 2, 1);
     unsigned char* wc = splat_weight_cache() ? wcache : nullptr;
-    if (splat_weight_warps() == 4)
+    if (splat_weight_warps((C + kCG - 1) / kCG) == 4)
         return launch_splat_kernel<4>(tma, omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units,
                                       tile_x_begin, G, density, grid_feats, wc, err, s);
     return launch_splat_kernel<8>(tma, omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units,

@@ -159,13 +159,15 @@ def test_feature_gradient_pair_variant_matches_default(n, c, seed, half, var_max
     assert_close("grad_features (pair)", pair[3], ref[3])
 
 
-@pytest.mark.parametrize("env", [{"G2V_SPLAT_WW": "8"}, {"G2V_SPLAT_WCACHE": "0"},
-                                 {"G2V_SPLAT_WW": "8", "G2V_SPLAT_WCACHE": "0"}])
-def test_splat_weight_variants_match_default(env):
-    """The weight cache changes where the weights come from, not their values: bit-identical.  Eight weight
-    warps sum the density over a different grouping of the Gaussians: within the parity bar."""
+@pytest.mark.parametrize("env,c", [({"G2V_SPLAT_WW": "8"}, 600), ({"G2V_SPLAT_WCACHE": "0"}, 600),
+                                   ({"G2V_SPLAT_WW": "8", "G2V_SPLAT_WCACHE": "0"}, 600),
+                                   ({"G2V_SPLAT_WW": "4"}, 200), ({"G2V_SPLAT_WCACHE": "0"}, 200)])
+def test_splat_weight_variants_match_default(env, c):
+    """The weight cache changes where the weights come from, not their values: bit-identical.  Four and eight
+    weight warps (the default is eight for one channel group, four for several) sum the density over a
+    different grouping of the Gaussians: within the parity bar."""
     rng = [-10.0, -10.0, -1.0, 10.0, 10.0, 5.4]
-    m, o, cv, f = oracle.generate_inputs(3000, 600, rng, seed=11, num_outside=150)
+    m, o, cv, f = oracle.generate_inputs(3000, c, rng, seed=11, num_outside=150)
     args = (m.numpy(), o.numpy(), cv.numpy(), f.numpy(), [0.4] * 3, rng)
     ref = _forward("tc", *args)
     got = _with_env(env, lambda: _forward("tc", *args))
