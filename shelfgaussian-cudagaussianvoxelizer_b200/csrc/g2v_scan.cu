@@ -1,4 +1,5 @@
-// g2v_scan.cu -- exclusive prefix sum of int32 counts (reduce, scan of block sums, scan + write).
+// g2v_scan.cu -- exclusive prefix sum of int32 counts: one block for up to 64k counts, else three
+// kernels (reduce, scan of block sums, scan + write).
 //
 // Used for the Gaussian->Tile offsets (N+1 entries, replacing the CUB InclusiveSum + memset of
 // src/cuda_gaussian_voxelizer.cu:1608-1615), the per-tile offsets of the Tile->Gaussian map and the
@@ -117,6 +118,56 @@ __global__ void __launch_bounds__(kScanThreads) scan_write_kernel(const int32_t*
     }
 }
 
+// Up to kSmallScan counts (the per-Gaussian and per-cell counts of a scene of up to 64k Gaussians or
+// cells): one block of 1024 threads scans them in chunks of 8192 with a running carry, one launch
+// instead of three.  Same results as the three-kernel path (integer sums), including the clamp to cap.
+constexpr int kSmallThreads = 1024;
+constexpr int kSmallChunk = kSmallThreads * kScanItems;  // 8192 counts, 32 KB of shared memory
+constexpr int64_t kSmallScan = 8 * kSmallChunk;
+
+__global__ void __launch_bounds__(kSmallThreads) scan_small_kernel(const int32_t* __restrict__ in, int64_t n,
+                                                                   int32_t* __restrict__ out,
+                                                                   int64_t* __restrict__ total, int64_t cap,
+                                                                   int* __restrict__ err) {
+    __shared__ int32_t stage[kSmallChunk];
+    int64_t carry = 0;
+    for (int64_t base = 0; base < n; base += kSmallChunk) {
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            const int64_t i = base + k * kSmallThreads + threadIdx.x;
+            stage[k * kSmallThreads + threadIdx.x] = i < n ? in[i] : 0;
+        }
+        __syncthreads();
+        int32_t v[kScanItems];
+        int64_t s = 0;
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            v[k] = stage[threadIdx.x * kScanItems + k];
+            s += v[k];
+        }
+        int64_t tot;
+        int64_t run = carry + block_exclusive<kSmallThreads>(s, &tot);  // ends with a barrier: stage is free
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            stage[threadIdx.x * kScanItems + k] = static_cast<int32_t>(cap >= 0 && run > cap ? cap : run);
+            run += v[k];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            const int64_t i = base + k * kSmallThreads + threadIdx.x;
+            if (i < n) out[i] = stage[k * kSmallThreads + threadIdx.x];
+        }
+        carry += tot;
+        __syncthreads();  // the next chunk overwrites stage
+    }
+    if (threadIdx.x == 0) {
+        out[n] = static_cast<int32_t>(cap >= 0 && carry > cap ? cap : carry);
+        *total = carry;
+        if (cap >= 0 && carry > cap && err) atomicOr(err, kErrCapacity);
+    }
+}
+
 __global__ void scan_empty_kernel(int32_t* out, int64_t* total) {
     out[0] = 0;
     *total = 0;
@@ -133,6 +184,12 @@ int launch_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_
     if (n == 0) {
         G2V_TIMED("scan_empty_kernel", s, scan_empty_kernel<<<1, 1, 0, s>>>(out, total));
         G2V_LAUNCH_CHECK("scan_empty_kernel");
+        return 0;
+    }
+    if (n <= kSmallScan) {
+        G2V_TIMED("scan_small_kernel", s,
+                  scan_small_kernel<<<1, kSmallThreads, 0, s>>>(counts, n, out, total, cap, err));
+        G2V_LAUNCH_CHECK("scan_small_kernel");
         return 0;
     }
     const int64_t nb = (n + kScanTile - 1) / kScanTile;

@@ -53,6 +53,22 @@ def test_csr_bit_exact_vs_oracle(golden, name):
     np.testing.assert_allclose(cov_inv, bx.cov_inv, rtol=2e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("n", [40000, 100000])
+def test_csr_bit_exact_both_scan_paths(n):
+    """g2t offsets of 40k Gaussians come from the one-block scan (5 chunks of 8192), of 100k from the
+    three-kernel scan; both bit-exact against the oracle's CSR of the same boxes."""
+    rng = [-20.0, -20.0, -1.0, 20.0, 20.0, 5.4]
+    m, o, cv, _ = oracle.generate_inputs(n, 0, rng, seed=5, num_outside=n // 20)
+    out, toff, t2g = _maps(m.numpy(), o.numpy(), cv.numpy(), None, [0.4] * 3, rng)
+    density, cov_inv, lb, ub, nvox, gf, off, ids, _ = out
+    dims = tuple(int(v) for v in density.shape)
+    goff, gids, otoff, ot2g = oracle.csr_from_boxes(lb, ub, dims)
+    np.testing.assert_array_equal(off.astype(np.int64), goff)
+    np.testing.assert_array_equal(ids, gids)
+    np.testing.assert_array_equal(toff.astype(np.int64), otoff)
+    np.testing.assert_array_equal(t2g, ot2g)
+
+
 @pytest.mark.parametrize("name", CASES)
 def test_forward_backward_vs_reference_golden(golden, name):
     g = golden(name)
