@@ -638,36 +638,62 @@ void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]) {
 namespace {
 // e_v = sum_c gF_vc F_vc (F = grid_feats, the forward's output: the reference's at::bmm, cu:1996) for the
 // voxels of the units with more than kSlots Gaussians, where forming e_v from S would need every slot
-// pass twice.  Block = unit, warp = voxel rows, fixed summation order (deterministic).
-__global__ void __launch_bounds__(256) unit_ev_kernel(const int32_t* __restrict__ unit_offsets, int tzp_n, int tx_begin,
-                                                      Grid G, const float* __restrict__ gF,
-                                                      const float* __restrict__ F, int C, int vec,
-                                                      float* __restrict__ ev) {
-    const int u = blockIdx.x;
-    if (unit_offsets[u + 1] - unit_offsets[u] <= kSlots) return;
-    const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int v = warp; v < kUV; v += 8) {
-        const int x = ug.tx * kTile + (v >> 5), y = ug.ty * kTile + ((v >> 3) & 3), z = ug.tzp * 8 + (v & 7);
-        if (x >= G.dims[0] || y >= G.dims[1] || z >= G.dims[2]) continue;  // warp-uniform
-        const int64_t row = grid_row(G, x, y, z);
-        const float* a = gF + row * C;
-        const float* b = F + row * C;
-        float acc = 0.0f;
+// pass twice.  Warp = one (unit, quad of 4 z-consecutive voxel rows) item of a grid-stride walk over all
+// units: the unit check and the geometry are paid once per quad, the loads of the 4 rows are in flight
+// together, and each row keeps the fixed per-lane channel order and warp reduction (deterministic).
+__global__ void __launch_bounds__(256, 4) unit_ev_kernel(const int32_t* __restrict__ unit_offsets, int num_units,
+                                                      int tzp_n, int tx_begin, Grid G,
+                                                      const float* __restrict__ gF, const float* __restrict__ F,
+                                                      int C, int vec, float* __restrict__ ev) {
+    constexpr int kQuads = kUV / 4;  // 32 quads of a unit: x 4, y 4, z half 2
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t items = (int64_t)num_units * kQuads;
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < items; w += nw) {
+        const int u = (int)(w / kQuads), q = (int)(w - (int64_t)u * kQuads);
+        if (unit_offsets[u + 1] - unit_offsets[u] <= kSlots) continue;  // warp-uniform
+        const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
+        const int x = ug.tx * kTile + (q >> 3), y = ug.ty * kTile + ((q >> 1) & 3);
+        const int z0 = ug.tzp * 8 + (q & 1) * 4;
+        if (x >= G.dims[0] || y >= G.dims[1] || z0 >= G.dims[2]) continue;  // warp-uniform
+        const int nz = min(4, G.dims[2] - z0);                               // rows of the quad in the grid
+        int64_t rows[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rows[i] = grid_row(G, x, y, z0 + (i < nz ? i : 0));
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (vec) {
             for (int c = 4 * lane; c < C; c += 128) {
-                const float4 p = *reinterpret_cast<const float4*>(a + c), q = *reinterpret_cast<const float4*>(b + c);
-                acc = fmaf(p.x, q.x, acc);
-                acc = fmaf(p.y, q.y, acc);
-                acc = fmaf(p.z, q.z, acc);
-                acc = fmaf(p.w, q.w, acc);
+                float4 p[4], r[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i < nz) {
+                        p[i] = *reinterpret_cast<const float4*>(gF + rows[i] * C + c);
+                        r[i] = *reinterpret_cast<const float4*>(F + rows[i] * C + c);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i < nz) {
+                        acc[i] = fmaf(p[i].x, r[i].x, acc[i]);
+                        acc[i] = fmaf(p[i].y, r[i].y, acc[i]);
+                        acc[i] = fmaf(p[i].z, r[i].z, acc[i]);
+                        acc[i] = fmaf(p[i].w, r[i].w, acc[i]);
+                    }
+                }
             }
         } else {
-            for (int c = lane; c < C; c += 32) acc = fmaf(a[c], b[c], acc);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (i < nz)
+                    for (int c = lane; c < C; c += 32) acc[i] = fmaf(gF[rows[i] * C + c], F[rows[i] * C + c], acc[i]);
+            }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) ev[row] = acc;
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+            if (lane == 0 && i < nz) ev[rows[i]] = acc[i];
+        }
     }
 }
 }  // namespace
@@ -705,9 +731,16 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
     if (grid_feats != nullptr && ev_buf != nullptr) {
         const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0) &&
                         (reinterpret_cast<uintptr_t>(grid_feats) % 16 == 0);
+        // 8 warps per block, as many blocks as are resident at once: the grid-stride walk covers every
+        // (unit, row quad) item
+        int per_sm = 0;
+        G2V_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, unit_ev_kernel, 256, 0));
+        const int64_t ev_blocks =
+            std::min<int64_t>((int64_t)sms * std::max(per_sm, 1), ((int64_t)num_units * (kUV / 4) + 7) / 8);
         G2V_TIMED("unit_ev_kernel", s,
-                  unit_ev_kernel<<<(unsigned)num_units, 256, 0, s>>>(unit_offsets, (G.tiles[2] + 1) / 2, tile_x_begin,
-                                                                     G, grad_feats, grid_feats, C, vec, ev_buf));
+                  unit_ev_kernel<<<(unsigned)ev_blocks, 256, 0, s>>>(unit_offsets, num_units, (G.tiles[2] + 1) / 2,
+                                                                     tile_x_begin, G, grad_feats, grid_feats, C, vec,
+                                                                     ev_buf));
         G2V_LAUNCH_CHECK("unit_ev_kernel");
         ev = ev_buf;
     }
