@@ -117,9 +117,11 @@ __global__ void __launch_bounds__(256) feature_colmax_kernel(const float* __rest
     atomicMax(&colmax[c], __float_as_uint(m));
 }
 
-// features (N, C) fp32 -> hi / lo halves (N, Cp) scaled by 2^k_c, and unscale[c] = 2^-k_c.
+// features (N, C) fp32 -> hi / lo halves (N, Cp) scaled by 2^k_c, and unscale[c] = 2^-k_c.  The scaling
+// is a product with the exact power of two (k_c in [-100, 100]: a normal float), which rounds like
+// ldexpf; vec: C % 8 == 0 and a 16-byte aligned base, so a thread's 8 features are two float4 loads.
 __global__ void __launch_bounds__(256) feature_split_kernel(const float* __restrict__ f, int64_t n, int C, int Cp,
-                                                            const unsigned* __restrict__ colmax,
+                                                            int vec, const unsigned* __restrict__ colmax,
                                                             __half* __restrict__ hi, __half* __restrict__ lo,
                                                             float* __restrict__ unscale) {
     const int64_t chunks = (int64_t)Cp / 8;
@@ -127,19 +129,27 @@ __global__ void __launch_bounds__(256) feature_split_kernel(const float* __restr
     if (i >= n * chunks) return;
     const int64_t r = i / chunks;
     const int c8 = (int)(i - r * chunks) * 8;
+    float x[8];
+    if (vec) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(f + r * C + c8));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(f + r * C + c8 + 4));
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = c8 + j < C ? f[r * C + c8 + j] : 0.0f;
+    }
     __align__(16) __half h[8], l[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int c = c8 + j;
-        float x = 0.0f;
         int k = 0;
         if (c < C) {
-            x = f[r * C + c];
             const float m = __uint_as_float(colmax[c]);
             k = (m > 0.0f) ? max(-100, min(100, 14 - pow2_exponent(m))) : 0;
         }
-        tc::split_half(ldexpf(x, k), h[j], l[j]);
-        if (r == 0) unscale[c] = ldexpf(1.0f, -k);
+        tc::split_half(x[j] * __int_as_float((127 + k) << 23), h[j], l[j]);
+        if (r == 0) unscale[c] = __int_as_float((127 - k) << 23);
     }
     *reinterpret_cast<uint4*>(hi + r * Cp + c8) = *reinterpret_cast<const uint4*>(h);
     *reinterpret_cast<uint4*>(lo + r * Cp + c8) = *reinterpret_cast<const uint4*>(l);
@@ -634,14 +644,15 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
     float* unscale = cv.take<float>((size_t)Cp);
     if (n > 0) {
         G2V_CUDA(cudaMemsetAsync(colmax, 0, sizeof(unsigned) * Cp, s));
-        const int rows = 256;
+        const int rows = 64;  // rows per block: enough blocks in flight to stream the features
         dim3 g1((C + 255) / 256, (unsigned)((n + rows - 1) / rows));
         G2V_TIMED("feature_colmax_kernel", s, feature_colmax_kernel<<<g1, 256, 0, s>>>(features, n, C, rows, colmax));
         G2V_LAUNCH_CHECK("feature_colmax_kernel");
         const int64_t total = n * (Cp / 8);
         G2V_TIMED("feature_split_kernel", s,
-                  feature_split_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(features, n, C, Cp, colmax, hi,
-                                                                                    lo, unscale));
+                  feature_split_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+                      features, n, C, Cp, (C % 8 == 0 && (reinterpret_cast<uintptr_t>(features) & 15) == 0) ? 1 : 0,
+                      colmax, hi, lo, unscale));
         G2V_LAUNCH_CHECK("feature_split_kernel");
     }
     GParams* gp = cv.take<GParams>((size_t)(n > 0 ? n : 1));
