@@ -184,7 +184,8 @@ def make_inputs(cfg, seed):
 
 
 def algorithmic_bytes(kernel, n, c, V, M, MB, ntiles):
-    """Algorithmic HBM bytes of one launch over the whole grid (per-unit figures of the design doc)."""
+    """Algorithmic HBM bytes of one launch over the whole grid: the bytes each kernel must move per unit of work
+    (voxel rows of grid_feats / its gradient, feature rows, per-Gaussian records, CSR entries)."""
     per_gauss = n * (12 + 4 + 36 + 24)  # mean, opacity, cov_inv, lb/ub
     kernel = {"splat_tc_kernel": "splat_tile_kernel", "spass_tc_kernel": "spass_kernel",
               "fpass_tc_kernel": "fpass_kernel"}.get(kernel, kernel)
@@ -200,7 +201,7 @@ def algorithmic_bytes(kernel, n, c, V, M, MB, ntiles):
 
 
 def algorithmic_flops(kernel, c, M):
-    """Contraction FLOPs of one launch (SURVEY 8d: forward 2*64*M*C, backward 4*64*M*C, split here between
+    """Contraction FLOPs of one launch (forward 2*64*M*C, backward 4*64*M*C, split here between
     the tile pass and the feature-gradient pass) and the tensor-core FLOPs that realise them with three
     bf16/f16 products (hi*hi + hi*lo + lo*hi) per fp32 product."""
     if kernel in ("splat_tc_kernel", "spass_tc_kernel", "fpass_tc_kernel"):
@@ -219,7 +220,9 @@ def load_bf16_peak():
 
 
 def step_bytes(n, c, V, M):
-    """Algorithmic bytes of one fwd+bwd step (SURVEY formula, 8.11 GB at cfg3)."""
+    """Algorithmic bytes of one fwd+bwd step (8.11 GB at cfg3): forward = N*52 (mean, opacity, covariance)
+    + 4NC (features) + 4V (density) + 4VC (grid_feats) + N*64 (cov_inv, boxes, voxel counts) + 4(N+1) + 4M;
+    backward = 8V + 8VC (both gradients and density / grid_feats) + 4NC + N*76 + 4(N+1) + 4M + N*52 + 4NC."""
     fwd = n * 52 + 4 * n * c + 4 * V + 4 * V * c + n * 64 + 4 * (n + 1) + 4 * M
     bwd = 8 * V + 8 * V * c + 4 * n * c + n * 76 + 4 * (n + 1) + 4 * M + n * 52 + 4 * n * c
     return fwd + bwd

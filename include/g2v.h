@@ -101,9 +101,11 @@ G2V_API int g2v_forward_prepare_capped(const float* means3d, const float* covari
  * callers cannot provide one -- e.g. a serving process that reserves all device memory at start-up and
  * must not call cudaMalloc afterwards, or a plugin whose host application owns every device allocation.
  * The scratch is a fixed array of about 1 MiB in the library's own device memory, so inputs are limited
- * to G2V_STATIC_MAX_GAUSSIANS Gaussians (larger inputs fail with G2V_ERROR_SIZE_LIMIT).  The first call
- * on a device looks up that array's address (call it once before any stream capture); all calls share
- * the array, so calls that overlap on the GPU race.
+ * to G2V_STATIC_MAX_GAUSSIANS Gaussians (larger inputs fail with G2V_ERROR_SIZE_LIMIT); the grid limits
+ * and the device-error reporting are those of g2v_forward_prepare.  The first call on a device looks up
+ * that array's address (call it once before any stream capture) and caches it per device ordinal, which
+ * assumes one primary context per device for the life of the process (not after cudaDeviceReset); all
+ * calls share the array, so calls that overlap on the GPU race.
  */
 #define G2V_STATIC_MAX_GAUSSIANS 262144
 G2V_API int g2v_forward_prepare_static(const float* means3d, const float* covariances, int64_t num_gaussians,

@@ -1,6 +1,6 @@
 """Build the reference's CUDA voxelizer into oracle/_ref/ -- TEST INFRASTRUCTURE ONLY.
 
-    python oracle/build_ref.py            # needs the reference checkout ($G2V_REFERENCE_ROOT or /root/reference)
+    python oracle/build_ref.py            # needs the reference checkout: $G2V_REFERENCE_ROOT, else a "reference" folder beside the repo
 
 Compiles the reference's src/cuda_gaussian_voxelizer.cu and src/cuda_feats_loss.cu where they lie
 (nothing is copied into this repository) together with oracle/ref_bindings.cpp, with the reference's own nvcc flags
@@ -15,7 +15,8 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REF = os.environ.get("G2V_REFERENCE_ROOT", "/root/reference")
+# the reference checkout: $G2V_REFERENCE_ROOT, else the folder "reference" next to this repository
+REF = os.environ.get("G2V_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 NAME = "g2v_reference_ext"
 
 

@@ -34,7 +34,6 @@ SOURCES = {
     "g2v_static.cu": [],
     "g2v_splat_tc.cu": [],
     "g2v_grad_tc.cu": [],
-    "g2v_fpass_pair.cu": [],
     "g2v_spass_tc.cu": [],
     "g2v_selftest.cu": [],
     "g2v_loss.cu": [],

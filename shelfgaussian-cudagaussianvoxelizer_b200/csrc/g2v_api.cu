@@ -112,6 +112,8 @@ int device_error_ptr(int** out) {
     return 0;
 }
 
+}  // namespace
+
 // Reads the error word with the caller's stream (the caller synchronises), queued before the sync.
 int queue_error_read(cudaStream_t s, int* host_word) {
     int* p = nullptr;
@@ -135,7 +137,7 @@ int report_device_error(int word, cudaStream_t s) {
 }
 
 // Kernel variant: the tensor-core path unless G2V_VARIANT=simt.
-bool use_tensor_cores() {
+static bool use_tensor_cores() {
     const char* v = getenv("G2V_VARIANT");
     return !(v && strcmp(v, "simt") == 0);
 }
@@ -170,6 +172,10 @@ int make_grid(const float size[3], const float range[6], Grid& G) {
     }
     return 0;
 }
+
+void clear_error() { g_msg[0] = 0; }
+
+namespace {
 
 // A batch of num_scenes scenes of the same grid stacked along x: scene b occupies voxel x rows
 // [b X, (b+1) X) of the volume arrays, i.e. the arrays are (B, X, Y, Z[, C]).  Tiles must not straddle

@@ -435,22 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
 }
 }  // namespace
 
-int launch_fpass_tc_pair(const float* grad_feats, int C, const float* density, const GParams* gparams,
-                         const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets,
-                         int bx_begin, int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end,
-                         const Grid& G, float* partialF, int64_t block_pair_cap, int* err, cudaStream_t s);
-
-// The feature-gradient pass: one CTA per (block, 256-channel group) with passes of 256 slots (the
-// kernel above, the default) or, with G2V_FPASS=pair, on CTA pairs with passes of 512 slots
-// (g2v_fpass_pair.cu; correct, measured slower at cfg3: 2.24 vs 1.81 ms).
+// The feature-gradient pass: one CTA per (block, 256-channel group) with passes of 256 slots.
 int launch_fpass_tc(const float* grad_feats, int C, const float* density, const GParams* gparams,
                     const int32_t* block_offsets, const int32_t* block_lists, const int32_t* g2b_offsets, int bx_begin,
                     int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
                     int64_t block_pair_cap, int* err, cudaStream_t s) {
-    const char* mode = getenv("G2V_FPASS");
-    if (mode && strcmp(mode, "pair") == 0)
-        return launch_fpass_tc_pair(grad_feats, C, density, gparams, block_offsets, block_lists, g2b_offsets, bx_begin,
-                                    nbx, nby, nbz, B, tx_begin, tx_end, G, partialF, block_pair_cap, err, s);
     const int64_t nblocks = (int64_t)nbx * nby * nbz;
     if (nblocks <= 0 || C <= 0) return 0;
     const int ngroups = (C + kCG - 1) / kCG;

@@ -97,7 +97,15 @@ struct Carver {
 
 // Error reporting (defined in g2v_api.cu).
 void set_error(const char* fmt, ...);
+void clear_error();  // empties the thread's g2v_last_error() message (done at every entry point)
 int cuda_fail(cudaError_t e, const char* what);
+// Grid geometry from voxel_size / voxel_range, with the library's size limits (a g2v_status code).
+int make_grid(const float size[3], const float range[6], Grid& G);
+// Device error word of the bounded waits and capacity guards: queue its read on `s` (the caller
+// synchronises the stream before looking at *host_word), then turn a non-zero word into a status
+// (clearing the word on the device).
+int queue_error_read(cudaStream_t s, int* host_word);
+int report_device_error(int word, cudaStream_t s);
 
 #define G2V_LAUNCH_CHECK(what)                                  \
     do {                                                        \

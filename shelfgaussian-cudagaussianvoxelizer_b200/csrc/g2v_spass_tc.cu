@@ -731,12 +731,9 @@ int launch_spass_tc(const float* grad_density, const float* grad_feats, const fl
     if (grid_feats != nullptr && ev_buf != nullptr) {
         const int vec = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(grad_feats) % 16 == 0) &&
                         (reinterpret_cast<uintptr_t>(grid_feats) % 16 == 0);
-        // 8 warps per block, as many blocks as are resident at once: the grid-stride walk covers every
-        // (unit, row quad) item
-        int per_sm = 0;
-        G2V_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, unit_ev_kernel, 256, 0));
-        const int64_t ev_blocks =
-            std::min<int64_t>((int64_t)sms * std::max(per_sm, 1), ((int64_t)num_units * (kUV / 4) + 7) / 8);
+        // 8 warps per block, as many blocks as are resident at once (__launch_bounds__(256, 4): four per
+        // SM): the grid-stride walk covers every (unit, row quad) item
+        const int64_t ev_blocks = std::min<int64_t>((int64_t)sms * 4, ((int64_t)num_units * (kUV / 4) + 7) / 8);
         G2V_TIMED("unit_ev_kernel", s,
                   unit_ev_kernel<<<(unsigned)ev_blocks, 256, 0, s>>>(unit_offsets, num_units, (G.tiles[2] + 1) / 2,
                                                                      tile_x_begin, G, grad_feats, grid_feats, C, vec,

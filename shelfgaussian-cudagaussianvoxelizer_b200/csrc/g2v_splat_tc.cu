@@ -35,8 +35,8 @@
 // unit's later jobs copy them back with cp.async.  Steps beyond kWcSteps (units of more than 512
 // Gaussians) are evaluated in every job.
 // Seven stages; every mbarrier wait is bounded.
+#include <algorithm>
 #include <cstddef>
-
 #include <cstring>
 
 #include "g2v_internal.cuh"
@@ -105,15 +105,17 @@ __device__ __forceinline__ int pow2_exponent(float m) {
     return e - 1;
 }
 
-// Per-channel max |f| (as float bits; non-negative floats order like integers).
+// Per-channel max |f| (as float bits; non-negative floats order like integers).  Row blocks of
+// rows_per_block rows are walked with a stride of gridDim.y, so any row count fits the grid's y limit.
 __global__ void __launch_bounds__(256) feature_colmax_kernel(const float* __restrict__ f, int64_t n, int C,
                                                              int rows_per_block, unsigned* __restrict__ colmax) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
-    const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
-    const int64_t r1 = min(n, r0 + rows_per_block);
     float m = 0.0f;
-    for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, fabsf(f[r * C + c]));
+    for (int64_t r0 = (int64_t)blockIdx.y * rows_per_block; r0 < n; r0 += (int64_t)gridDim.y * rows_per_block) {
+        const int64_t r1 = min(n, r0 + rows_per_block);
+        for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, fabsf(f[r * C + c]));
+    }
     atomicMax(&colmax[c], __float_as_uint(m));
 }
 
@@ -645,7 +647,8 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
     if (n > 0) {
         G2V_CUDA(cudaMemsetAsync(colmax, 0, sizeof(unsigned) * Cp, s));
         const int rows = 64;  // rows per block: enough blocks in flight to stream the features
-        dim3 g1((C + 255) / 256, (unsigned)((n + rows - 1) / rows));
+        const int64_t row_blocks = (n + rows - 1) / rows;
+        dim3 g1((C + 255) / 256, (unsigned)std::min<int64_t>(row_blocks, 65535));
         G2V_TIMED("feature_colmax_kernel", s, feature_colmax_kernel<<<g1, 256, 0, s>>>(features, n, C, rows, colmax));
         G2V_LAUNCH_CHECK("feature_colmax_kernel");
         const int64_t total = n * (Cp / 8);

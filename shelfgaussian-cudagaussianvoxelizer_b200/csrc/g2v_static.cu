@@ -10,8 +10,14 @@
 // until the process exits.  Host code cannot use the array's name as a device address, so the first
 // call on each device looks the address up with cudaGetSymbolAddress (with that device current) and
 // caches it; that lookup can load the library's device code on the device, so make the first call
-// before capturing a stream into a CUDA graph.  All calls share the one array: two calls whose work
-// overlaps on the GPU (different streams, or different host threads without ordering) race on it.
+// before capturing a stream into a CUDA graph.  The cache is kept per device ordinal and assumes one
+// primary context per device for the life of the process: after cudaDeviceReset (or any teardown and
+// re-creation of the device's context) the cached address is stale and must not be used.  All calls
+// share the one array: two calls whose work overlaps on the GPU (different streams, or different host
+// threads without ordering) race on it.
+//
+// Grid limits and error reporting are those of g2v_forward_prepare: the same make_grid checks, and the
+// library's device error word is read at the call's one synchronisation and reported as a status.
 #include <mutex>
 
 #include "g2v.h"
@@ -60,36 +66,24 @@ extern "C" int g2v_forward_prepare_static(const float* means3d, const float* cov
                                           const float voxel_size[3], const float voxel_range[6], float* cov_inv,
                                           int32_t* valid_voxel_lb, int32_t* valid_voxel_ub, int32_t* num_voxels,
                                           int32_t* g2t_offsets, void* stream, int64_t* num_pairs) {
+    clear_error();
     if (num_gaussians > kStaticMaxGaussians) {
         set_error("g2v_forward_prepare_static handles at most %lld Gaussians (got %lld); use "
                   "g2v_forward_prepare with a workspace for larger inputs",
                   (long long)kStaticMaxGaussians, (long long)num_gaussians);
         return G2V_ERROR_SIZE_LIMIT;
     }
-    if (num_gaussians < 0 || !g2t_offsets || !num_pairs || !voxel_size || !voxel_range ||
+    Grid G;
+    int rc = make_grid(voxel_size, voxel_range, G);
+    if (rc) return rc;
+    if (num_gaussians < 0 || !g2t_offsets || !num_pairs ||
         (num_gaussians > 0 && (!means3d || !covariances || !cov_inv || !valid_voxel_lb || !valid_voxel_ub ||
                                !num_voxels))) {
         set_error("g2v_forward_prepare_static: invalid pointer or Gaussian count");
         return G2V_ERROR_INVALID_VALUE;
     }
-    Grid G;
-    for (int a = 0; a < 3; ++a) {
-        const float q = (voxel_range[3 + a] - voxel_range[a]) / voxel_size[a];
-        if (!(q >= 1.0f) || !(q < 1073741824.0f)) {
-            set_error("invalid voxel grid along axis %d", a);
-            return G2V_ERROR_INVALID_VALUE;
-        }
-        G.r0[a] = voxel_range[a];
-        G.r1[a] = voxel_range[3 + a];
-        G.h[a] = voxel_size[a];
-        G.dims[a] = static_cast<int>(q);
-        G.tiles[a] = (G.dims[a] + kTile - 1) / kTile;
-    }
-    G.xoff = 0;
-    G.xlen = G.dims[0];
-    G.scene_x = 0;
     void* base = nullptr;
-    int rc = scratch_address(&base);
+    rc = scratch_address(&base);
     if (rc) return rc;
     unsigned char* b = static_cast<unsigned char*>(base);
     int32_t* counts = reinterpret_cast<int32_t*>(b);
@@ -103,8 +97,11 @@ extern "C" int g2v_forward_prepare_static(const float* means3d, const float* cov
         return rc;
     if ((rc = launch_exclusive_scan(counts, num_gaussians, g2t_offsets, total, scan_ws, s))) return rc;
     int64_t m = 0;
+    int word = 0;
     G2V_CUDA(cudaMemcpyAsync(&m, total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    if ((rc = queue_error_read(s, &word))) return rc;
     G2V_CUDA(cudaStreamSynchronize(s));
+    if ((rc = report_device_error(word, s))) return rc;
     if (m > INT32_MAX) {
         set_error("%lld (Gaussian, tile) pairs exceed the int32 range of the Gaussian->Tile map", (long long)m);
         return G2V_ERROR_SIZE_LIMIT;

@@ -341,65 +341,3 @@ struct __align__(16) GParams {
 int launch_pack_params(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
                        const int32_t* ub, int64_t n, GParams* out, cudaStream_t s);
 }  // namespace g2v
-
-namespace g2v {
-namespace tc {
-// ---------------------------------------------------------------------------------------------
-// CTA pairs (a cluster of two CTAs sharing one tcgen05 MMA, cta_group::2).  The even CTA of the pair
-// (rank 0) issues the MMAs; the A operand's M rows and the B operand's N columns are split between the
-// two CTAs' shared memory at the same offsets, and each CTA's TMEM holds the accumulator rows of its own
-// A rows.  Producers of both CTAs arrive on the leader's mbarriers through shared::cluster addresses;
-// the leader's commits arrive on the same barrier offset in both CTAs.  Every load of the pair is a plain
-// per-CTA load.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// shared::cluster address of the variable at shared::cta address `saddr` in the cluster's CTA `rank`.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
-    return d;
-}
-// Arrive on an mbarrier given by its shared::cluster address (another CTA's barrier).  The operands the
-// arrival announces were written with ordinary stores and made visible to the async proxy
-// (fence.proxy.async) before it; the MMAs that read them are issued after the barrier's phase completed.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// TMEM allocation for a CTA pair: one warp of each CTA (same warp index, same destination offset).
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
-                 "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D[tmem] (+)= A * B over the pair (M = 256: rows 0-127 from the leader's A, 128-255 from the peer's;
-// B's N columns: the first N/2 from the leader, the rest from the peer); issued by one leader thread.
-__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                                bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
-}
-// Arrive on the mbarrier at shared::cta offset `mbar_saddr` in every CTA of `cta_mask` once all prior
-// pair MMAs of this thread have completed.
-__device__ __forceinline__ void mma_commit_pair(uint32_t mbar_saddr, uint16_t cta_mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            mbar_saddr),
-        "h"(cta_mask)
-        : "memory");
-}
-// All threads of both CTAs of the cluster.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-}  // namespace tc
-}  // namespace g2v

@@ -1,6 +1,6 @@
 """Generate the golden vectors in tests/golden/*.npz from the reference's own brute force.
 
-Run in a container that has the reference checkout (default /root/reference, or $G2V_REFERENCE_ROOT):
+Run in a container that has the reference checkout ($G2V_REFERENCE_ROOT, else a "reference" folder beside the repo):
 
     python tests/golden/make_golden.py
 
@@ -33,7 +33,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle import oracle  # noqa: E402
 
-REF_ROOT = os.environ.get("G2V_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("G2V_REFERENCE_ROOT") or os.path.join(os.path.dirname(REPO), "reference")
 
 
 def load_reference_test():

@@ -128,12 +128,13 @@ def test_tensor_core_backward_matches_oracle_and_fp32_variant(n, c, seed, half, 
 
 
 @pytest.mark.parametrize("n,c,seed,half,var_max", [
-    (300, 24, 1, 6.0, 2.5),      # one pair pass, the peer CTA's channels all beyond C
-    (3000, 300, 3, 6.0, 8.0),    # blocks of > 256 and > 512 Gaussians (two slot ranges, several passes)
+    (300, 24, 1, 6.0, 2.5),      # one slot pass, a single channel group with most channels beyond C
+    (3000, 300, 3, 6.0, 8.0),    # blocks of > 256 and > 512 Gaussians (several slot passes)
     (2000, 37, 2, 8.0, 2.5),     # C not a multiple of 4 (converters load the gradient rows themselves)
 ])
-def test_feature_gradient_pair_variant_matches_default(n, c, seed, half, var_max):
-    """G2V_FPASS=pair (CTA pairs sharing each MMA, cta_group::2) gives the default kernel's gradients."""
+def test_feature_gradient_pass_against_oracle(n, c, seed, half, var_max):
+    """The tensor-core backward on block lists of one, two and several slot passes: every gradient,
+    the feature gradient included, within the parity bar of the float64 oracle."""
     from CudaGaussianVoxelizer import _C
     size, rng = [0.4] * 3, [-half, -half, -1.0, half, half, 5.4]
     m, o, cv, f = oracle.generate_inputs(n, c, rng, seed=seed, num_outside=n // 20, var_max=var_max)
@@ -142,21 +143,14 @@ def test_feature_gradient_pair_variant_matches_default(n, c, seed, half, var_max
     gD, gF = torch.randn(*dims, generator=g).cuda(), torch.randn(*dims, c, generator=g).cuda()
     mt, ot, ct, ft = dev(m.numpy(), o.numpy(), cv.numpy(), f.numpy())
     density, cov_inv, lb, ub, nvox, grid_feats, off, ids, _ = _C.gaussian_voxelizer_forward(mt, ot, ct, size, rng, ft)
-
-    def bwd():
-        return [t.cpu().numpy() for t in _C.gaussian_voxelizer_backward(
-            gD, gF, mt, ot, cov_inv, size, rng, lb, ub, nvox, off, ids, density, grid_feats, ft)[:4]]
-
-    single = _with_env({"G2V_FPASS": "single"}, bwd)
-    pair = _with_env({"G2V_FPASS": "pair"}, bwd)
-    for name, a, b in zip(("grad_means", "grad_cov", "grad_opacity"), pair[:3], single[:3]):
-        np.testing.assert_array_equal(a, b, err_msg=name)  # the feature pass does not touch these
-    assert_close("grad_features pair vs single", pair[3], single[3])
+    got = [t.cpu().numpy() for t in _C.gaussian_voxelizer_backward(
+        gD, gF, mt, ot, cov_inv, size, rng, lb, ub, nvox, off, ids, density, grid_feats, ft)[:4]]
     lb_h, ub_h = lb.cpu().numpy(), ub.cpu().numpy()
     m, o, cv, f = m.numpy(), o.numpy(), cv.numpy(), f.numpy()
     dref, fref = oracle.forward(m, o, cv, f, lb_h, ub_h, size, rng, dims)
     ref = oracle.backward(m, o, cv, f, lb_h, ub_h, size, rng, dims, gD.cpu().numpy(), gF.cpu().numpy(), dref, fref)
-    assert_close("grad_features (pair)", pair[3], ref[3])
+    for name, a, b in zip(("grad_means", "grad_cov", "grad_opacity", "grad_features"), got, ref):
+        assert_close(name, a, b)
 
 
 @pytest.mark.parametrize("env,c", [({"G2V_SPLAT_WW": "8"}, 600), ({"G2V_SPLAT_WCACHE": "0"}, 600),

@@ -5,8 +5,10 @@ later, a plugin whose host application owns every allocation) cannot pass the wo
 g2v_forward_prepare needs; this entry point keeps its scratch in a fixed array inside the library.
 The test calls it through the C ABI and checks that, on two calls in a row with different inputs
 (a large scene, then a smaller one, so stale scratch from the first call would show), it returns
-exactly what g2v_forward_prepare returns.  It also checks the size limit.  The file is named so that
-pytest collects it last.
+exactly what g2v_forward_prepare returns.  The first size (200000 Gaussians, above the 65536 counts
+the one-block scan handles) takes the three-kernel scan through the block-sum region of the static
+scratch; the second takes the one-block scan.  It also checks the size limit, and that a grid the
+workspace entry point rejects is rejected here too.  The file is named so that pytest collects it last.
 """
 import ctypes
 
@@ -52,7 +54,7 @@ def _static(lib, _lib, means, cov, n, stream):
     return outs, m.value
 
 
-@pytest.mark.parametrize("sizes", [(20000, 700)])
+@pytest.mark.parametrize("sizes", [(200000, 700)])
 def test_static_prepare_matches_workspace_prepare_twice(sizes):
     from CudaGaussianVoxelizer import _lib
     lib = _lib.load()
@@ -80,3 +82,19 @@ def test_static_prepare_rejects_oversized_input():
                                         dummy, None, ctypes.byref(m))
     assert rc == 3  # G2V_ERROR_SIZE_LIMIT, before any device work
     assert b"at most 262144" in lib.g2v_last_error()
+
+
+def test_static_prepare_rejects_the_grids_the_workspace_path_rejects():
+    """Grid limits are shared with g2v_forward_prepare: a grid of more than INT32_MAX / 2 tiles fails
+    with the same status on both entry points, before any device work."""
+    from CudaGaussianVoxelizer import _lib
+    lib = _lib.load()
+    m = ctypes.c_int64()
+    dummy = ctypes.c_void_p(256)
+    size, rng = [1e-3] * 3, [-500.0, -500.0, -500.0, 500.0, 500.0, 500.0]
+    rc_ws = lib.g2v_forward_prepare(dummy, dummy, 10, _lib.f3(size), _lib.f6(rng), dummy, dummy, dummy, dummy,
+                                    dummy, dummy, 1 << 20, None, ctypes.byref(m))
+    rc_st = lib.g2v_forward_prepare_static(dummy, dummy, 10, _lib.f3(size), _lib.f6(rng), dummy, dummy, dummy,
+                                           dummy, dummy, None, ctypes.byref(m))
+    assert rc_ws == rc_st == 3  # G2V_ERROR_SIZE_LIMIT
+    assert b"too large" in lib.g2v_last_error()
