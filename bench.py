@@ -308,6 +308,8 @@ def run_ours(args, rank, world, dev):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    resident = torch.cuda.memory_allocated(dev)
     sampler = ClockSampler(gpu_id_for(dev.index))
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -317,6 +319,7 @@ def run_ours(args, rank, world, dev):
     ev1.record(stream)
     torch.cuda.synchronize()
     clocks = sampler.stop()
+    peak_mem = torch.cuda.max_memory_allocated(dev)
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
     if world > 1:
@@ -412,9 +415,10 @@ def run_ours(args, rank, world, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    cpu = None
+    cpu = cpu1 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cfg, args.seed, threads=os.cpu_count() or 1, steps=1)
+        cpu1 = cpu_baseline_cfg1(args.seed)
 
     line = {
         "metric": METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
@@ -435,9 +439,14 @@ def run_ours(args, rank, world, dev):
         "step_roofline": {"algorithmic_bytes": sb, "achieved_gbs": sb / (ms * 1e-3) / 1e9,
                           "frac": sb / (ms * 1e-3) / 1e9 / peak},
         "cpu_baseline": cpu,
+        "cpu_baseline_cfg1": cpu1,
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clocks,
+        "memory": {"peak_gb": round(peak_mem / 1e9, 3), "resident_before_steps_gb": round(resident / 1e9, 3),
+                   "what": "torch.cuda.max_memory_allocated over the timed steps: inputs and the randn upstream "
+                           "gradients (resident before the steps), outputs, gradients and the library's "
+                           "workspaces"},
     }
     return line
 
@@ -475,8 +484,39 @@ def cpu_baseline(cfg, seed, threads, steps=1, slab_vox=16):
                       f"float64, scaled x{X / (x1 - x0):.1f} to the full grid; {t:.2f} s per sample"}
 
 
-def reference_cuda(cfg, seed, dev, steps=2):
-    """Time the reference's own CUDA build (oracle/_ref, compiled from its sources) on this GPU."""
+def cpu_baseline_cfg1(seed, steps=3):
+    """The reference's CPU brute force (its float64 restatement in oracle/, test/test_reference.py:57-79) at
+    cfg1, the configuration the reference's own CPU test runs (N=512, C=32, 40x40x16): the whole grid,
+    forward + backward with randn upstream gradients, timed on one thread and on every host thread."""
+    import numpy as np
+    import torch
+    from oracle import oracle
+    size, rng, m, o, c, f = make_inputs(CONFIGS["cfg1"], seed)
+    m, o, c, f = m.numpy(), o.numpy(), c.numpy(), f.numpy()
+    bx = oracle.boxes(m, c, size, rng)
+    dims = bx.dims
+    rs = np.random.default_rng(7)
+    gD = rs.standard_normal(tuple(dims), dtype=np.float32)
+    gF = rs.standard_normal(tuple(dims) + (f.shape[1],), dtype=np.float32)
+    nproc = os.cpu_count() or 1
+    out = {"unit": "ms", "kind": "port", "nproc": nproc, "torch_num_threads": torch.get_num_threads(),
+           "steps": steps, "workload": "cfg1: N=512, C=32, 40x40x16 voxels, whole grid, fwd+bwd, float64"}
+    for key, threads in (("threads_1", 1), ("threads_all", nproc)):
+        ts = []
+        for _ in range(steps + 1):  # the first run is a warm-up
+            t0 = time.perf_counter()
+            D, F = oracle.forward(m, o, c, f, bx.lb, bx.ub, size, rng, dims, nthreads=threads)
+            oracle.backward(m, o, c, f, bx.lb, bx.ub, size, rng, dims, gD, gF, D, F, nthreads=threads)
+            ts.append(time.perf_counter() - t0)
+        out[key] = round(statistics.median(ts[1:]) * 1e3, 2)
+    out["cores"] = {"threads_1": 1, "threads_all": nproc}
+    return out
+
+
+def reference_cuda(cfg, seed, dev, steps=5, warmup=2):
+    """Time the reference's own CUDA build (oracle/_ref, compiled from its sources) on this GPU: `steps`
+    forward + backward steps after `warmup`, CUDA events on the current stream, clocks sampled over the
+    timed steps, and the allocator's peak memory over them (inputs and upstream gradients included)."""
     from oracle import build_ref
     ext = build_ref.load()
     if ext is None:
@@ -498,16 +538,22 @@ def reference_cuda(cfg, seed, dev, steps=2):
         r = ext.gaussian_voxelizer_backward(gD, gF, m, o, ci, vs, vr, lb, ub, nv, off, ids, d, gf, f)
         return fs, r[4]
 
-    step()
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    sampler = ClockSampler(gpu_id_for(dev.index))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     st = [step() for _ in range(steps)]
     e1.record()
     torch.cuda.synchronize()
+    clocks = sampler.stop()
     ms = e0.elapsed_time(e1) / steps
-    return {"value": round(ms, 3), "unit": "ms", "steps": steps, "device": torch.cuda.get_device_name(dev),
+    return {"value": round(ms, 3), "unit": "ms", "steps": steps, "warmup": warmup,
+            "device": torch.cuda.get_device_name(dev),
             "fwd_sec": [round(a, 5) for a, _ in st], "bwd_sec": [round(b, 5) for _, b in st],
+            "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 3), "clocks": clocks,
             "source": "reference src/cuda_gaussian_voxelizer.cu built for sm_100a by oracle/build_ref.py"}
 
 
@@ -534,10 +580,14 @@ def run_reference(args, rank, world, dev):
     cfg = CONFIGS[args.config]
     threads = os.cpu_count() or 1
     vals = []
+    t_region = time.perf_counter()
     for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            t_region = time.perf_counter()
         r = cpu_baseline(cfg, args.seed, threads=threads, steps=1)
         if i >= args.warmup:
             vals.append(r["value"])
+    region_s = time.perf_counter() - t_region
     value = statistics.median(vals)
     cpu = dict(r)
     cpu["value"] = value
@@ -547,7 +597,11 @@ def run_reference(args, rank, world, dev):
             "config": {"workload": f"{args.config}: N={cfg['n']}, C={cfg['c']}, CPU x-slab sample",
                        "global_batch": 1},
             "cpu_baseline": cpu, "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0,
-                                         "d2h_bytes_per_step": 0}}
+                                         "d2h_bytes_per_step": 0},
+            "what_ran": {"samples_timed": args.steps, "samples_warmup": args.warmup,
+                         "sample": cpu["sample"], "timed_region_s": round(region_s, 2),
+                         "value_is": "median over the timed samples of the sample time scaled to the full grid"},
+            "cpu_baseline_cfg1": cpu_baseline_cfg1(args.seed)}
     if dev is not None and not args.no_reference_cuda:
         try:
             line["reference_cuda"] = reference_cuda(cfg, args.seed, dev)
@@ -760,6 +814,112 @@ def run_batched(args, rank, world, dev):
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches), "clocks": clocks,
     }
+
+
+def _timed_steps(fn, args, world, dev):
+    """W untimed steps, then K steps between CUDA events on the current stream; max over ranks (ms/step)."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    return t
+
+
+def extra_batch8_cfg4(args, rank, world, dev, total=8):
+    """The batched-scenes config (cfg4: B=8 scenes of 18k x 1024-D over the range widened by 10%): the 8
+    scenes are dealt to the ranks (scene b to rank b % N), each rank splats its scenes in one batched call
+    and backpropagates; no collective inside the step.  ms per batch of 8 = max over ranks."""
+    import torch
+    from CudaGaussianVoxelizer import PyCudaGaussianVoxelizer, _C
+    cfg = CONFIGS["cfg4"]
+    mine = [b for b in range(total) if b % world == rank]
+    B = len(mine)
+    scenes = [make_inputs(cfg, seed=args.seed + 100 + b) for b in mine]
+    size, rng = scenes[0][0], scenes[0][1]
+    (X, Y, Z), _ = _C.grid_shape(size, rng)
+    n, c = cfg["n"], cfg["c"]
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    shape = (B, X, Y, Z) if B > 1 else (X, Y, Z)
+    gD = torch.randn(shape, device=dev, generator=g)
+    gF = torch.randn(shape + (c,), device=dev, generator=g)
+    leaves = [torch.cat([sc[2 + k] for sc in scenes]).to(dev).requires_grad_() for k in range(4)]
+    vox = PyCudaGaussianVoxelizer(voxel_size=size, voxel_range=rng, timing=False)
+    sizes = [n] * B
+
+    def step():
+        if B > 1:
+            density, grid_feats, _ = vox(*leaves, scene_sizes=sizes)
+        else:
+            density, grid_feats, _ = vox(*leaves)
+        return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
+
+    ms = _timed_steps(step, args, world, dev)
+    del leaves, gD, gF
+    torch.cuda.empty_cache()
+    return {"value": round(ms, 4), "unit": "ms per batch of 8 scenes", "scenes_per_rank": B, "n_gpus": world,
+            "workload": f"cfg4: {total} scenes, N={n} Gaussians each over the range widened by 10%, C={c}, "
+                        f"{X}x{Y}x{Z} voxels; scene b on rank b % N, one batched call per rank",
+            "scaling": "strong (the batch of 8 is fixed)", "collective_in_step": False}
+
+
+def extra_single_scene_cfg5(args, rank, world, dev):
+    """The spatially sharded config (cfg5: one scene of 100k Gaussians x 256-D on 400x400x32): x-slabs of
+    tiles over the ranks, replicated Gaussians, one NCCL all-reduce of the packed gradients per step
+    (CudaGaussianVoxelizer.distributed).  ms per step = max over ranks; the all-reduce's own time
+    (CUDA events around it on rank 0) is reported beside it."""
+    import torch
+    from CudaGaussianVoxelizer import _C
+    from CudaGaussianVoxelizer import distributed as dmod
+    cfg = CONFIGS["cfg5"]
+    size, rng, m_h, o_h, c_h, f_h = make_inputs(cfg, seed=args.seed)
+    (X, Y, Z), tiles = _C.grid_shape(size, rng)
+    vox = dmod.SlabGaussianVoxelizer(voxel_size=size, voxel_range=rng, rank=rank, world=world)
+    x0, x1 = vox.rows
+    g = torch.Generator(device=dev).manual_seed(1000)
+    gD = torch.randn((X, Y, Z), device=dev, generator=g)[x0:x1].contiguous()
+    gF = torch.empty((x1 - x0, Y, Z, cfg["c"]), device=dev).normal_(generator=g)
+    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
+
+    def step():
+        density, grid_feats, _ = vox(*leaves)
+        return torch.autograd.grad([density, grid_feats], leaves, [gD, gF])
+
+    ms = _timed_steps(step, args, world, dev)
+    ar_ms = None
+    if world > 1:
+        dmod.allreduce_events = []
+        try:
+            for _ in range(max(3, args.steps // 4)):
+                step()
+            torch.cuda.synchronize()
+            ar_ms = statistics.median(a.elapsed_time(b) for a, b in dmod.allreduce_events)
+        finally:
+            dmod.allreduce_events = None
+    packed_mb = cfg["n"] * (13 + cfg["c"]) * 4 / 1e6
+    del leaves, gD, gF
+    torch.cuda.empty_cache()
+    return {"value": round(ms, 4), "unit": "ms", "n_gpus": world, "scaling": "strong (one fixed scene)",
+            "workload": f"cfg5: N={cfg['n']} Gaussians, C={cfg['c']}, {X}x{Y}x{Z} voxels, var U(0.5,8); "
+                        f"{world} x-slabs of tiles (rank 0: tiles {vox.tile_range})",
+            "allreduce_ms": None if ar_ms is None else round(ar_ms, 4),
+            "allreduce_mb": round(packed_mb, 1) if world > 1 else 0.0,
+            "collective_in_step": "one NCCL all-reduce (sum) of the packed [N x (13 + C)] gradients" if world > 1
+            else "none (one rank)"}
 
 
 LOSS_METRIC = "feature cosine loss fwd+bwd ms/step over the voxel grid and % HBM roofline"
@@ -996,6 +1156,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-cuda", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the cfg4 batch-of-8 and cfg5 single-scene measurements of the default run")
     ap.add_argument("--forward-only", action="store_true", help="profiling mode: forward passes only")
     ap.add_argument("--path", default="voxelizer", choices=["voxelizer", "loss"],
                     help="voxelizer: the G2V fwd+bwd step (default); loss: the feature cosine loss fwd+bwd")
@@ -1033,11 +1195,25 @@ def main():
         print(json.dumps(run_forward_only(args, dev)), flush=True)
         return
     if world > 1:
+        # NCCL's initialisation log (communicator size, ranks, transports) goes to stderr, so the rank count
+        # of the run is on record without touching the one JSON line on stdout
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     try:
         run = (run_loss if args.path == "loss" else run_single_scene if args.single_scene else
                run_batched if args.scenes > 1 else run_ours)
         line = run(args, rank, world, dev)
+        default = run is run_ours and args.config == "cfg3" and not (args.density_only or args.graph or
+                                                                      args.cov_input != "cov")
+        if default and not args.no_extra:
+            # the multi-GPU configs of the workload, measured in the same run at the same N
+            line["batch8_cfg4"] = extra_batch8_cfg4(args, rank, world, dev)
+            line["single_scene_cfg5"] = extra_single_scene_cfg5(args, rank, world, dev)
+        if world > 1:
+            line["comm"] = {"backend": dist.get_backend(), "world_size": dist.get_world_size(),
+                            "nccl_version": ".".join(map(str, torch.cuda.nccl.version()))}
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

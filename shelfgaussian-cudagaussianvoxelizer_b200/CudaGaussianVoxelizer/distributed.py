@@ -57,12 +57,24 @@ def unpack_grads(buf: torch.Tensor, c: int):
             buf[:, 13:13 + c].contiguous().reshape(n, c))
 
 
+# Optional timing of the all-reduce: when `allreduce_events` is a list, allreduce_grads appends a pair of
+# CUDA events recorded on the current stream around each all-reduce (a benchmark reads the elapsed times).
+allreduce_events = None
+
+
 def allreduce_grads(grad_means, grad_cov, grad_opacity, grad_features, group=None):
     """Sum the slab-partial gradients of all ranks with one all-reduce of the packed buffer."""
     c = 0 if grad_features is None else int(grad_features.reshape(grad_means.shape[0], -1).shape[1])
     buf = pack_grads(grad_means, grad_cov, grad_opacity, grad_features)
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        ev = None
+        if allreduce_events is not None and buf.is_cuda:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+        if ev is not None:
+            ev[1].record()
+            allreduce_events.append(ev)
     return unpack_grads(buf, c)
 
 

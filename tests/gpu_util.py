@@ -24,6 +24,18 @@ def assert_close(name, got, ref, rtol=RTOL, atol=ATOL):
                            f"max abs diff {float(np.abs(got - ref).max()):.3e} (scale {scale:.3g})")
 
 
+def margin(got, ref, rtol=RTOL, atol=ATOL):
+    """Precision margin against the parity bar: (max elementwise |a - b| / bound, relative L2 / rtol).
+    Both must stay below 1 for assert_close to pass; 0.1 means a 10x margin."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    if ref.size == 0:
+        return 0.0, 0.0
+    scale = max(1.0, float(np.abs(ref).max()))
+    elem = float((np.abs(got - ref) / (atol * scale + rtol * np.abs(ref))).max())
+    return elem, oracle.rel_err(got, ref) / rtol
+
+
 def dev(*arrs, requires_grad=False):
     out = []
     for a in arrs:

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_close, dev, run_fwd_bwd
+from gpu_util import assert_close, dev, margin, run_fwd_bwd
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -98,15 +98,35 @@ def _random_case(n, c, size, rng, seed, n_out=0, var_max=2.5, expand=0.0):
     return m.numpy(), o.numpy(), cv.numpy(), (f.numpy() if f is not None else None)
 
 
-def _oracle_check(means, opacity, cov, feats, size, rng, seed, x_tiles=None, check_boxes=True):
-    """Full forward+backward on the GPU vs the float64 oracle (given the GPU's boxes)."""
+def _slab_upstream(dims, c, x_rows, seed):
+    """randn upstream gradients on the voxel rows x_rows, zeros elsewhere (the slab backward reads only its
+    own rows, so the rest need not be drawn)."""
+    X, Y, Z = dims
+    x0, x1 = x_rows
+    g = torch.Generator().manual_seed(seed + 7)
+    gD = np.zeros((X, Y, Z), np.float32)
+    gD[x0:x1] = torch.randn(x1 - x0, Y, Z, generator=g).numpy()
+    gF = None
+    if c > 0:
+        gF = np.zeros((X, Y, Z, c), np.float32)
+        gF[x0:x1] = torch.randn(x1 - x0, Y, Z, c, generator=g).numpy()
+    return gD, gF
+
+
+def _oracle_check(means, opacity, cov, feats, size, rng, seed, x_tiles=None, check_boxes=True, slab_upstream=False,
+                  margins=None):
+    """Full forward+backward on the GPU vs the float64 oracle (given the GPU's boxes).  `margins` (a dict)
+    receives each output's precision margin (gpu_util.margin)."""
     from CudaGaussianVoxelizer import _C
     dims, tiles = oracle.grid_shape(size, rng)
     X, Y, Z = dims
     c = 0 if feats is None else feats.shape[1]
-    g = torch.Generator().manual_seed(seed + 7)
-    gD = torch.randn(X, Y, Z, generator=g).numpy()
-    gF = torch.randn(X, Y, Z, c, generator=g).numpy() if c > 0 else None
+    if slab_upstream:
+        gD, gF = _slab_upstream(dims, c, (x_tiles[0] * 4, min(x_tiles[1] * 4, X)), seed)
+    else:
+        g = torch.Generator().manual_seed(seed + 7)
+        gD = torch.randn(X, Y, Z, generator=g).numpy()
+        gF = torch.randn(X, Y, Z, c, generator=g).numpy() if c > 0 else None
     mt, ot, ct, ft = dev(means, opacity, cov, feats)
     out = _C.gaussian_voxelizer_forward(mt, ot, ct, list(size), list(rng), ft)
     density, cov_inv, lb, ub, nvox, grid_feats, off, ids, _ = out
@@ -123,21 +143,34 @@ def _oracle_check(means, opacity, cov, feats, size, rng, seed, x_tiles=None, che
         xr = (x_tiles[0] * 4, min(x_tiles[1] * 4, X))
     dref, fref = oracle.forward(means, opacity, cov, feats, lb_h, ub_h, size, rng, dims, x_range=xr)
     sl = slice(None) if xr is None else slice(xr[0], xr[1])
-    assert_close("density", density.cpu().numpy()[sl], dref[sl])
+    checks = [("density", density[sl].cpu().numpy(), dref[sl])]
     if c > 0:
-        assert_close("grid_feats", grid_feats.cpu().numpy()[sl], fref[sl])
+        checks.append(("grid_feats", grid_feats[sl].cpu().numpy(), fref[sl]))
+    for name, a, b in checks:
+        if margins is not None:
+            margins[name] = margin(a, b)
+        assert_close(name, a, b)
     gDt = torch.from_numpy(gD).cuda()
     gFt = torch.from_numpy(gF).cuda() if c > 0 else torch.empty(0, device="cuda")
     gm, gc, go, gfe, _ = _C.gaussian_voxelizer_backward(gDt, gFt, mt, ot, cov_inv, list(size), list(rng), lb, ub,
                                                         nvox, off, ids, density, grid_feats, ft, tile_x_range=tr)
     rm, rc, ro, rf = oracle.backward(means, opacity, cov, feats, lb_h, ub_h, size, rng, dims, gD, gF, dref, fref,
                                      x_range=xr)
-    assert_close("grad_means", gm.cpu().numpy(), rm)
-    assert_close("grad_cov", gc.cpu().numpy(), rc)
-    assert_close("grad_opacity", go.cpu().numpy(), ro)
+    checks = [("grad_means", gm.cpu().numpy(), rm), ("grad_cov", gc.cpu().numpy(), rc),
+              ("grad_opacity", go.cpu().numpy(), ro)]
     if c > 0:
-        assert_close("grad_features", gfe.cpu().numpy(), rf)
+        checks.append(("grad_features", gfe.cpu().numpy(), rf))
+    for name, a, b in checks:
+        if margins is not None:
+            margins[name] = margin(a, b)
+        assert_close(name, a, b)
     return out
+
+
+def _print_margins(label, margins):
+    print(f"\nprecision margin {label} (max |err| / elementwise bound, rel L2 / 1e-4):")
+    for k, (e, r) in margins.items():
+        print(f"  {k:14s} {e:.3e}  {r:.3e}")
 
 
 def test_reference_backward_case():
@@ -172,7 +205,20 @@ def test_cfg3_shape_slab_against_oracle():
     against the oracle restricted to the same voxels (size-independent property: the slab's values)."""
     size, rng = [0.4] * 3, [-40.0, -40.0, -1.0, 40.0, 40.0, 5.4]
     args = _random_case(18000, 1024, size, rng, seed=0)
-    _oracle_check(*args, size, rng, seed=0, x_tiles=(10, 12))
+    margins = {}
+    _oracle_check(*args, size, rng, seed=0, x_tiles=(10, 12), margins=margins)
+    _print_margins("cfg3 slab", margins)
+
+
+def test_cfg5_shape_slab_against_oracle():
+    """Single-scene config (N=100000, C=256, 0.2 m voxels -> 400x400x32, covariance eigenvalues U(0.5, 8)):
+    ~2400 Gaussians per tile, so nearly every unit runs several slot passes and its e_v from grid_feats.
+    Forward + backward on a 2-tile x-slab against the oracle restricted to the same voxels."""
+    size, rng = [0.2] * 3, [-40.0, -40.0, -1.0, 40.0, 40.0, 5.4]
+    args = _random_case(100000, 256, size, rng, seed=0, var_max=8.0)
+    margins = {}
+    _oracle_check(*args, size, rng, seed=0, x_tiles=(50, 52), slab_upstream=True, margins=margins)
+    _print_margins("cfg5 slab", margins)
 
 
 def test_features_with_zero_channels_zero_density():
