@@ -51,9 +51,8 @@ constexpr int kMaxBlockTiles = 16;              // tiles per block (2 x 2 x 4)
 // N of a pass = its slot count rounded up to 16 (a pass that is not full issues narrower MMAs)
 
 struct FMisc {
-    uint64_t full_a[kStages];
-    uint64_t full_w[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kStages];   // 8 converter-warp + 8 weight-warp arrivals: both operands of the stage written
+    uint64_t empty[kStages];  // MMA commit: the stage has been read
     uint64_t mma_done;
     uint32_t tmem_base;
     int fail;
@@ -122,8 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
-            tc::mbar_init(&ms.full_a[i], 8);
-            tc::mbar_init(&ms.full_w[i], 8);
+            tc::mbar_init(&ms.full[i], 16);
             tc::mbar_init(&ms.empty[i], 1);
         }
         tc::mbar_init(&ms.mma_done, 1);
@@ -160,7 +158,13 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     for (int pass = 0; pass < npass; ++pass) {
         const int p0 = pass * kSlots, ns = min(kSlots, Kb - p0);
         const int nn = (ns + 15) & ~15;  // MMA N of this pass
-        const uint32_t idesc = tc::idesc_bf16_f32(128, nn, /*A MN-major*/ 1, /*B K-major*/ 0);
+        // A pass of at most 128 slots runs transposed: the slots' weights are the A operand (M = 128, K-major)
+        // and the converted gradient the B operand (N = 256 channels, MN-major), so a step issues three
+        // MMAs of N = 256 instead of six narrow ones; the accumulator then holds slots in lanes, channels
+        // in columns.
+        const bool tr = ns <= 128;
+        const uint32_t idesc = tr ? tc::idesc_bf16_f32(128, 256, /*A K-major*/ 0, /*B MN-major*/ 1)
+                                  : tc::idesc_bf16_f32(128, nn, /*A MN-major*/ 1, /*B K-major*/ 0);
         if (warp < 8) {
             // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 2 voxel rows) ----------
             const int jc = lane;                                     // channels c0 + 8 jc .. + 7
@@ -197,19 +201,21 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                         }
                     }
                     uint4 h, l;
-                    tc::split_bf16x2(f[0], f[1], h.x, l.x);
-                    tc::split_bf16x2(f[2], f[3], h.y, l.y);
-                    tc::split_bf16x2(f[4], f[5], h.z, l.z);
-                    tc::split_bf16x2(f[6], f[7], h.w, l.w);
+                    tc::split_bf16x2_p(make_float2(f[0], f[1]), h.x, l.x);
+                    tc::split_bf16x2_p(make_float2(f[2], f[3]), h.y, l.y);
+                    tc::split_bf16x2_p(make_float2(f[4], f[5]), h.z, l.z);
+                    tc::split_bf16x2_p(make_float2(f[6], f[7]), h.w, l.w);
                     const int g8 = r >> 3, rr = r & 7;
-                    const int off = mb * 4096 + a * 1024 + g8 * 2048 + rr * 128 + ((jj ^ rr) << 4);
+                    // channel atom n = 2 mb + a at n KB, voxel octet g8 at 4 g8 KB: uniform strides, so the
+                    // stage is both the A operand (two M-blocks of 128 channels) and a B operand of N = 256
+                    const int off = mb * 2048 + a * 1024 + g8 * 4096 + rr * 128 + ((jj ^ rr) << 4);
                     *reinterpret_cast<uint4*>(a_stage(st, 0) + off) = h;
                     *reinterpret_cast<uint4*>(a_stage(st, 1) + off) = l;
                 }
                 tc::fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tc::mbar_arrive(&ms.full_a[st]);
+                    tc::mbar_arrive(&ms.full[st]);
                     if (kTma) tc::mbar_arrive(&ms.gempty[gs]);
                 }
             }
@@ -238,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             // (ly, lz), the x mask decides the whole slice.  Voxel centres are linear within a tile (a tile
             // never spans two stacked scenes).
             const int t = tid - 256;
-            const bool trow = t < nn;  // rows >= N are not read by the MMAs
+            const bool trow = t < (tr ? 128 : nn);  // rows the MMAs read (zero beyond the pass's slots)
             const bool slot = t < ns;
             if (pass == 0) {
                 // log2(1 / max(D, eps)) of every voxel of the block's tiles (tile order of the steps); only
@@ -265,7 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             const float hx = G.h[0], hy = G.h[1], hz = G.h[2];
             float opa = 0.0f, A0 = 0.0f, Bx = 0.0f, By = 0.0f, Bz = 0.0f;
             float Qxx = 0.0f, Qyy = 0.0f, Qzz = 0.0f, Qxy = 0.0f, Qxz = 0.0f, Qyz = 0.0f;
-            float my[4], mz[4];
+            float my[4];
+            float2 Zq01 = make_float2(0.f, 0.f), Zq23 = make_float2(0.f, 0.f);  // Qzz lz^2 + z box mask
             int xlo = 1, xhi = 0;
             for (int j = 0; j < nsteps && ok; ++j, ++it) {
                 const int st = it % kStages;
@@ -298,56 +305,63 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     xhi = __float_as_int(e4.x) - o.x;
                     const int ylo = __float_as_int(d.z) - o.y, yhi = __float_as_int(e4.y) - o.y;
                     const int zlo = __float_as_int(d.w) - o.z, zhi = __float_as_int(e4.z) - o.z;
+                    float mz[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         my[i] = (i >= ylo && i <= yhi) ? 0.0f : -INFINITY;
-                        mz[i] = (i >= zlo && i <= zhi) ? 0.0f : -INFINITY;
+                        mz[i] = (i >= zlo && i <= zhi) ? Qzz * (float)(i * i) : -INFINITY;
                     }
+                    Zq01 = make_float2(mz[0], mz[1]);
+                    Zq23 = make_float2(mz[2], mz[3]);
                 }
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                 if (!ok) break;
                 if (trow) {
-                float w[16];
+                    // pairs of z-consecutive voxels (lz = 0,1 and 2,3) in packed f32x2 arithmetic:
+                    //   m = (Ay + Qzz lz^2 + z mask) + lz Bz2 + log2(1 / den_v),  w = o 2^m
+                    float2 w[8];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) w[e] = 0.0f;
-                if (slot && ks >= xlo && ks <= xhi) {
-                    const float fk = (float)ks;
-                    const float Ak = fmaf(fmaf(Qxx, fk, Bx), fk, A0);
-                    const float Byk = fmaf(Qxy, fk, By), Bzk = fmaf(Qxz, fk, Bz);
-                    const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[(j >> 2) * kVoxPerTile + ks * 16]);
+                    for (int e = 0; e < 8; ++e) w[e] = make_float2(0.0f, 0.0f);
+                    if (slot && ks >= xlo && ks <= xhi) {
+                        const float fk = (float)ks;
+                        const float Ak = fmaf(fmaf(Qxx, fk, Bx), fk, A0);
+                        const float Byk = fmaf(Qxy, fk, By), Bzk = fmaf(Qxz, fk, Bz);
+                        const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[(j >> 2) * kVoxPerTile + ks * 16]);
+                        const float2 o2 = make_float2(opa, opa);
 #pragma unroll
-                    for (int ly = 0; ly < 4; ++ly) {
-                        const float4 L = L4[ly];  // log2(1 / den) of the 4 voxels (ly, 0..3); -inf outside the grid
-                        const float Ay = fmaf(fmaf(Qyy, (float)ly, Byk), (float)ly, Ak) + my[ly];
-                        const float Bz2 = fmaf(Qyz, (float)ly, Bzk);
-                        const float Lz[4] = {L.x + mz[0], L.y + mz[1], L.z + mz[2], L.w + mz[3]};
-#pragma unroll
-                        for (int lz = 0; lz < 4; ++lz) {
-                            const float m = fmaf(fmaf(Qzz, (float)lz, Bz2), (float)lz, Ay) + Lz[lz];
-                            w[ly * 4 + lz] = opa * tc::exp2_approx(m);
+                        for (int ly = 0; ly < 4; ++ly) {
+                            const float4 L = L4[ly];  // log2(1 / den) of the voxels (ly, 0..3); -inf outside the grid
+                            const float Ay = fmaf(fmaf(Qyy, (float)ly, Byk), (float)ly, Ak) + my[ly];
+                            const float Bz2 = fmaf(Qyz, (float)ly, Bzk);
+                            const float2 A2 = make_float2(Ay, Ay), B2 = make_float2(Bz2, Bz2);
+                            const float2 m01 = __fadd2_rn(__ffma2_rn(make_float2(0.0f, 1.0f), B2, __fadd2_rn(A2, Zq01)),
+                                                          make_float2(L.x, L.y));
+                            const float2 m23 = __fadd2_rn(__ffma2_rn(make_float2(2.0f, 3.0f), B2, __fadd2_rn(A2, Zq23)),
+                                                          make_float2(L.z, L.w));
+                            w[2 * ly] = __fmul2_rn(make_float2(tc::exp2_approx(m01.x), tc::exp2_approx(m01.y)), o2);
+                            w[2 * ly + 1] = __fmul2_rn(make_float2(tc::exp2_approx(m23.x), tc::exp2_approx(m23.y)), o2);
                         }
                     }
-                }
-                uint4 h0, h1, l0, l1;
-                tc::split_bf16x2(w[0], w[1], h0.x, l0.x);
-                tc::split_bf16x2(w[2], w[3], h0.y, l0.y);
-                tc::split_bf16x2(w[4], w[5], h0.z, l0.z);
-                tc::split_bf16x2(w[6], w[7], h0.w, l0.w);
-                tc::split_bf16x2(w[8], w[9], h1.x, l1.x);
-                tc::split_bf16x2(w[10], w[11], h1.y, l1.y);
-                tc::split_bf16x2(w[12], w[13], h1.z, l1.z);
-                tc::split_bf16x2(w[14], w[15], h1.w, l1.w);
-                // K-major, 32-byte swizzle: row t = the slot's 16 voxels (32 bytes), chunk c at c ^ ((t / 4) % 2)
-                const int sw = (t >> 2) & 1;
-                const int off0 = (t >> 3) * 256 + (t & 7) * 32 + (sw << 4), off1 = off0 ^ 16;
-                *reinterpret_cast<uint4*>(b_stage(st, 0) + off0) = h0;
-                *reinterpret_cast<uint4*>(b_stage(st, 0) + off1) = h1;
-                *reinterpret_cast<uint4*>(b_stage(st, 1) + off0) = l0;
-                *reinterpret_cast<uint4*>(b_stage(st, 1) + off1) = l1;
+                    uint4 h0, h1, l0, l1;
+                    tc::split_bf16x2_p(w[0], h0.x, l0.x);
+                    tc::split_bf16x2_p(w[1], h0.y, l0.y);
+                    tc::split_bf16x2_p(w[2], h0.z, l0.z);
+                    tc::split_bf16x2_p(w[3], h0.w, l0.w);
+                    tc::split_bf16x2_p(w[4], h1.x, l1.x);
+                    tc::split_bf16x2_p(w[5], h1.y, l1.y);
+                    tc::split_bf16x2_p(w[6], h1.z, l1.z);
+                    tc::split_bf16x2_p(w[7], h1.w, l1.w);
+                    // K-major, 32-byte swizzle: row t = the slot's 16 voxels (32 bytes), chunk c at c ^ ((t / 4) % 2)
+                    const int sw = (t >> 2) & 1;
+                    const int off0 = (t >> 3) * 256 + (t & 7) * 32 + (sw << 4), off1 = off0 ^ 16;
+                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off0) = h0;
+                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off1) = h1;
+                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off0) = l0;
+                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off1) = l1;
                 }
                 tc::fence_async_smem();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&ms.full_w[st]);
+                if (lane == 0) tc::mbar_arrive(&ms.full[st]);
             }
         } else if (kTma && warp == 17 && lane == 0) {
             // ---------------- TMA thread: the step's gradient rows into the staging ring ----------------
@@ -363,28 +377,42 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             }
         } else if (warp == 16 && lane == 0) {
             // ---------------- MMA thread ----------------
-            const uint64_t adesc0 = tc::smem_desc(tc::smem_u32(a_stage(0, 0)), 1024, 2048, tc::kLayoutSw128);
+            // Every stage's descriptors are formed once and kept in registers: the step loop is unrolled by
+            // the stage count (a pass has 4 x-slices per tile, so its steps come in whole rounds of the ring
+            // and stage s of a round is step j0 + s), and each step is one wait and one block of six MMAs
+            // plus the commit that frees the stage.
+            static_assert(kStages == 4 && kMB == 2, "the MMA loop is unrolled for four stages of two M-blocks");
+            const uint64_t adesc0 = tc::smem_desc(tc::smem_u32(a_stage(0, 0)), 1024, 4096, tc::kLayoutSw128);
             const uint64_t bdesc0 = tc::smem_desc(tc::smem_u32(b_stage(0, 0)), 16, 256, tc::kLayoutSw32);
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
-                const int st = it % kStages;
-                const uint32_t par = (it / kStages) & 1;
-                ok = tc::mbar_wait(&ms.full_a[st], par, err) && tc::mbar_wait(&ms.full_w[st], par, err);
-                if (!ok) break;
-                tc::tc_fence_after();
-                // descriptors of the stage from the stage-0 ones (the start-address field counts 16-byte units)
+            uint64_t dah[kStages][kMB], dal[kStages][kMB], dbh[kStages], dbl[kStages];
+#pragma unroll
+            for (int st = 0; st < kStages; ++st) {
+                // the start-address field counts 16-byte units
                 const uint64_t soff = (uint64_t)((st * kStageBytes) >> 4);
-                const uint64_t bh = bdesc0 + soff, blo = bh + (uint64_t)(kBHalf >> 4);
+                dbh[st] = bdesc0 + soff;
+                dbl[st] = dbh[st] + (uint64_t)(kBHalf >> 4);
 #pragma unroll
                 for (int mb = 0; mb < kMB; ++mb) {
-                    const uint64_t ah = adesc0 + soff + (uint64_t)((mb * 4096) >> 4);
-                    const uint64_t al = ah + (uint64_t)(kAHalf >> 4);
-                    const uint32_t dcol = tmem + mb * kSlots;
-                    tc::mma_f16_ss(dcol, ah, bh, idesc, j > 0);
-                    tc::mma_f16_ss(dcol, ah, blo, idesc, true);
-                    tc::mma_f16_ss(dcol, al, bh, idesc, true);
+                    dah[st][mb] = adesc0 + soff + (uint64_t)((mb * 2048) >> 4);
+                    dal[st][mb] = dah[st][mb] + (uint64_t)(kAHalf >> 4);
                 }
-                tc::mma_commit(tc::smem_u32(&ms.empty[st]));
             }
+            for (int j0 = 0; j0 < nsteps && ok; j0 += kStages) {
+                const uint32_t par = (uint32_t)((it + j0) / kStages) & 1;
+#pragma unroll
+                for (int st = 0; st < kStages; ++st) {
+                    ok = ok && tc::mbar_wait(&ms.full[st], par, err);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    if (tr)
+                        tc::mma_step1x3_commit(tmem, dbh[st], dbl[st], dah[st][0], dal[st][0], idesc, (j0 + st) > 0,
+                                               tc::smem_u32(&ms.empty[st]));
+                    else
+                        tc::mma_step2x3_commit(tmem, tmem + kSlots, dah[st][0], dal[st][0], dah[st][1], dal[st][1],
+                                               dbh[st], dbl[st], idesc, (j0 + st) > 0, tc::smem_u32(&ms.empty[st]));
+                }
+            }
+            it += nsteps;
             tc::mma_commit(tc::smem_u32(&ms.mma_done));
         } else {
             it += nsteps;
@@ -397,7 +425,33 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         tc::tc_fence_after();
         // epilogue: warp w < 16 reads lanes 32*(w%4).. (channels) of M-block (w/4)%2, slot columns
         // 128*(w/8) .. +127; the next 16 columns load from TMEM while the current ones are stored
-        if (warp < 16 && !ms.fail) {
+        if (warp < 16 && !ms.fail && tr) {
+            // transposed pass: warp w reads lanes 32*(w%4).. (slots) and the 64 channel columns of (w/4);
+            // a thread stores 16 consecutive channels of its slot's partial row per TMEM load
+            const int q = warp & 3, cb = warp >> 2;
+            const int sl = q * 32 + lane;
+            const int64_t ro = sl < ns ? ms.rowoff[sl] : -1;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + cb * 64;
+#pragma unroll 1
+            for (int jc = 0; jc < 4; ++jc) {
+                const int cc = c0 + cb * 64 + jc * 16;
+                if (cc >= C) break;  // warp-uniform
+                float v[16];
+                tc::tmem_ld16(tbase + jc * 16, v);
+                if (ro >= 0) {
+                    float* dst = partialF + ro * C + cc;
+                    if (vec && cc + 16 <= C) {
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4)
+                            *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            if (cc + e < C) dst[e] = v[e];
+                    }
+                }
+            }
+        } else if (warp < 16 && !ms.fail) {
             const int q = warp & 3, mb = (warp >> 2) & 1, half = warp >> 3;
             const int c = c0 + mb * 128 + q * 32 + lane;
             const int jc0 = half * 8, jc1 = min(half * 8 + 8, (ns + 15) >> 4);  // warp-uniform

@@ -68,6 +68,46 @@ __device__ __forceinline__ void mma_commit(uint32_t mbar_saddr) {
                  : "memory");
 }
 
+// One pipeline step of a split-operand contraction over two accumulators: for m = 0, 1
+//     D_m (+)= Ah_m * Bh + Ah_m * Bl + Al_m * Bh
+// (six MMAs, the first of each accumulator overwriting it when `accumulate` is false), then a commit
+// that arrives on `mbar` once they have completed.  One asm block, so the issuing thread spends no
+// instructions between the MMAs.
+__device__ __forceinline__ void mma_step2x3_commit(uint32_t d0, uint32_t d1, uint64_t ah0, uint64_t al0, uint64_t ah1,
+                                                   uint64_t al1, uint64_t bh, uint64_t bl, uint32_t idesc,
+                                                   bool accumulate, uint32_t mbar) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t"
+        "setp.ne.b32 p, %9, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %8, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %7, %8, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %6, %8, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %4, %6, %8, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %4, %7, %8, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %5, %6, %8, t;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%10];\n\t}\n" ::"r"(d0),
+        "r"(d1), "l"(ah0), "l"(al0), "l"(ah1), "l"(al1), "l"(bh), "l"(bl), "r"(idesc), "r"((uint32_t)accumulate),
+        "r"(mbar)
+        : "memory");
+}
+
+// One pipeline step over one accumulator: D (+)= Ah * Bh + Ah * Bl + Al * Bh, then the commit that
+// arrives on `mbar` once the three MMAs have completed (one asm block, like mma_step2x3_commit).
+__device__ __forceinline__ void mma_step1x3_commit(uint32_t d, uint64_t ah, uint64_t al, uint64_t bh, uint64_t bl,
+                                                   uint32_t idesc, bool accumulate, uint32_t mbar) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %3, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %4, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %3, %5, t;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}\n" ::"r"(d),
+        "l"(ah), "l"(al), "l"(bh), "l"(bl), "r"(idesc), "r"((uint32_t)accumulate), "r"(mbar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -144,12 +184,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_saddr, uint32_t parit
     return done != 0;
 }
 
+// Non-blocking test of the phase: true when it has already completed.  A phase that is complete by the
+// time a consumer reaches it is the common case of a deep ring; the test avoids try_wait's suspend path.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_saddr, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar_saddr), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Wait until the phase with the given parity has completed.  Bounded: after kWaitLimitNs of waiting it
 // records kErrWaitTimeout in *err and returns false instead of waiting forever; once any wait of any CTA
 // has given up (*err != 0), later waits that do not complete at once return false, so that the whole
 // grid drains quickly.  The error word (global memory) is read only on that slow path.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     const uint32_t a = smem_u32(bar);
+    if (mbar_test_wait(a, parity)) return true;
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
@@ -207,6 +262,15 @@ __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, u
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
     const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(x1 - h1), "f"(x0 - h0));
+}
+
+// split_bf16x2 of a float pair with the remainder formed by one packed f32x2 operation (sm_100):
+// x.x goes to the low half of each word.
+__device__ __forceinline__ void split_bf16x2_p(float2 x, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x.y), "f"(x.x));
+    const float2 h = make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
+    const float2 r = __ffma2_rn(h, make_float2(-1.0f, -1.0f), x);  // x - h, exact
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r.y), "f"(r.x));
 }
 
 // Two floats -> packed f16x2 hi / lo words (x0 in the low half) with x ~= hi + lo as in split_half.
