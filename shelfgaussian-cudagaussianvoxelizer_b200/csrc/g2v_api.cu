@@ -59,7 +59,7 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
                     int nbx, int nby, int nbz, const int B[3], int tx_begin, int tx_end, const Grid& G, float* partialF,
                     int64_t block_pair_cap, int* err, cudaStream_t s);
 size_t spass_tc_split_bytes(int64_t n, int64_t C);
-void spass_tc_unit_shape(const Grid& G, int cell[3], int ncells[3]);
+void tc_unit_shape(const Grid& G, int cell[3], int ncells[3]);
 int launch_spass_tc(const float* grad_density, const float* grad_feats, const float* features, int64_t n, int C,
                     const float* density, const GParams* gparams, const int32_t* g2t_offsets,
                     const int32_t* unit_offsets, const int32_t* unit_lists, int tile_x_begin, int tile_x_end,
@@ -448,7 +448,7 @@ int g2v_forward_splat_workspace_size(int64_t num_gaussians, int64_t num_pairs, c
     Carver c(nullptr);
     T2GWs w, wu;
     carve_t2g(c, ntiles, num_pairs, w);
-    carve_t2g(c, ntiles, num_pairs, wu);  // the tensor-core path's unit lists (z pairs of tiles)
+    carve_t2g(c, ntiles, num_pairs, wu);  // the tensor-core path's unit lists (z quads of tiles)
     c.take<char>(splat_tc_split_bytes(num_gaussians, channels));
     *bytes = c.bytes();
     return G2V_SUCCESS;
@@ -489,7 +489,7 @@ static int forward_splat_impl(const float* means3d, const float* opacity, const 
     const int one[3] = {1, 1, 1};
     const bool tcore = features != nullptr && C > 0 && use_tensor_cores();
     // the reference's G2T tile ids; the per-tile Gaussian lists only for the FP32-FMA splat (the
-    // tensor-core splat lists z pairs of tiles; g2v_build_t2g builds the per-tile map on request)
+    // tensor-core splat lists z quads of tiles; g2v_build_t2g builds the per-tile map on request)
     if (tcore) {
         if ((rc = fill_g2t(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, g2t_offsets, g2t_tile_ids, num_pairs, s)))
             return rc;
@@ -501,9 +501,9 @@ static int forward_splat_impl(const float* means3d, const float* opacity, const 
     const int first_tile = tile_x_begin * G.tiles[1] * G.tiles[2];
     const int nt = (tile_x_end - tile_x_begin) * G.tiles[1] * G.tiles[2];
     if (tcore) {
-        // unit lists: z pairs of tiles, Gaussian ids ascending (at most M entries over fewer cells)
+        // unit lists: z quads of tiles, Gaussian ids ascending (at most M entries over fewer cells)
         int cell[3], ncells[3];
-        spass_tc_unit_shape(G, cell, ncells);
+        tc_unit_shape(G, cell, ncells);
         if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, cell, ncells, tile_x_begin,
                                    tile_x_end, g2t_offsets, nullptr, 0, nullptr, wu.counts, wu.tile_offsets,
                                    wu.unsorted, wu.lists, wu.scan, wu.total, s, num_pairs, err)))
@@ -571,7 +571,7 @@ int g2v_forward_splat_unit_lists(const void* splat_workspace, int64_t num_gaussi
         G.tiles[a] = (dims[a] + 3) / 4;
     }
     int cell[3], ncells[3];
-    spass_tc_unit_shape(G, cell, ncells);
+    tc_unit_shape(G, cell, ncells);
     const int64_t nu = (int64_t)ncells[0] * ncells[1] * ncells[2];
     *num_units = nu;
     if (!unit_offsets) return G2V_SUCCESS;  // size query
@@ -920,9 +920,9 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool tcore = C > 0 && num_gaussians > 0 && use_tensor_cores();
     // Tile->Gaussian lists for the FP32-FMA tile pass, or the lists of the tensor-core pass's units
-    // (z pairs of tiles); both fit the tile-sized buffers (fewer cells, at most M entries)
+    // (z quads of tiles); both fit the tile-sized buffers (fewer cells, at most M entries)
     int cell[3] = {1, 1, 1}, ncells[3] = {G.tiles[0], G.tiles[1], G.tiles[2]};
-    if (tcore) spass_tc_unit_shape(G, cell, ncells);
+    if (tcore) tc_unit_shape(G, cell, ncells);
     int* err = nullptr;
     if ((rc = device_error_ptr(&err))) return rc;
     // the tile pass's unit lists: given by the caller (the forward splat built the same ones) or built here

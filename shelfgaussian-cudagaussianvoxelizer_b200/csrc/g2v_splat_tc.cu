@@ -194,6 +194,14 @@ __device__ __forceinline__ UnitGeom unit_geom(int u, int ty_n, int tzp_n, int tx
     return g;
 }
 
+// The unit lists are those of z quads of tiles (tc_unit_shape, shared with the backward's tile pass):
+// z pair u of the slab reads the list of its quad; the quad's Gaussians that miss the pair weigh zero
+// there through the box test of the weight evaluation.
+__device__ __forceinline__ int list_unit(int u, int tzp_n) {
+    const int row = u / tzp_n;
+    return row * ((tzp_n + 1) / 2) + (u - row * tzp_n) / 2;
+}
+
 // Named barrier of the 8 epilogue warps.
 __device__ __forceinline__ void epi_barrier() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
@@ -251,7 +259,8 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
         const uint64_t pol = tc::l2_policy_evict_last();
         int it = 0;
         for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-            const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            const int lu = list_unit(u, tzp_n);
+            const int s0 = unit_offsets[lu], K = unit_offsets[lu + 1] - s0;
             if (K == 0) continue;
             const int32_t* list = unit_lists + s0;
             const int nsteps = (K + kKStep - 1) / kKStep;
@@ -308,7 +317,8 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
         // `ok` says (a wait that gave up only skips work), so a failed wait cannot split the barrier.
         int it = 0, nu = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-            const int s0 = unit_offsets[u], K = unit_offsets[u + 1] - s0;
+            const int lu = list_unit(u, tzp_n);
+            const int s0 = unit_offsets[lu], K = unit_offsets[lu + 1] - s0;
             if (K == 0) continue;
             const int32_t* list = unit_lists + s0;
             const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
@@ -434,7 +444,8 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
             const uint64_t adesc0 = tc::smem_desc(a_stage(0, 0), 1024, 2048, tc::kLayoutSw128);
             const uint64_t bdesc0 = tc::smem_desc(b_stage(0, 0), 1024, 2048, tc::kLayoutSw128);
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-                const int K = unit_offsets[u + 1] - unit_offsets[u];
+                const int lu = list_unit(u, tzp_n);
+                const int K = unit_offsets[lu + 1] - unit_offsets[lu];
                 if (K == 0) continue;
                 const int nsteps = (K + kKStep - 1) / kKStep;
                 for (int cg = 0; cg < ngroups && ok; ++cg, ++job) {
@@ -477,7 +488,8 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
         const uint64_t opol = tc::l2_policy_evict_first();  // grid_feats is written once
         int job = 0, nu = 0, ochunk = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-            const int K = unit_offsets[u + 1] - unit_offsets[u];
+            const int lu = list_unit(u, tzp_n);
+            const int K = unit_offsets[lu + 1] - unit_offsets[lu];
             const UnitGeom ug = unit_geom(u, G.tiles[1], tzp_n, tx_begin);
             const int x0 = ug.tx * kTile, y0 = ug.ty * kTile, z0 = ug.tzp * 8;
             const int nx = min(kTile, G.dims[0] - x0), ny = min(kTile, G.dims[1] - y0), nz = min(8, G.dims[2] - z0);
@@ -631,7 +643,8 @@ int launch_splat_kernel(bool tma, const CUtensorMap& omap, const __half* hi, con
 }  // namespace
 
 // Splits the features (per-channel power-of-two scale) into `split` (splat_tc_split_bytes) and runs the
-// tensor-core splat over the units (z pairs of tiles) of the slab [tile_x_begin, tile_x_end).
+// tensor-core splat over the units (z pairs of tiles) of the slab [tile_x_begin, tile_x_end), whose
+// Gaussians come from the z-quad unit lists (unit_offsets / unit_lists, tc_unit_shape cells).
 int launch_splat_tc(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
                     const int32_t* ub, const float* features, int64_t n, int C, const int32_t* unit_offsets,
                     const int32_t* unit_lists, int tile_x_begin, int tile_x_end, const Grid& G, float* density,

@@ -405,3 +405,111 @@ struct __align__(16) GParams {
 int launch_pack_params(const float* means, const float* opacity, const float* cov_inv, const int32_t* lb,
                        const int32_t* ub, int64_t n, GParams* out, cudaStream_t s);
 }  // namespace g2v
+
+namespace g2v {
+namespace tc {
+// ---------------------------------------------------------------------------------------------
+// CTA pairs (a cluster of two CTAs sharing one tcgen05 MMA, cta_group::2).  The even CTA of the pair
+// (rank 0, the leader) issues the MMAs; the A operand's M rows and the B operand's N rows are split
+// between the two CTAs' shared memory at the same offsets, and each CTA's TMEM holds the accumulator
+// rows of its own A rows over all N columns.  Producers of the other CTA reach the leader's mbarriers
+// through shared::cluster addresses; the leader's commits arrive on the same barrier offset in both
+// CTAs.  Every load of the pair is a plain per-CTA load (no multicast).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the variable at shared::cta address `saddr` in the cluster's CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+// Arrive (release at cluster scope) on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Relaxed arrive on another CTA's mbarrier: no release fence.  For hand-offs whose data is already in
+// place and visible within its own CTA when the arrive is issued (the arriving thread acquired it), where
+// a cluster-scope release costs ~1600 cycles per arrive.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// try_wait with acquire at cluster scope: for phases completed by arrivals or transfers of the other CTA.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_saddr, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar_saddr), "r"(parity), "r"(kWaitHintNs)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait like mbar_wait, with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_cluster(a, parity)) return true;
+        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+        if (global_ns() - t0 > kWaitLimitNs) break;
+    }
+    atomicOr(err, kErrWaitTimeout);
+    return false;
+}
+// 4-byte store into the other CTA's shared memory whose completion counts 4 bytes on that CTA's mbarrier
+// (both given as shared::cluster addresses).
+__device__ __forceinline__ void st_async_f32(uint32_t cluster_addr, float v, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(cluster_addr),
+                 "r"(__float_as_uint(v)), "r"(cluster_bar)
+                 : "memory");
+}
+// TMEM allocation for a CTA pair: one warp of each CTA (same warp index, same destination offset).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A * B over the pair (M = 256: rows 0-127 from the leader's A, 128-255 from the other
+// CTA's; B's N rows: the first N/2 from the leader, the rest from the other CTA); one leader thread.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+// Arrive on the mbarrier at shared::cta offset `mbar_saddr` in every CTA of `cta_mask` once all prior
+// pair MMAs of this thread have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t mbar_saddr, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            mbar_saddr),
+        "h"(cta_mask)
+        : "memory");
+}
+// All threads of both CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 32 lanes x 8 columns of 32-bit words from TMEM (thread i of the warp gets lane base + i).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+}  // namespace tc
+}  // namespace g2v
