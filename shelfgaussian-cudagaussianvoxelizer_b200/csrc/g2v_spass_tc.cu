@@ -346,8 +346,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) spass_t
                                 const uint64_t al = ah + (uint64_t)(kAHalf >> 4);
                                 const uint64_t bh = bdesc0 + so + (uint64_t)(ks * 2);
                                 const uint64_t bl = bh + (uint64_t)(kBHalf >> 4);
-                                tc::mma_f16_ss_pair(d, ah, bh, kIdesc, j + h2 > 0 || ks > 0);
-                                tc::mma_f16_ss_pair(d, ah, bl, kIdesc, true);
+                                tc::mma_f16_ss_pair<tc::kColFill>(d, ah, bh, kIdesc, j + h2 > 0 || ks > 0);
+                                tc::mma_f16_ss_pair<tc::kColLastUse>(d, ah, bl, kIdesc, true);
                                 tc::mma_f16_ss_pair(d, al, bh, kIdesc, true);
                             }
                             tc::mma_commit_pair(tc::smem_u32(&ms.empty[st]), (uint16_t)3);

@@ -469,8 +469,8 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
                             const uint64_t ah = adesc0 + soff + (uint64_t)((mb * 4096) >> 4);
                             const uint64_t al = ah + (uint64_t)(kAHalf >> 4);
                             const uint32_t d = tmem + (uint32_t)(buf * kBufCols + mb * kUV);
-                            tc::mma_f16_ss(d, ah, bh, kIdesc, i > 0);
-                            tc::mma_f16_ss(d, ah, bl, kIdesc, true);
+                            tc::mma_f16_ss<tc::kColFill>(d, ah, bh, kIdesc, i > 0);
+                            tc::mma_f16_ss<tc::kColLastUse>(d, ah, bl, kIdesc, true);
                             tc::mma_f16_ss(d, al, bh, kIdesc, true);
                         }
                         tc::mma_commit(tc::smem_u32(&ms.empty[st]));

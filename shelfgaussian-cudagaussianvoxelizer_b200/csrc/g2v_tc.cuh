@@ -52,14 +52,33 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn, int
            ((uint32_t)(M >> 4) << 24);
 }
 
+// A-operand collector use of an MMA: kColNone reads A from shared memory; kColFill reads it and keeps it
+// in the tensor core's collector buffer; kColLastUse takes A from the collector (the previous MMA's A,
+// which the descriptor must repeat) and releases it.  hi*hi + hi*lo of a split contraction share A_hi.
+constexpr int kColNone = 0, kColFill = 1, kColLastUse = 2;
+
 // D[tmem] (+)= A[smem] * B[smem], issued by one thread.
+template <int kCol = kColNone>
 __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                            bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+    if constexpr (kCol == kColFill)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+    else if constexpr (kCol == kColLastUse)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
 }
 
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread have completed.
@@ -80,11 +99,11 @@ __device__ __forceinline__ void mma_step2x3_commit(uint32_t d0, uint32_t d1, uin
         "{\n\t.reg .pred p, t;\n\t"
         "setp.ne.b32 p, %9, 0;\n\t"
         "setp.eq.u32 t, 0, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %8, p;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %7, %8, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%0], %2, %6, %8, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%0], %2, %7, %8, t;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %6, %8, t;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%1], %4, %6, %8, p;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%1], %4, %7, %8, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%1], %4, %6, %8, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%1], %4, %7, %8, t;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%1], %5, %6, %8, t;\n\t"
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%10];\n\t}\n" ::"r"(d0),
         "r"(d1), "l"(ah0), "l"(al0), "l"(ah1), "l"(al1), "l"(bh), "l"(bl), "r"(idesc), "r"((uint32_t)accumulate),
@@ -100,8 +119,8 @@ __device__ __forceinline__ void mma_step1x3_commit(uint32_t d, uint64_t ah, uint
         "{\n\t.reg .pred p, t;\n\t"
         "setp.ne.b32 p, %6, 0;\n\t"
         "setp.eq.u32 t, 0, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %3, %5, p;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %4, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%0], %1, %3, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%0], %1, %4, %5, t;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %3, %5, t;\n\t"
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}\n" ::"r"(d),
         "l"(ah), "l"(al), "l"(bh), "l"(bl), "r"(idesc), "r"((uint32_t)accumulate), "r"(mbar)
@@ -480,13 +499,27 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 }
 // D[tmem] (+)= A * B over the pair (M = 256: rows 0-127 from the leader's A, 128-255 from the other
 // CTA's; B's N rows: the first N/2 from the leader, the rest from the other CTA); one leader thread.
+template <int kCol = kColNone>
 __device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                 bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+    if constexpr (kCol == kColFill)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16.collector::a::fill [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+    else if constexpr (kCol == kColLastUse)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16.collector::a::lastuse [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
 }
 // Arrive on the mbarrier at shared::cta offset `mbar_saddr` in every CTA of `cta_mask` once all prior
 // pair MMAs of this thread have completed.
