@@ -226,7 +226,7 @@ void block_shape(const Grid& G, int B[3], int nb[3]) {
     B[2] = 4;
     if (const char* e = getenv("G2V_FPASS_BLOCK")) {
         int b[3];
-        if (sscanf(e, "%d,%d,%d", &b[0], &b[1], &b[2]) == 3 && b[0] > 0 && b[1] > 0 && b[2] > 0 && b[0] * b[1] * b[2] <= 16)
+        if (sscanf(e, "%d,%d,%d", &b[0], &b[1], &b[2]) == 3 && b[0] > 0 && b[1] > 0 && b[2] > 0 && b[0] * b[1] * b[2] <= 32)
             for (int a = 0; a < 3; ++a) B[a] = b[a];
     }
     B[2] = G.tiles[2] < B[2] ? G.tiles[2] : B[2];
