@@ -219,9 +219,11 @@ void set_slab_local(Grid& G, int tx_begin, int tx_end) {
     G.xlen = (tx_end * kTile < G.dims[0] ? tx_end * kTile : G.dims[0]) - G.xoff;
 }
 
-// Blocks of tiles used by the feature-gradient pass.
+// Blocks of tiles used by the feature-gradient pass: 4 x 2 x 4 by default (cfg3: a block holds ~370
+// Gaussians, so its two slot passes are fuller than the 256 + ~33 of 2 x 2 x 4 blocks, and a Gaussian has
+// ~40% fewer block partial rows to write and reduce; the pass time is the same).
 void block_shape(const Grid& G, int B[3], int nb[3]) {
-    B[0] = 2;
+    B[0] = 4;
     B[1] = 2;
     B[2] = 4;
     if (const char* e = getenv("G2V_FPASS_BLOCK")) {

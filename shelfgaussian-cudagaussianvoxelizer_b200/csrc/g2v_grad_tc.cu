@@ -47,7 +47,7 @@ constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kGS = 4;                          // staging stages of the fp32 gradient
 constexpr int kGBytes = 16 * kCG * 4;           // 16 KB: [ly][lz][256 channels]
-constexpr int kMaxBlockTiles = 32;              // tiles per block (default 2 x 2 x 4)
+constexpr int kMaxBlockTiles = 32;              // tiles per block (default 4 x 2 x 4)
 // N of a pass = its slot count rounded up to 16 (a pass that is not full issues narrower MMAs)
 
 struct FMisc {
