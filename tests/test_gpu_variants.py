@@ -172,3 +172,35 @@ def test_splat_weight_variants_match_default(env, c):
         ref = same_ww
     np.testing.assert_array_equal(got[0], ref[0])
     np.testing.assert_array_equal(got[5], ref[5])
+
+
+@pytest.mark.parametrize("shape", ["2,2,4", "1,1,4", "2,1,2", "4,4,2"])
+def test_feature_gradient_block_shapes_match_default(shape):
+    """The feature-gradient blocks (G2V_FPASS_BLOCK) change which Gaussians share a block, how many slot
+    passes a block takes and how many partial rows a Gaussian sums, not the gradient: every shape agrees
+    with the default blocks and with the float64 oracle within the parity bar."""
+    from CudaGaussianVoxelizer import _C
+    size, rng = [0.4] * 3, [-8.0, -8.0, -1.0, 8.0, 8.0, 5.4]
+    n, c = 3000, 300
+    m, o, cv, f = oracle.generate_inputs(n, c, rng, seed=21, num_outside=n // 20, var_max=8.0)
+    dims = oracle.grid_shape(size, rng)[0]
+    g = torch.Generator().manual_seed(22)
+    gD, gF = torch.randn(*dims, generator=g).cuda(), torch.randn(*dims, c, generator=g).cuda()
+    mt, ot, ct, ft = dev(m.numpy(), o.numpy(), cv.numpy(), f.numpy())
+    density, cov_inv, lb, ub, nvox, grid_feats, off, ids, _ = _C.gaussian_voxelizer_forward(mt, ot, ct, size, rng, ft)
+
+    def bwd():
+        return [t.cpu().numpy() for t in _C.gaussian_voxelizer_backward(
+            gD, gF, mt, ot, cov_inv, size, rng, lb, ub, nvox, off, ids, density, grid_feats, ft)[:4]]
+
+    ref = bwd()
+    got = _with_env({"G2V_FPASS_BLOCK": shape}, bwd)
+    names = ("grad_means", "grad_cov", "grad_opacity", "grad_features")
+    for name, a, b in zip(names, got, ref):
+        assert_close(f"{name} ({shape} vs default blocks)", a, b)
+    lb_h, ub_h = lb.cpu().numpy(), ub.cpu().numpy()
+    m, o, cv, f = m.numpy(), o.numpy(), cv.numpy(), f.numpy()
+    dref, fref = oracle.forward(m, o, cv, f, lb_h, ub_h, size, rng, dims)
+    oref = oracle.backward(m, o, cv, f, lb_h, ub_h, size, rng, dims, gD.cpu().numpy(), gF.cpu().numpy(), dref, fref)
+    for name, a, b in zip(names, got, oref):
+        assert_close(f"{name} ({shape} blocks vs oracle)", a, b)
