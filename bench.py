@@ -193,8 +193,8 @@ def algorithmic_bytes(kernel, n, c, V, M, MB, ntiles):
         return 4 * V * c + 4 * V + 4 * n * c + per_gauss + 4 * M + 4 * (ntiles + 1)
     if kernel == "spass_kernel":
         return 4 * V * c + 4 * n * c + 8 * V + 40 * M + per_gauss + 4 * M + 4 * (ntiles + 1)
-    if kernel == "fpass_kernel":
-        return 4 * V * c + 4 * V + 4 * MB * c + per_gauss
+    if kernel == "fpass_kernel":  # the gradient rows, D, the feature-gradient rows; partial rows are not algorithmic
+        return 4 * V * c + 4 * V + 4 * n * c + per_gauss
     if kernel == "reduce_feats_kernel":
         return 4 * MB * c + 4 * n * c
     return None
