@@ -243,7 +243,7 @@ G2V_API int g2v_backward_workspace_size(int64_t num_gaussians, int64_t num_pairs
  * Only the voxels of tiles with tile x in [tile_x_begin, tile_x_end) contribute (0 / tiles[0] for the
  * whole grid): on an x-slab the outputs are that slab's partial gradients.
  * e_v = sum_c dL/dF_vc F_vc (the reference's at::bmm) is formed from the per-pair dot products the
- * tile pass computes anyway; only for the voxels of cells (z pairs of tiles) with more than 256 Gaussians
+ * tile pass computes anyway; only for the voxels of cells (z columns of four tiles) with more than 256 Gaussians
  * is it read from grid_feats (the forward's output), which saves running their slot passes twice.
  * grid_feats may be NULL: then those cells run both passes.
  * Replaces src/cuda_gaussian_voxelizer.cu:1920-2057 (the at::bmm at cu:1996 and
@@ -260,7 +260,7 @@ G2V_API int g2v_backward(const float* grad_density, const float* grad_grid_feats
 
 /*
  * g2v_backward over the whole grid with the tile pass's unit lists supplied by the caller instead of
- * rebuilt: unit_offsets (num_units + 1) and unit_lists (num_pairs), the z-pairs-of-tiles CSR that
+ * rebuilt: unit_offsets (num_units + 1) and unit_lists (num_pairs), the z-columns-of-four-tiles CSR that
  * g2v_forward_splat built for the same Gaussians (copied out with g2v_forward_splat_unit_lists).  Used
  * only by the tensor-core path (the FP32-FMA variant builds its own lists).  Same outputs and workspace as
  * g2v_backward; a host-side saving of the reference's backward, which rebuilds nothing because it walks
@@ -278,7 +278,7 @@ G2V_API int g2v_backward_units(const float* grad_density, const float* grad_grid
                                size_t workspace_bytes, void* stream);
 
 /*
- * Copies the unit lists (Gaussian ids of each z pair of tiles, ascending; the cell->Gaussian CSR the
+ * Copies the unit lists (Gaussian ids of each z column of four tiles, ascending; the cell->Gaussian CSR the
  * tensor-core splat and tile pass work on) out of a g2v_forward_splat workspace after the call:
  * unit_offsets (num_units + 1, int32) and unit_lists (num_pairs, int32; entries beyond
  * unit_offsets[num_units] unspecified).  With unit_offsets == NULL only *num_units is returned.  Fails
@@ -385,7 +385,7 @@ G2V_API int g2v_cosine_loss_backward(const float* grad_loss, const int32_t* coun
  * sort of the (tile id, Gaussian id) pairs by tile, run-length encoding and scan of
  * src/cuda_gaussian_voxelizer.cu:1675-1772 (CUB there; the reference keeps the map internal).
  * tile_offsets (num_tiles+1, int32, all tiles), t2g_gaussians (num_pairs, int32, Gaussian ids ascending
- * within each tile).  The tensor-core splat does not need this map (it lists z pairs of tiles), so the
+ * within each tile).  The tensor-core splat does not need this map (it lists z columns of four tiles), so the
  * forward no longer builds it; this call exposes it.  workspace: g2v_build_t2g_workspace_size.
  */
 G2V_API int g2v_build_t2g_workspace_size(int64_t num_gaussians, int64_t num_pairs, const int dims[3],
