@@ -396,10 +396,10 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
                             if (cg == 0) dsum[lz] += w[lz];
                         }
                         uint4 h, l;
-                        tc::split_half2(w[0], w[1], h.x, l.x);
-                        tc::split_half2(w[2], w[3], h.y, l.y);
-                        tc::split_half2(w[4], w[5], h.z, l.z);
-                        tc::split_half2(w[6], w[7], h.w, l.w);
+                        tc::split_half2_v(w[0], w[1], h.x, l.x);
+                        tc::split_half2_v(w[2], w[3], h.y, l.y);
+                        tc::split_half2_v(w[4], w[5], h.z, l.z);
+                        tc::split_half2_v(w[6], w[7], h.w, l.w);
                         const int r = k & 7;
                         const uint32_t off = (k >> 3) * 2048 + (o >> 3) * 1024 + r * 128 + (((o & 7) ^ r) << 4);
                         *reinterpret_cast<uint4*>(bst + off) = h;

@@ -301,6 +301,20 @@ __device__ __forceinline__ void split_half2(float x0, float x1, uint32_t& hi, ui
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(x1 - hf.y), "f"(x0 - hf.x));
 }
 
+// split_half2 with the hi half rounded to 11 significant bits by Veltkamp's splitting, c = (2^13 + 1) x,
+// h = c - (c - x) (packed f32x2 operations on the FMA pipes), so that converting h to f16 is exact (for
+// |x| >= 2^-14; below, f16 subnormals round h once more, an error under 2^-24 of the 2^14..2^15 range the
+// splat scales its weights to) and no f16 -> f32 conversion is needed for the remainder: two conversions per
+// pair instead of four.
+__device__ __forceinline__ void split_half2_v(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const float2 x = make_float2(x0, x1), m1 = make_float2(-1.0f, -1.0f);
+    const float2 c = __fmul2_rn(x, make_float2(8193.0f, 8193.0f));
+    const float2 h = __ffma2_rn(__ffma2_rn(x, m1, c), m1, c);  // c - (c - x)
+    const float2 r = __ffma2_rn(h, m1, x);                      // x - h, exact
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(h.y), "f"(h.x));
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r.y), "f"(r.x));
+}
+
 // 2^x with the hardware approximation (ex2.approx.ftz).
 __device__ __forceinline__ float exp2_approx(float x) {
     float y;
