@@ -679,8 +679,10 @@ int launch_splat_tc(const float* means, const float* opacity, const float* cov_i
     memset(&omap, 0, sizeof(omap));
     const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
     const bool tma = C > 0 && encode_grid_rows_f32(&omap, grid_feats, ldims, C, kCG, 8, 2, 1);
-    unsigned char* wc = splat_weight_cache() ? wcache : nullptr;
-    if (splat_weight_warps((C + kCG - 1) / kCG) == 4)
+    // the cache serves a unit's later channel groups: with one group (C <= 256) nothing would read it
+    const int ngroups = (C + kCG - 1) / kCG;
+    unsigned char* wc = (splat_weight_cache() && ngroups > 1) ? wcache : nullptr;
+    if (splat_weight_warps(ngroups) == 4)
         return launch_splat_kernel<4>(tma, omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units,
                                       tile_x_begin, G, density, grid_feats, wc, err, s);
     return launch_splat_kernel<8>(tma, omap, hi, lo, unscale, C, Cp, gp, unit_offsets, unit_lists, num_units,
