@@ -546,6 +546,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) spass_t
                         float gr[10];
 #pragma unroll
                         for (int i = 0; i < 10; ++i) gr[i] = 0.0f;
+                        // Qz lz^2 plus the z box mask (0 / -inf) of the tile's four z layers
+                        float zq[4];
+#pragma unroll
+                        for (int lz = 0; lz < kTile; ++lz) {
+                            const int zz = kTile * t + lz;
+                            zq[lz] = (zz >= zlo && zz <= zhi) ? Qz * (float)(lz * lz) : -INFINITY;
+                        }
+                        const float2 Zq01 = make_float2(zq[0], zq[1]), Zq23 = make_float2(zq[2], zq[3]);
                         const float dzt = fmaf((float)(kTile * t), hz, dz0);  // slice origin z offset
                         const float dy0 = voxel_centre(G, 1, y0) - A.y;
 #pragma unroll 1
@@ -571,22 +579,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) spass_t
                                 const float bzy = fmaf(Qyz, (float)ly, bz);
                                 const float4* V4 = reinterpret_cast<const float4*>(&ms.va[lx * 64 + ly * 16 + kTile * t]);
                                 const float4 va01 = V4[0], va23 = V4[1];
-                                const float vax[4] = {va01.x, va01.z, va23.x, va23.z};
-                                const float vay[4] = {va01.y, va01.w, va23.y, va23.w};
-#pragma unroll
-                                for (int lz = 0; lz < kTile; ++lz) {
-                                    const int zz = kTile * t + lz;
-                                    const float mzl = (zz >= zlo && zz <= zhi) ? 0.0f : -INFINITY;
-                                    const float m = fmaf(fmaf(Qz, (float)lz, bzy), (float)lz, ay) + mzl;
-                                    const float ex = tc::exp2_approx(m);
-                                    const float ae = fmaf(Sv[lz], vax[lz], vay[lz]) * ex;
-                                    M00 += ae;
-                                    M10 = fmaf(ae, (float)ly, M10);
-                                    M01 = fmaf(ae, (float)lz, M01);
-                                    M20 = fmaf(ae, (float)(ly * ly), M20);
-                                    M11 = fmaf(ae, (float)(ly * lz), M11);
-                                    M02 = fmaf(ae, (float)(lz * lz), M02);
-                                }
+                                // z pairs (0, 1), (2, 3) in packed f32x2 arithmetic: m = (ay + Qz lz^2 + z mask) + lz bzy
+                                const float2 A2 = make_float2(ay, ay), B2 = make_float2(bzy, bzy);
+                                const float2 m01 = __ffma2_rn(make_float2(0.0f, 1.0f), B2, __fadd2_rn(A2, Zq01));
+                                const float2 m23 = __ffma2_rn(make_float2(2.0f, 3.0f), B2, __fadd2_rn(A2, Zq23));
+                                const float2 e01 = make_float2(tc::exp2_approx(m01.x), tc::exp2_approx(m01.y));
+                                const float2 e23 = make_float2(tc::exp2_approx(m23.x), tc::exp2_approx(m23.y));
+                                // a e = (S * va.x + va.y) e
+                                const float2 a01 = __fmul2_rn(__ffma2_rn(make_float2(Sv[0], Sv[1]), make_float2(va01.x, va01.z),
+                                                                         make_float2(va01.y, va01.w)), e01);
+                                const float2 a23 = __fmul2_rn(__ffma2_rn(make_float2(Sv[2], Sv[3]), make_float2(va23.x, va23.z),
+                                                                         make_float2(va23.y, va23.w)), e23);
+                                // row sums over lz of a e, lz a e, lz^2 a e; the ly moments from them
+                                const float2 s0 = __fadd2_rn(a01, a23);
+                                const float2 s1 = __ffma2_rn(make_float2(2.0f, 3.0f), a23, __fmul2_rn(make_float2(0.0f, 1.0f), a01));
+                                const float2 s2 = __ffma2_rn(make_float2(4.0f, 9.0f), a23, __fmul2_rn(make_float2(0.0f, 1.0f), a01));
+                                const float r0 = s0.x + s0.y, r1 = s1.x + s1.y, r2 = s2.x + s2.y;
+                                const float fy = (float)ly;
+                                M00 += r0;
+                                M10 = fmaf(fy, r0, M10);
+                                M20 = fmaf(fy * fy, r0, M20);
+                                M01 += r1;
+                                M11 = fmaf(fy, r1, M11);
+                                M02 += r2;
                             }
                             gr[9] += M00;
                             gr[0] = fmaf(q0x, M00, fmaf(ux, M10, fmaf(wx, M01, gr[0])));
