@@ -472,6 +472,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) spass_t
                 const float Qz = k2 * hz * hz * P2.x;
                 if (do1) {
                     if (wact) {
+                        // Qz lz^2 plus the z box mask (0 / -inf) of this thread's z half, as z pairs
+                        float2 zh[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int l0 = 8 * h + 2 * i, l1 = l0 + 1;
+                            zh[i] = make_float2((l0 >= zlo && l0 <= zhi) ? Qz * (float)(l0 * l0) : -INFINITY,
+                                                (l1 >= zlo && l1 <= zhi) ? Qz * (float)(l1 * l1) : -INFINITY);
+                        }
 #pragma unroll 1
                         for (int lx = 0; lx < kTile; ++lx) {
                             const float dx = voxel_centre(G, 0, x0 + lx) - A.x;
@@ -491,13 +499,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) spass_t
                                 const float b0 = k2 * hz * (qz + ptz);
                                 const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[vb]);
                                 const float4 La = L4[0], Lb = L4[1];
-                                const float L[8] = {La.x, La.y, La.z, La.w, Lb.x, Lb.y, Lb.z, Lb.w};
+                                const float2 L2[4] = {make_float2(La.x, La.y), make_float2(La.z, La.w),
+                                                      make_float2(Lb.x, Lb.y), make_float2(Lb.z, Lb.w)};
+                                const float2 A2 = make_float2(a0, a0), B2 = make_float2(b0, b0);
+                                const float2 O2 = make_float2(A.w, A.w);
 #pragma unroll
-                                for (int i = 0; i < 8; ++i) {
-                                    const int lz = 8 * h + i;
-                                    const float mzl = (lz >= zlo && lz <= zhi) ? L[i] : -INFINITY;
-                                    const float m = fmaf(fmaf(Qz, (float)lz, b0), (float)lz, a0) + mzl;
-                                    Sv[i] *= A.w * tc::exp2_approx(m);
+                                for (int i = 0; i < 4; ++i) {
+                                    // m = (a0 + Qz lz^2 + z mask + log2(1/den)) + lz b0 for lz = 8 h + 2 i, + 1
+                                    const float l0 = (float)(8 * h + 2 * i);
+                                    const float2 m = __ffma2_rn(make_float2(l0, l0 + 1.0f), B2,
+                                                                __fadd2_rn(__fadd2_rn(A2, zh[i]), L2[i]));
+                                    const float2 e = make_float2(tc::exp2_approx(m.x), tc::exp2_approx(m.y));
+                                    const float2 sv = __fmul2_rn(make_float2(Sv[2 * i], Sv[2 * i + 1]), __fmul2_rn(O2, e));
+                                    Sv[2 * i] = sv.x;
+                                    Sv[2 * i + 1] = sv.y;
                                 }
                                 const float r = warp_reduce_scatter8(Sv, lane);
                                 if ((lane & 3) == 0) ms.epart[q][vb + (lane >> 2)] = r;

@@ -387,13 +387,25 @@ __global__ void __launch_bounds__(Roles<NW>::kThreads, 1) splat_tc_kernel(
                         // base-2 exponent along the line: k2 (a + b lz + P8 hz^2 lz^2) + kt; -inf outside the box
                         const float a0 = live ? fmaf(k2, dx * qx + dy * qy + dz * qz, fkt) : -INFINITY;
                         const float b0 = k2 * hz * (qz + ptz), qq = k2 * hz * hz * P2.x;
+                        // z pairs (lz, lz + 1) in packed f32x2 arithmetic
                         float w[8];
+                        const float2 A2 = make_float2(a0, a0), B2 = make_float2(b0, b0), Q2 = make_float2(qq, qq);
+                        const float2 O2 = make_float2(A.w, A.w);
 #pragma unroll
-                        for (int lz = 0; lz < 8; ++lz) {
-                            const float mzl = (lz >= zlo && lz <= zhi) ? 0.0f : -INFINITY;
-                            const float m = fmaf(fmaf(qq, (float)lz, b0), (float)lz, a0) + mzl;
-                            w[lz] = A.w * tc::exp2_approx(m);
-                            if (cg == 0) dsum[lz] += w[lz];
+                        for (int p = 0; p < 4; ++p) {
+                            const int l0 = 2 * p, l1 = l0 + 1;
+                            const float2 mz = make_float2((l0 >= zlo && l0 <= zhi) ? 0.0f : -INFINITY,
+                                                          (l1 >= zlo && l1 <= zhi) ? 0.0f : -INFINITY);
+                            const float2 lz2 = make_float2((float)l0, (float)l1);
+                            const float2 m = __fadd2_rn(__ffma2_rn(__ffma2_rn(Q2, lz2, B2), lz2, A2), mz);
+                            const float2 wv = __fmul2_rn(O2, make_float2(tc::exp2_approx(m.x), tc::exp2_approx(m.y)));
+                            w[l0] = wv.x;
+                            w[l1] = wv.y;
+                            if (cg == 0) {
+                                const float2 d = __fadd2_rn(make_float2(dsum[l0], dsum[l1]), wv);
+                                dsum[l0] = d.x;
+                                dsum[l1] = d.y;
+                            }
                         }
                         uint4 h, l;
                         tc::split_half2_v(w[0], w[1], h.x, l.x);
