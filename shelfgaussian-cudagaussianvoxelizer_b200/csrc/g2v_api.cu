@@ -30,7 +30,7 @@ int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid
                      const int ncells_dim[3], int cell_x_begin, int cell_x_end, const int32_t* g2t_offsets,
                      int32_t* g2t_tile_ids, int64_t g2t_cap, int32_t* per_gaussian, int32_t* counts, int32_t* cell_offsets,
                      int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s,
-                     int64_t list_cap, int* err);
+                     int64_t list_cap, int* err, bool x_order = false);
 int count_gaussian_cells(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                          int32_t* per_gaussian, int32_t* dummy_counts, cudaStream_t s);
 int fill_g2t(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int32_t* g2t_offsets,
@@ -969,7 +969,8 @@ static int backward_impl(const float* grad_density, const float* grad_grid_feats
         // per-Gaussian block counts, then the offsets of the partial rows
         if ((rc = build_cell_lists(valid_voxel_lb, valid_voxel_ub, num_gaussians, G, B, nb, bx_begin, bx_end,
                                    nullptr, nullptr, 0, w.g2b_counts, w.block_counts, w.block_offsets,
-                                   w.block_unsorted, w.block_lists, w.block_scan, total, s, num_block_pairs, err)))
+                                   w.block_unsorted, w.block_lists, w.block_scan, total, s, num_block_pairs, err,
+                                   /*x_order: the tensor-core pass skips the steps outside a slot range's boxes*/ tcore)))
             return rc;
         if ((rc = launch_exclusive_scan(w.g2b_counts, num_gaussians, w.g2b_offsets, total, w.g_scan, s,
                                         num_block_pairs, err)))

@@ -134,6 +134,11 @@ constexpr int kBitonicMax = 1024;
 constexpr int kBitmapBits = 1 << 16;                 // ids per bitmap pass
 constexpr int kBitmapWords = kBitmapBits / 32;       // 2048 words, 8 per thread
 
+// Ordered bitmap compaction of the k distinct ids in[0..k) into out[0..k), in passes of 65536 ids over
+// [0, n_ids); `bits` is kBitmapWords words of shared memory.
+__device__ void sort_ids_bitmap(const int32_t* __restrict__ in, int32_t* __restrict__ out, int k, int64_t n_ids,
+                                unsigned* bits, int64_t* warp_sums);
+
 // One block per cell: writes the cell's Gaussian ids in ascending order from `in` to `out`.
 // Small lists use a bitonic sort in shared memory; long lists an ordered bitmap compaction over the
 // id range in passes of 65536 ids (the ids of one cell are distinct).
@@ -174,13 +179,17 @@ __global__ void __launch_bounds__(kSortThreads) cells_sort_kernel(const int32_t*
         for (int i = threadIdx.x; i < k; i += kSortThreads) out[s + i] = sh[i];
         return;
     }
+    sort_ids_bitmap(in + s, out + s, k, n_ids, reinterpret_cast<unsigned*>(sh), warp_sums);
+}
+
+__device__ void sort_ids_bitmap(const int32_t* __restrict__ in, int32_t* __restrict__ out, int k, int64_t n_ids,
+                                unsigned* bits, int64_t* warp_sums) {
     int64_t written = 0;
-    unsigned* bits = reinterpret_cast<unsigned*>(sh);
     for (int64_t c0 = 0; c0 < n_ids; c0 += kBitmapBits) {
         for (int w = threadIdx.x; w < kBitmapWords; w += kSortThreads) bits[w] = 0u;
         __syncthreads();
         for (int i = threadIdx.x; i < k; i += kSortThreads) {
-            const int64_t id = in[s + i];
+            const int64_t id = in[i];
             if (id >= c0 && id < c0 + kBitmapBits) {
                 const int r = (int)(id - c0);
                 atomicOr(&bits[r >> 5], 1u << (r & 31));
@@ -203,12 +212,66 @@ __global__ void __launch_bounds__(kSortThreads) cells_sort_kernel(const int32_t*
             while (m) {
                 const int bpos = __ffs(m) - 1;
                 m &= m - 1;
-                out[s + pos++] = (int32_t)(c0 + (int64_t)(threadIdx.x * per + q) * 32 + bpos);
+                out[pos++] = (int32_t)(c0 + (int64_t)(threadIdx.x * per + q) * 32 + bpos);
             }
         }
         written += tot;
         __syncthreads();
     }
+}
+
+constexpr int kSortXMax = 4096;  // 32 KB of 64-bit keys
+static_assert(kSortXMax * 2 >= kBitmapWords, "the x-order sort's keys also hold the bitmap");
+
+// One block per cell: writes the cell's Gaussian ids ordered by (voxel box lower x, id), so that the
+// Gaussians of a slot range of the feature-gradient pass lie close together along x and its steps
+// outside their boxes can be skipped.  Lists longer than kSortXMax keep the ascending id order.
+__global__ void __launch_bounds__(kSortThreads) cells_sort_x_kernel(const int32_t* __restrict__ offsets,
+                                                                    const int32_t* __restrict__ in,
+                                                                    const int32_t* __restrict__ lb,
+                                                                    int32_t* __restrict__ out, int64_t n_ids) {
+    __shared__ unsigned long long sh[kSortXMax];
+    __shared__ int64_t warp_sums[kSortThreads / 32];
+    const int cell = blockIdx.x;
+    const int s = offsets[cell], e = offsets[cell + 1];
+    const int k = e - s;
+    if (k <= 0) return;
+    if (k == 1) {
+        if (threadIdx.x == 0) out[s] = in[s];
+        return;
+    }
+    if (k > kSortXMax) {
+        sort_ids_bitmap(in + s, out + s, k, n_ids, reinterpret_cast<unsigned*>(sh), warp_sums);
+        return;
+    }
+    int p = 2;
+    while (p < k) p <<= 1;
+    for (int i = threadIdx.x; i < p; i += kSortThreads) {
+        unsigned long long key = ~0ull;
+        if (i < k) {
+            const int g = in[s + i];
+            key = ((unsigned long long)(uint32_t)lb[(int64_t)g * 3] << 32) | (uint32_t)g;
+        }
+        sh[i] = key;
+    }
+    __syncthreads();
+    for (int kk = 2; kk <= p; kk <<= 1) {
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < p; i += kSortThreads) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = sh[i], b = sh[ixj];
+                    const bool up = (i & kk) == 0;
+                    if ((a > b) == up) {
+                        sh[i] = b;
+                        sh[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = threadIdx.x; i < k; i += kSortThreads) out[s + i] = (int32_t)(uint32_t)sh[i];
 }
 
 }  // namespace
@@ -217,12 +280,13 @@ __global__ void __launch_bounds__(kSortThreads) cells_sort_kernel(const int32_t*
 // (ncx, ncy, ncz) cells of (cx, cy, cz) tiles.  Also writes the reference's G2T tile ids when
 // g2t_tile_ids != nullptr (1x1x1 cells) and the per-Gaussian cell count when per_gaussian != nullptr.
 // Buffers: counts (ncells, zeroed here), cell_offsets (ncells+1), unsorted and lists (>= pairs),
-// scan_ws (scan_workspace_bytes(ncells)), total (1 int64).
+// scan_ws (scan_workspace_bytes(ncells)), total (1 int64).  x_order: each list ordered by (voxel box
+// lower x, id) instead of by id (lists of at most 4096 Gaussians).
 int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid& G, const int cell[3],
                      const int ncells_dim[3], int cell_x_begin, int cell_x_end, const int32_t* g2t_offsets,
                      int32_t* g2t_tile_ids, int64_t g2t_cap, int32_t* per_gaussian, int32_t* counts, int32_t* cell_offsets,
                      int32_t* unsorted, int32_t* lists, void* scan_ws, int64_t* total, cudaStream_t s,
-                     int64_t list_cap, int* err) {
+                     int64_t list_cap, int* err, bool x_order) {
     const int nx = cell_x_end - cell_x_begin;
     const int64_t ncells = (int64_t)nx * ncells_dim[1] * ncells_dim[2];
     if (ncells > 0) G2V_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)ncells, s));
@@ -244,8 +308,14 @@ int build_cell_lists(const int32_t* lb, const int32_t* ub, int64_t n, const Grid
                                                     ncells_dim[2], cell_x_begin, cell_x_end, cell_offsets,
                                                     counts, unsorted));
         G2V_LAUNCH_CHECK("cells_scatter_kernel");
-        G2V_TIMED("cells_sort_kernel", s, cells_sort_kernel<<<(unsigned)ncells, kSortThreads, 0, s>>>(cell_offsets, unsorted, lists, n));
-        G2V_LAUNCH_CHECK("cells_sort_kernel");
+        if (x_order) {
+            G2V_TIMED("cells_sort_x_kernel", s,
+                      cells_sort_x_kernel<<<(unsigned)ncells, kSortThreads, 0, s>>>(cell_offsets, unsorted, lb, lists, n));
+            G2V_LAUNCH_CHECK("cells_sort_x_kernel");
+        } else {
+            G2V_TIMED("cells_sort_kernel", s, cells_sort_kernel<<<(unsigned)ncells, kSortThreads, 0, s>>>(cell_offsets, unsorted, lists, n));
+            G2V_LAUNCH_CHECK("cells_sort_kernel");
+        }
     }
     return 0;
 }

@@ -48,6 +48,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr int kGS = 4;                          // staging stages of the fp32 gradient
 constexpr int kGBytes = 16 * kCG * 4;           // 16 KB: [ly][lz][256 channels]
 constexpr int kMaxBlockTiles = 32;              // tiles per block (default 4 x 2 x 4)
+constexpr int kMaskPasses = 32;                 // passes with a step mask; later passes take every step
 // N of a pass = its slot count rounded up to 16 (a pass that is not full issues narrower MMAs)
 
 struct FMisc {
@@ -56,12 +57,27 @@ struct FMisc {
     uint64_t mma_done;
     uint32_t tmem_base;
     int fail;
+    uint32_t smask[kMaskPasses][4];  // per pass: the steps that meet a slot's box (bit j = step j)
     uint64_t gfull[kGS];   // TMA bytes of a staged step
     uint64_t gempty[kGS];  // 8 converter-warp arrivals
     alignas(16) GParams prm[kSlots];  // slot records of the pass (each weight thread stages its own)
     int64_t rowoff[kSlots];
     alignas(16) float lrd[kMaxBlockTiles * kVoxPerTile];  // log2(1 / max(D, eps)), -inf outside the grid
     int4 org[kMaxBlockTiles];  // voxel origin of each tile of the block, in step order
+};
+// Walks the set bits of a 128-bit step mask in ascending order.
+struct StepList {
+    uint64_t lo, hi;
+    __device__ __forceinline__ int next() {
+        if (lo) {
+            const int j = __ffsll((long long)lo) - 1;
+            lo &= lo - 1;
+            return j;
+        }
+        const int j = 64 + __ffsll((long long)hi) - 1;
+        hi &= hi - 1;
+        return j;
+    }
 };
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(FMisc);
 static_assert(kSmemBytes <= 227 * 1024, "fpass_tc_kernel shared memory");
@@ -109,7 +125,6 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         }
         return;
     }
-    const int nsteps = ntiles * 4;  // 4 x-slices of 16 voxels per tile
     if (ntiles > kMaxBlockTiles) {  // the host sizes blocks within the limit
         if (tid == 0) atomicOr(err, 4);
         return;
@@ -125,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             tc::mbar_init(&ms.empty[i], 1);
         }
         tc::mbar_init(&ms.mma_done, 1);
+        for (int i = 0; i < kMaskPasses * 4; ++i) ms.smask[i >> 2][i & 3] = 0u;
         for (int i = 0; i < kGS; ++i) {
             tc::mbar_init(&ms.gfull[i], 1);
             tc::mbar_init(&ms.gempty[i], 8);
@@ -138,6 +154,44 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     tc::tc_fence_after();
     const uint32_t tmem = ms.tmem_base;
     bool ok = true;
+
+    // The steps of each pass whose x-slice meets at least one of its slots' voxel boxes; every role
+    // walks the same list, so the others (no weight of the pass is non-zero there) are skipped.  The
+    // block lists are ordered by the boxes' lower x, so a pass's slots lie close together along x.
+    // A warp's 32 slots belong to one pass (576 and 256 are multiples of 32).
+    {
+        const int nmask = min(Kb, kMaskPasses * kSlots);
+        for (int sl0 = 0; sl0 < nmask; sl0 += kThreads) {
+            const int sl = sl0 + tid;
+            uint64_t mlo = 0, mhi = 0;
+            if (sl < nmask) {
+                const GParams& gp = gparams[block_lists[s0 + sl]];
+                const float4 d = gp.w[3], e4 = gp.w[4];
+                const int lx = __float_as_int(d.y), ly = __float_as_int(d.z), lz = __float_as_int(d.w);
+                const int ux = __float_as_int(e4.x), uy = __float_as_int(e4.y), uz = __float_as_int(e4.z);
+                for (int ti = 0; ti < ntiles; ++ti) {
+                    const int4 o = ms.org[ti];
+                    const int a = max(lx - o.x, 0), b = min(ux - o.x, 3);
+                    if (a > b || ly > o.y + 3 || uy < o.y || lz > o.z + 3 || uz < o.z) continue;
+                    const uint64_t bits = (uint64_t)(((2u << (b - a)) - 1u) << a);  // x-slices a..b of tile ti
+                    if (ti < 16) mlo |= bits << (ti * 4);
+                    else mhi |= bits << ((ti - 16) * 4);
+                }
+            }
+            const uint32_t w0 = __reduce_or_sync(0xffffffffu, (uint32_t)mlo);
+            const uint32_t w1 = __reduce_or_sync(0xffffffffu, (uint32_t)(mlo >> 32));
+            const uint32_t w2 = __reduce_or_sync(0xffffffffu, (uint32_t)mhi);
+            const uint32_t w3 = __reduce_or_sync(0xffffffffu, (uint32_t)(mhi >> 32));
+            if (lane == 0 && sl < nmask) {
+                uint32_t* m = ms.smask[sl / kSlots];
+                if (w0) atomicOr(&m[0], w0);
+                if (w1) atomicOr(&m[1], w1);
+                if (w2) atomicOr(&m[2], w2);
+                if (w3) atomicOr(&m[3], w3);
+            }
+        }
+    }
+    __syncthreads();
 
     auto a_stage = [&](int st, int hl) -> unsigned char* { return base + st * kStageBytes + hl * kAHalf; };
     auto b_stage = [&](int st, int hl) -> unsigned char* {
@@ -165,11 +219,32 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         const bool tr = ns <= 128;
         const uint32_t idesc = tr ? tc::idesc_bf16_f32(128, 256, /*A K-major*/ 0, /*B MN-major*/ 1)
                                   : tc::idesc_bf16_f32(128, nn, /*A MN-major*/ 1, /*B K-major*/ 0);
+        // the pass's step list, padded to whole rounds of the operand ring with skipped steps (their
+        // weights are zero) so that the MMA loop keeps one register set of descriptors per stage
+        const int nsteps = ntiles * 4;
+        uint64_t step_lo = nsteps >= 64 ? ~0ull : (1ull << nsteps) - 1;
+        uint64_t step_hi = nsteps <= 64 ? 0ull : (nsteps == 128 ? ~0ull : (1ull << (nsteps - 64)) - 1);
+        if (pass < kMaskPasses) {
+            const uint64_t all_lo = step_lo, all_hi = step_hi;
+            step_lo = ((uint64_t)ms.smask[pass][1] << 32) | ms.smask[pass][0];
+            step_hi = ((uint64_t)ms.smask[pass][3] << 32) | ms.smask[pass][2];
+            for (int pad = (4 - (__popcll(step_lo) + __popcll(step_hi))) & 3; pad > 0; --pad) {
+                const uint64_t flo = all_lo & ~step_lo;  // lowest skipped step
+                if (flo) step_lo |= flo & (~flo + 1);
+                else {
+                    const uint64_t fhi = all_hi & ~step_hi;
+                    step_hi |= fhi & (~fhi + 1);
+                }
+            }
+        }
+        const int nact = __popcll(step_lo) + __popcll(step_hi);
+        StepList steps{step_lo, step_hi};
         if (warp < 8) {
             // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 2 voxel rows) ----------
             const int jc = lane;                                     // channels c0 + 8 jc .. + 7
             const int mb = jc >> 4, a = (jc >> 3) & 1, jj = jc & 7;
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+            for (int sk = 0; sk < nact && ok; ++sk, ++it) {
+                const int j = steps.next();
                 const int st = it % kStages, gs = it % kGS;
                 int x0, y0, z0, ks;
                 step_geom(j, x0, y0, z0, ks);
@@ -274,10 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             float my[4];
             float2 Zq01 = make_float2(0.f, 0.f), Zq23 = make_float2(0.f, 0.f);  // Qzz lz^2 + z box mask
             int xlo = 1, xhi = 0;
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+            bool yz_in = false;  // the slot's box meets the tile's y and z ranges
+            int cur_tile = -1;
+            for (int sk = 0; sk < nact && ok; ++sk, ++it) {
+                const int j = steps.next();
                 const int st = it % kStages;
                 const int ks = j & 3;
-                if (ks == 0 && trow) {
+                if ((j >> 2) != cur_tile && trow) {  // first step of the pass in this tile
                     const int4 o = ms.org[j >> 2];
                     const GParams& gp = ms.prm[t];
                     const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
@@ -305,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     xhi = __float_as_int(e4.x) - o.x;
                     const int ylo = __float_as_int(d.z) - o.y, yhi = __float_as_int(e4.y) - o.y;
                     const int zlo = __float_as_int(d.w) - o.z, zhi = __float_as_int(e4.z) - o.z;
+                    yz_in = ylo <= 3 && yhi >= 0 && zlo <= 3 && zhi >= 0;
                     float mz[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -314,15 +393,17 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     Zq01 = make_float2(mz[0], mz[1]);
                     Zq23 = make_float2(mz[2], mz[3]);
                 }
+                cur_tile = j >> 2;
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                 if (!ok) break;
+                const bool act = slot && yz_in && ks >= xlo && ks <= xhi;
                 if (trow) {
                     // pairs of z-consecutive voxels (lz = 0,1 and 2,3) in packed f32x2 arithmetic:
                     //   m = (Ay + Qzz lz^2 + z mask) + lz Bz2 + log2(1 / den_v),  w = o 2^m
                     float2 w[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) w[e] = make_float2(0.0f, 0.0f);
-                    if (slot && ks >= xlo && ks <= xhi) {
+                    if (act) {
                         const float fk = (float)ks;
                         const float Ak = fmaf(fmaf(Qxx, fk, Bx), fk, A0);
                         const float Byk = fmaf(Qxy, fk, By), Bzk = fmaf(Qxz, fk, Bz);
@@ -365,7 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             }
         } else if (kTma && warp == 17 && lane == 0) {
             // ---------------- TMA thread: the step's gradient rows into the staging ring ----------------
-            for (int j = 0; j < nsteps && ok; ++j, ++it) {
+            for (int sk = 0; sk < nact && ok; ++sk, ++it) {
+                const int j = steps.next();
                 const int gs = it % kGS;
                 int x0, y0, z0, ks;
                 step_geom(j, x0, y0, z0, ks);
@@ -378,9 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         } else if (warp == 16 && lane == 0) {
             // ---------------- MMA thread ----------------
             // Every stage's descriptors are formed once and kept in registers: the step loop is unrolled by
-            // the stage count (a pass has 4 x-slices per tile, so its steps come in whole rounds of the ring
-            // and stage s of a round is step j0 + s), and each step is one wait and one block of six MMAs
-            // plus the commit that frees the stage.
+            // the stage count (a pass's step list comes in whole rounds of the ring, so stage s of a round
+            // is its step j0 + s), and each step is one wait and one block of six MMAs plus the commit that
+            // frees the stage.
             static_assert(kStages == 4 && kMB == 2, "the MMA loop is unrolled for four stages of two M-blocks");
             const uint64_t adesc0 = tc::smem_desc(tc::smem_u32(a_stage(0, 0)), 1024, 4096, tc::kLayoutSw128);
             const uint64_t bdesc0 = tc::smem_desc(tc::smem_u32(b_stage(0, 0)), 16, 256, tc::kLayoutSw32);
@@ -397,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     dal[st][mb] = dah[st][mb] + (uint64_t)(kAHalf >> 4);
                 }
             }
-            for (int j0 = 0; j0 < nsteps && ok; j0 += kStages) {
+            for (int j0 = 0; j0 < nact && ok; j0 += kStages) {
                 const uint32_t par = (uint32_t)((it + j0) / kStages) & 1;
 #pragma unroll
                 for (int st = 0; st < kStages; ++st) {
@@ -412,10 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                                                dbh[st], dbl[st], idesc, (j0 + st) > 0, tc::smem_u32(&ms.empty[st]));
                 }
             }
-            it += nsteps;
+            it += nact;
             tc::mma_commit(tc::smem_u32(&ms.mma_done));
         } else {
-            it += nsteps;
+            it += nact;
         }
 
         ok = tc::mbar_wait_drain(&ms.mma_done, pass & 1, err) && ok;
@@ -437,7 +519,12 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 const int cc = c0 + cb * 64 + jc * 16;
                 if (cc >= C) break;  // warp-uniform
                 float v[16];
-                tc::tmem_ld16(tbase + jc * 16, v);
+                if (nact > 0) {
+                    tc::tmem_ld16(tbase + jc * 16, v);
+                } else {  // no step of the pass: the accumulator was never written
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+                }
                 if (ro >= 0) {
                     float* dst = partialF + ro * C + cc;
                     if (vec && cc + 16 <= C) {
@@ -456,7 +543,13 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             const int c = c0 + mb * 128 + q * 32 + lane;
             const int jc0 = half * 8, jc1 = min(half * 8 + 8, (ns + 15) >> 4);  // warp-uniform
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + mb * kSlots;
-            if (jc0 < jc1) {
+            if (jc0 < jc1 && nact == 0) {  // no step of the pass: the accumulator was never written
+                if (c < C)
+                    for (int sl = jc0 * 16; sl < min(jc1 * 16, ns); ++sl) {
+                        const int64_t ro = ms.rowoff[sl];
+                        if (ro >= 0) partialF[ro * C + c] = 0.0f;
+                    }
+            } else if (jc0 < jc1) {
                 float va[16], vb[16];
                 tc::tmem_ld16(tbase + jc0 * 16, va);
                 for (int jc = jc0; jc < jc1; ++jc) {
