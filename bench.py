@@ -673,18 +673,20 @@ def run_single_scene(args, rank, world, dev):
     import torch
     import torch.distributed as dist
     from CudaGaussianVoxelizer import _C, _lib
-    from CudaGaussianVoxelizer.distributed import SlabGaussianVoxelizer
+    from CudaGaussianVoxelizer.distributed import SlabGaussianVoxelizer, balanced_slab_bounds, tile_pairs_per_column
 
     cfg = CONFIGS[args.config]
     size, rng, m_h, o_h, c_h, f_h = make_inputs(cfg, seed=args.seed)  # the same scene on every rank
     (X, Y, Z), tiles = _C.grid_shape(size, rng)
     n, c = cfg["n"], cfg["c"]
-    vox = SlabGaussianVoxelizer(voxel_size=size, voxel_range=rng, rank=rank, world=world)
+    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
+    # slabs split by the (Gaussian, tile) pairs per tile column (the same counts on every rank)
+    bounds = balanced_slab_bounds(tile_pairs_per_column(leaves[0].detach(), leaves[2].detach(), size, rng), world)
+    vox = SlabGaussianVoxelizer(voxel_size=size, voxel_range=rng, rank=rank, world=world, tile_bounds=bounds)
     x0, x1 = vox.rows
     g = torch.Generator(device=dev).manual_seed(1000)
     gD = torch.randn((X, Y, Z), device=dev, generator=g)[x0:x1].contiguous()
     gF = torch.randn((X, Y, Z, c), device=dev, generator=g)[x0:x1].contiguous()
-    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
 
     def step():
         density, grid_feats, _ = vox(*leaves)
@@ -739,7 +741,8 @@ def run_single_scene(args, rank, world, dev):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, reference distributions)",
         "config": {"workload": f"{args.config}: one scene, N={n} Gaussians, C={c}, {X}x{Y}x{Z} voxels, split into "
-                               f"{world} x-slabs of tiles (rank 0: tiles {vox.tile_range}), one NCCL all-reduce of "
+                               f"{world} x-slabs of tiles balanced by (Gaussian, tile) pairs (tile column bounds "
+                               f"{bounds}), one NCCL all-reduce of "
                                f"the packed gradients per step", "global_batch": 1,
                    "parallelism": f"x-slab split over {world} GPUs",
                    "l2": "inputs larger than L2 (grid_feats 4*V*C bytes)"},
@@ -944,12 +947,15 @@ def extra_single_scene_cfg5(args, rank, world, dev):
     cfg = CONFIGS["cfg5"]
     size, rng, m_h, o_h, c_h, f_h = make_inputs(cfg, seed=args.seed)
     (X, Y, Z), tiles = _C.grid_shape(size, rng)
-    vox = dmod.SlabGaussianVoxelizer(voxel_size=size, voxel_range=rng, rank=rank, world=world)
+    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
+    # slabs split by the (Gaussian, tile) pairs per tile column (the same counts on every rank)
+    bounds = dmod.balanced_slab_bounds(dmod.tile_pairs_per_column(leaves[0].detach(), leaves[2].detach(), size, rng),
+                                       world)
+    vox = dmod.SlabGaussianVoxelizer(voxel_size=size, voxel_range=rng, rank=rank, world=world, tile_bounds=bounds)
     x0, x1 = vox.rows
     g = torch.Generator(device=dev).manual_seed(1000)
     gD = torch.randn((X, Y, Z), device=dev, generator=g)[x0:x1].contiguous()
     gF = torch.empty((x1 - x0, Y, Z, cfg["c"]), device=dev).normal_(generator=g)
-    leaves = [t.to(dev).requires_grad_() for t in (m_h, o_h, c_h, f_h)]
 
     def step():
         density, grid_feats, _ = vox(*leaves)
@@ -971,7 +977,7 @@ def extra_single_scene_cfg5(args, rank, world, dev):
     torch.cuda.empty_cache()
     return {"value": round(ms, 4), "unit": "ms", "n_gpus": world, "scaling": "strong (one fixed scene)",
             "workload": f"cfg5: N={cfg['n']} Gaussians, C={cfg['c']}, {X}x{Y}x{Z} voxels, var U(0.5,8); "
-                        f"{world} x-slabs of tiles (rank 0: tiles {vox.tile_range})",
+                        f"{world} x-slabs of tiles balanced by (Gaussian, tile) pairs (tile column bounds {bounds})",
             "allreduce_ms": None if ar_ms is None else round(ar_ms, 4),
             "allreduce_mb": round(packed_mb, 1) if world > 1 else 0.0,
             "collective_in_step": "one NCCL all-reduce (sum) of the packed [N x (13 + C)] gradients" if world > 1

@@ -20,8 +20,8 @@ import torch.nn as nn
 
 from . import _C, _lib
 
-__all__ = ["slab_tiles", "slab_voxel_rows", "pack_grads", "unpack_grads", "allreduce_grads", "slab_forward",
-           "slab_backward", "SlabGaussianVoxelizer"]
+__all__ = ["slab_tiles", "slab_voxel_rows", "balanced_slab_bounds", "tile_pairs_per_column", "pack_grads",
+           "unpack_grads", "allreduce_grads", "slab_forward", "slab_backward", "SlabGaussianVoxelizer"]
 
 
 def slab_tiles(tiles_x: int, rank: int, world: int) -> tuple[int, int]:
@@ -32,6 +32,78 @@ def slab_tiles(tiles_x: int, rank: int, world: int) -> tuple[int, int]:
     q, r = divmod(tiles_x, world)
     b = rank * q + min(rank, r)
     return b, b + q + (1 if rank < r else 0)
+
+
+def balanced_slab_bounds(column_work, world: int) -> list[int]:
+    """Slab boundaries [0 = b_0 < b_1 < ... < b_world = len(column_work)] over the tile x columns that split
+    the work per column (the (Gaussian, tile) pairs of each column, tile_pairs_per_column) as evenly as
+    contiguous slabs can: b_r is the column boundary whose running work is nearest r / world of the total,
+    kept strictly increasing so that every slab has at least one column.  Plain host arithmetic on the
+    given list, so every rank that passes the same counts gets the same slabs.  With equal work per column
+    the slab sizes differ by at most one column."""
+    work = [max(0, int(w)) for w in column_work]
+    tiles_x = len(work)
+    if world < 1 or tiles_x < world:
+        raise ValueError(f"{tiles_x} tile columns cannot be split into {world} non-empty slabs")
+    prefix = [0]
+    for w in work:
+        prefix.append(prefix[-1] + w)
+    total = prefix[-1]
+    if total == 0:
+        return [slab_tiles(tiles_x, r, world)[0] for r in range(world)] + [tiles_x]
+    bounds = [0]
+    k = 0
+    for r in range(1, world):
+        target = total * r / world
+        lo, hi = bounds[-1] + 1, tiles_x - (world - r)  # leave a column for each slab still to come
+        k = max(k, lo)
+        while k < hi and prefix[k + 1] <= target:
+            k += 1
+        if k < hi and abs(prefix[k + 1] - target) < abs(prefix[k] - target):
+            k += 1
+        bounds.append(min(max(k, lo), hi))
+    bounds.append(tiles_x)
+    return bounds
+
+
+def tile_pairs_per_column(means3D, covariances, voxel_size, voxel_range) -> list[int]:
+    """(Gaussian, tile) pairs of the scene per tile x column: the library's boxes (g2v_forward_prepare_plan
+    on the Gaussians' device) and one read back to the host.  The same inputs give the same counts on every
+    rank, so balanced_slab_bounds of them needs no communication."""
+    lib = _lib.load()
+    size_h = _C._host_values(voxel_size, 3, "voxel_size")
+    range_h = _C._host_values(voxel_range, 6, "voxel_range")
+    _C._need(means3D, "means3D", dim=2)
+    dev = means3D.device
+    n = means3D.shape[0]
+    (X, _, _), tiles = _lib.grid_shape(size_h, range_h)
+    if n == 0:
+        return [0] * tiles[0]
+    means3D, covariances = means3D.contiguous(), covariances.contiguous()
+    i32 = dict(dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        cov_inv = torch.empty((n, 9), dtype=torch.float32, device=dev)
+        lb = torch.empty((n, 3), **i32)
+        ub = torch.empty((n, 3), **i32)
+        nvox = torch.empty((n,), **i32)
+        g2t_offsets = torch.empty((n + 1,), **i32)
+        nbytes = ctypes.c_size_t()
+        _lib.check(lib.g2v_forward_prepare_plan_workspace_size(n, ctypes.byref(nbytes)),
+                   "g2v_forward_prepare_plan_workspace_size")
+        ws = _C._workspace(nbytes.value, dev)
+        m, mb = ctypes.c_int64(), ctypes.c_int64()
+        _lib.check(lib.g2v_forward_prepare_plan(_C._ptr(means3D), _C._ptr(covariances), n, _lib.f3(size_h),
+                                                _lib.f6(range_h), _C._ptr(cov_inv), _C._ptr(lb), _C._ptr(ub),
+                                                _C._ptr(nvox), _C._ptr(g2t_offsets), 0, _C._ptr(ws), ws.numel(),
+                                                sptr, ctypes.byref(m), ctypes.byref(mb)), "g2v_forward_prepare_plan")
+        live = (ub >= lb).all(dim=1)
+        tlo, thi = torch.div(lb, 4, rounding_mode="floor"), torch.div(ub, 4, rounding_mode="floor")
+        per = ((thi[:, 1] - tlo[:, 1] + 1) * (thi[:, 2] - tlo[:, 2] + 1)).to(torch.int64) * live.to(torch.int64)
+        diff = torch.zeros(tiles[0] + 1, dtype=torch.int64, device=dev)
+        diff.index_add_(0, tlo[:, 0].to(torch.int64).clamp(0, tiles[0]), per)
+        diff.index_add_(0, (thi[:, 0].to(torch.int64) + 1).clamp(0, tiles[0]), -per)
+        return torch.cumsum(diff, 0)[:tiles[0]].tolist()
 
 
 def slab_voxel_rows(dims_x: int, tile_range: tuple[int, int]) -> tuple[int, int]:
@@ -228,10 +300,13 @@ class SlabGaussianVoxelizer(nn.Module):
     rank, returns ``(density (rows,Y,Z), grid_feats (rows,Y,Z,C), (x0, x1))``: this rank's slab of the
     reference outputs, voxel x rows [x0, x1).  Gradients reaching the inputs are the whole scene's on every
     rank (one all-reduce inside backward).  With a single rank it is PyCudaGaussianVoxelizer without stats.
+    The slabs hold equal numbers of tile columns unless ``tile_bounds`` (world + 1 increasing column
+    boundaries from 0 to the grid's tile columns, e.g. balanced_slab_bounds of tile_pairs_per_column) gives
+    them, the same list on every rank.
     """
 
     def __init__(self, voxel_size=[0.4, 0.4, 0.4], voxel_range=[-40, -40, -1, 40, 40, 5.4], group=None,
-                 rank: int | None = None, world: int | None = None):
+                 rank: int | None = None, world: int | None = None, tile_bounds=None):
         super().__init__()
         self.voxel_size = torch.tensor(voxel_size, dtype=torch.float32, device="cuda")
         self.voxel_range = torch.tensor(voxel_range, dtype=torch.float32, device="cuda")
@@ -242,7 +317,15 @@ class SlabGaussianVoxelizer(nn.Module):
         size_h = _C._host_values(self.voxel_size, 3, "voxel_size")
         range_h = _C._host_values(self.voxel_range, 6, "voxel_range")
         (X, _, _), tiles = _lib.grid_shape(size_h, range_h)
-        self.tile_range = slab_tiles(tiles[0], self.rank, self.world)
+        if tile_bounds is None:
+            self.tile_range = slab_tiles(tiles[0], self.rank, self.world)
+        else:
+            b = [int(v) for v in tile_bounds]
+            if (len(b) != self.world + 1 or b[0] != 0 or b[-1] != tiles[0] or
+                    any(e <= s for s, e in zip(b, b[1:]))):
+                raise ValueError(f"tile_bounds must be {self.world + 1} increasing column boundaries from 0 to "
+                                 f"{tiles[0]}, got {b}")
+            self.tile_range = (b[self.rank], b[self.rank + 1])
         self.rows = slab_voxel_rows(X, self.tile_range)
 
     def forward(self, means3D, opacity, covariances, features=None):

@@ -23,6 +23,35 @@ def test_slab_tiles_partition(tiles, world):
     assert max(sizes) - min(sizes) <= 1
 
 
+@pytest.mark.parametrize("tiles,world,seed", [(50, 2, 0), (100, 4, 1), (100, 8, 2), (13, 5, 3), (7, 7, 4)])
+def test_balanced_slab_bounds(tiles, world, seed):
+    rs = np.random.default_rng(seed)
+    work = rs.integers(0, 1000, size=tiles).tolist()
+    b = D.balanced_slab_bounds(work, world)
+    assert len(b) == world + 1 and b[0] == 0 and b[-1] == tiles
+    assert all(e > s for s, e in zip(b, b[1:]))  # every slab keeps a column
+    total = sum(work)
+    per = [sum(work[s:e]) for s, e in zip(b, b[1:])]
+    assert sum(per) == total
+    if tiles >= 4 * world:  # room to balance: no slab exceeds its share by more than one column
+        assert max(per) <= total / world + max(work)
+    # the same counts give the same slabs (every rank computes them on its own)
+    assert D.balanced_slab_bounds(list(work), world) == b
+
+
+def test_balanced_slab_bounds_uniform_and_degenerate():
+    for tiles, world in [(50, 2), (100, 8), (12, 3)]:
+        b = D.balanced_slab_bounds([5] * tiles, world)  # equal work: slab sizes differ by at most one column
+        sizes = [e - s for s, e in zip(b, b[1:])]
+        assert max(sizes) - min(sizes) <= 1 and sum(sizes) == tiles
+    assert D.balanced_slab_bounds([0] * 10, 3) == [D.slab_tiles(10, r, 3)[0] for r in range(3)] + [10]
+    # work piled on one edge column: the other slabs still get a column each
+    b = D.balanced_slab_bounds([1000] + [0] * 9, 4)
+    assert b[0] == 0 and b[-1] == 10 and all(e > s for s, e in zip(b, b[1:]))
+    with pytest.raises(ValueError):
+        D.balanced_slab_bounds([1, 2], 3)
+
+
 def test_slab_voxel_rows_clip_the_last_tile():
     assert D.slab_voxel_rows(10, (0, 2)) == (0, 8)
     assert D.slab_voxel_rows(10, (2, 3)) == (8, 10)  # the last tile holds 2 voxel rows

@@ -21,8 +21,9 @@ def _scene(n=3000, c=96, half=10.0, seed=21, var_max=2.5):
     return size, rng, m.numpy(), o.numpy(), cv.numpy(), f.numpy()
 
 
-@pytest.mark.parametrize("world,c", [(2, 96), (3, 96), (4, 37), (3, 0)])
-def test_slab_local_matches_whole_grid(world, c):
+@pytest.mark.parametrize("world,c,balanced", [(2, 96, False), (3, 96, False), (4, 37, False), (3, 0, False),
+                                              (3, 96, True), (5, 37, True)])
+def test_slab_local_matches_whole_grid(world, c, balanced):
     from CudaGaussianVoxelizer import _C
     from CudaGaussianVoxelizer import distributed as D
     size, rng, m, o, cv, f = _scene(c=max(c, 1))
@@ -39,9 +40,13 @@ def test_slab_local_matches_whole_grid(world, c):
     ref = _C.gaussian_voxelizer_backward(gD, gF if c > 0 else torch.empty(0, device="cuda"), mt, ot, cov_inv, st, rt,
                                          lb, ub, nvox, off, ids, density, grid_feats, ft, timing=False)
     tiles_x = (X + 3) // 4
+    if balanced:  # slabs split by the (Gaussian, tile) pairs per tile column
+        cols = D.tile_pairs_per_column(mt, ct, st, rt)
+        assert len(cols) == tiles_x and sum(cols) == int(off[-1])
+        bounds = D.balanced_slab_bounds(cols, world)
     sums = None
     for r in range(world):
-        tr = D.slab_tiles(tiles_x, r, world)
+        tr = (bounds[r], bounds[r + 1]) if balanced else D.slab_tiles(tiles_x, r, world)
         x0, x1 = D.slab_voxel_rows(X, tr)
         d_s, f_s, state = D.slab_forward(mt, ot, ct, st, rt, ft, tr)
         torch.cuda.synchronize()
@@ -74,6 +79,19 @@ def test_slab_module_single_rank_matches_reference_api():
     b = torch.autograd.grad([d2, f2], ins2, [gD, gF])
     for x, y in zip(a, b):
         assert_close("grad", x.cpu().numpy(), y.cpu().numpy(), rtol=1e-6)
+
+
+def test_slab_module_tile_bounds():
+    from CudaGaussianVoxelizer import distributed as D
+    size, rng = [0.4] * 3, [-10.0, -10.0, -1.0, 10.0, 10.0, 5.4]  # 50 x 50 x 16 voxels, 13 tile columns
+    bounds = [0, 2, 9, 13]
+    for r in range(3):
+        vox = D.SlabGaussianVoxelizer(size, rng, rank=r, world=3, tile_bounds=bounds)
+        assert vox.tile_range == (bounds[r], bounds[r + 1])
+        assert vox.rows == D.slab_voxel_rows(50, vox.tile_range)
+    for bad in ([0, 2, 9], [0, 9, 2, 13], [1, 2, 9, 13], [0, 2, 9, 12], [0, 2, 2, 13]):
+        with pytest.raises(ValueError):
+            D.SlabGaussianVoxelizer(size, rng, rank=0, world=3, tile_bounds=bad)
 
 
 def _nccl_rank(rank, world, port, out):
