@@ -3,25 +3,27 @@
 // For a block of tiles b and its Gaussians (the block's list, up to 256 "slots" per pass):
 //     dF[slot][c] = sum_{v in b} w_slot,v / max(D_v, 1e-6) * gF[v][c]
 // computed as D^T in TMEM: M = 128 channels (2 M-blocks = 256 channels per CTA), N = 256 slots,
-// K = 16 voxels per step (a quarter of a tile: the 16 voxels of one x-slice).  Accuracy: both operands
+// K = 32 voxels per pipeline step (half a tile: the 16 voxels of each of two x-slices, two MMA K-steps).  Accuracy: both operands
 // are split into bf16 pairs (x = hi + lo to ~2^-17) and hi*hi + hi*lo + lo*hi is accumulated in fp32;
 // bf16 keeps the fp32 exponent range, so no scaling is needed.
 //
 // Operands in shared memory (per stage):
-//   A = gF^T slice (256 channels x 16 voxels) MN-major, 128-byte swizzle (64-channel x 8-voxel atoms),
+//   A = gF^T slices (256 channels x 32 voxels) MN-major, 128-byte swizzle (64-channel x 8-voxel atoms),
 //       converted from the fp32 gradient rows by the producer warps;
-//   B = weights (256 slots x 16 voxels) K-major, 32-byte swizzle (a row = one slot's 16 voxels), evaluated by the weight
+//   B = weights (256 slots x 16 voxels, one block per x-slice) K-major, 32-byte swizzle (a row = one slot's 16 voxels), evaluated by the weight
 //       warps from the slot's parameters: over the 4x4 voxels of an x-slice the Mahalanobis distance is a
 //       quadratic in (ly, lz), so each weight costs a few FMAs and one exp.
-// The fp32 gradient rows of a step (16 voxels x 256 channels, 16 KB) arrive in a staging ring through
+// The fp32 gradient rows of a step (32 voxels x 256 channels, 32 KB) arrive in a staging ring through
 // one tiled TMA load of the 4-D tensor map {C, Z, Y, X} (zero fill beyond the grid and beyond C); when
 // the map cannot be built (C % 4 != 0, unaligned base) the converting threads load the rows themselves.
 // log2(1 / max(D, eps)) of the block's voxels is computed once per CTA into shared memory and folded,
 // with the box masks (-inf), into the base-2 exponent of each weight: w / den = o * 2^(quadratic + L_v).
 // Roles (576 threads): warps 0-7 convert A (two voxel rows each), warps 8-15 produce B (one Gaussian
 // slot per thread), warp 16 (one thread) issues the 6 MMAs of a step, warp 17 (one thread) issues the
-// TMA loads; two warps of each producer role per scheduler hide the latency of the dependent math.  Four operand stages and four staging stages are
-// handed over through mbarriers; every wait is bounded.  The epilogue writes the
+// TMA loads; two warps of each producer role per scheduler hide the latency of the dependent math.  Two
+// operand stages and two staging stages of two x-slices each are handed over through mbarriers (a step of
+// two slices halves the barrier round trips per voxel, which the pipeline's hand-offs are bound by); every
+// wait is bounded.  The epilogue writes the
 // per-(Gaussian, block) partial rows of the reference's dL/dfeatures; a deterministic CSR-order reduction
 // sums them per Gaussian.
 #include <cstddef>
@@ -40,13 +42,15 @@ constexpr int kThreads = 576;
 constexpr int kSlots = 256;
 constexpr int kMB = 2;                          // M-blocks of 128 channels per CTA
 constexpr int kCG = kMB * 128;                  // channels per CTA
-constexpr int kStages = 4;
-constexpr int kAHalf = kMB * 4096;              // one operand half, one stage
-constexpr int kBHalf = kSlots * 16 * 2;
+constexpr int kStages = 2;                      // operand stages of two x-slices (K = 32 voxels) each
+constexpr int kASub = kMB * 4096;               // one operand half of one x-slice
+constexpr int kAHalf = 2 * kASub;               // one operand half, one stage
+constexpr int kBSub = kSlots * 16 * 2;
+constexpr int kBHalf = 2 * kBSub;
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
 constexpr uint32_t kTmemCols = 512;
-constexpr int kGS = 4;                          // staging stages of the fp32 gradient
-constexpr int kGBytes = 16 * kCG * 4;           // 16 KB: [ly][lz][256 channels]
+constexpr int kGS = 2;                          // staging stages of the fp32 gradient
+constexpr int kGBytes = 32 * kCG * 4;           // 32 KB: [lx][ly][lz][256 channels]
 constexpr int kMaxBlockTiles = 32;              // tiles per block (default 4 x 2 x 4)
 constexpr int kMaskPasses = 32;                 // passes with a step mask; later passes take every step
 // N of a pass = its slot count rounded up to 16 (a pass that is not full issues narrower MMAs)
@@ -155,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     const uint32_t tmem = ms.tmem_base;
     bool ok = true;
 
-    // The steps of each pass whose x-slice meets at least one of its slots' voxel boxes; every role
+    // The steps of each pass whose pair of x-slices meets at least one of its slots' voxel boxes; every role
     // walks the same list, so the others (no weight of the pass is non-zero there) are skipped.  The
     // block lists are ordered by the boxes' lower x, so a pass's slots lie close together along x.
     // A warp's 32 slots belong to one pass (576 and 256 are multiples of 32).
@@ -173,9 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     const int4 o = ms.org[ti];
                     const int a = max(lx - o.x, 0), b = min(ux - o.x, 3);
                     if (a > b || ly > o.y + 3 || uy < o.y || lz > o.z + 3 || uz < o.z) continue;
-                    const uint64_t bits = (uint64_t)(((2u << (b - a)) - 1u) << a);  // x-slices a..b of tile ti
-                    if (ti < 16) mlo |= bits << (ti * 4);
-                    else mhi |= bits << ((ti - 16) * 4);
+                    const int pa = a >> 1, pb = b >> 1;  // slice pairs of x-slices a..b
+                    mlo |= (uint64_t)(((2u << (pb - pa)) - 1u) << pa) << (ti * 2);
                 }
             }
             const uint32_t w0 = __reduce_or_sync(0xffffffffu, (uint32_t)mlo);
@@ -197,10 +200,10 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
     auto b_stage = [&](int st, int hl) -> unsigned char* {
         return base + st * kStageBytes + 2 * kAHalf + hl * kBHalf;
     };
-    // tile and x-slice of step j of a pass
+    // tile and first x-slice of step j (a pair of x-slices) of a pass
     auto step_geom = [&](int j, int& x0, int& y0, int& z0, int& ks) {
-        const int4 o = ms.org[j >> 2];
-        ks = j & 3;
+        const int4 o = ms.org[j >> 1];
+        ks = (j & 1) * 2;
         x0 = o.x;
         y0 = o.y;
         z0 = o.z;
@@ -221,14 +224,14 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                                   : tc::idesc_bf16_f32(128, nn, /*A MN-major*/ 1, /*B K-major*/ 0);
         // the pass's step list, padded to whole rounds of the operand ring with skipped steps (their
         // weights are zero) so that the MMA loop keeps one register set of descriptors per stage
-        const int nsteps = ntiles * 4;
+        const int nsteps = ntiles * 2;
         uint64_t step_lo = nsteps >= 64 ? ~0ull : (1ull << nsteps) - 1;
-        uint64_t step_hi = nsteps <= 64 ? 0ull : (nsteps == 128 ? ~0ull : (1ull << (nsteps - 64)) - 1);
+        uint64_t step_hi = 0ull;
         if (pass < kMaskPasses) {
             const uint64_t all_lo = step_lo, all_hi = step_hi;
             step_lo = ((uint64_t)ms.smask[pass][1] << 32) | ms.smask[pass][0];
             step_hi = ((uint64_t)ms.smask[pass][3] << 32) | ms.smask[pass][2];
-            for (int pad = (4 - (__popcll(step_lo) + __popcll(step_hi))) & 3; pad > 0; --pad) {
+            for (int pad = (kStages - (__popcll(step_lo) + __popcll(step_hi))) & (kStages - 1); pad > 0; --pad) {
                 const uint64_t flo = all_lo & ~step_lo;  // lowest skipped step
                 if (flo) step_lo |= flo & (~flo + 1);
                 else {
@@ -252,16 +255,18 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 if (kTma && ok) ok = tc::mbar_wait(&ms.gfull[gs], (it / kGS) & 1, err);
                 if (!ok) break;
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int r = warp * 2 + i;  // voxel row of the step: (ly, lz) = (r / 4, r % 4)
+                for (int i4 = 0; i4 < 4; ++i4) {
+                    const int kk = i4 >> 1;                // x-slice of the pair
+                    const int r = warp * 2 + (i4 & 1);     // voxel row of the slice: (ly, lz) = (r / 4, r % 4)
+                    const int v = kk * 16 + r;             // K index within the stage
                     float f[8];
                     if (kTma) {
-                        const float4* src = reinterpret_cast<const float4*>(gstage + gs * kGBytes + r * (kCG * 4) + jc * 32);
+                        const float4* src = reinterpret_cast<const float4*>(gstage + gs * kGBytes + v * (kCG * 4) + jc * 32);
                         const float4 u = src[0], w4 = src[1];
                         f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
                         f[4] = w4.x; f[5] = w4.y; f[6] = w4.z; f[7] = w4.w;
                     } else {
-                        const int x = x0 + ks, y = y0 + (r >> 2), z = z0 + (r & 3);
+                        const int x = x0 + ks + kk, y = y0 + (r >> 2), z = z0 + (r & 3);
                         const bool vok = x < G.dims[0] && y < G.dims[1] && z < G.dims[2];
                         const int c = c0 + jc * 8;
                         const float* src = grad_feats + grid_row(G, x, y, z) * C + c;
@@ -280,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     tc::split_bf16x2_p(make_float2(f[2], f[3]), h.y, l.y);
                     tc::split_bf16x2_p(make_float2(f[4], f[5]), h.z, l.z);
                     tc::split_bf16x2_p(make_float2(f[6], f[7]), h.w, l.w);
-                    const int g8 = r >> 3, rr = r & 7;
+                    const int g8 = v >> 3, rr = v & 7;
                     // channel atom n = 2 mb + a at n KB, voxel octet g8 at 4 g8 KB: uniform strides, so the
                     // stage is both the A operand (two M-blocks of 128 channels) and a B operand of N = 256
                     const int off = mb * 2048 + a * 1024 + g8 * 4096 + rr * 128 + ((jj ^ rr) << 4);
@@ -311,11 +316,11 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                 ms.rowoff[sl] = ro;
             }
         } else if (warp < 16) {
-            // ---------------- weight warps: thread = slot t, the 16 voxels of the step's x-slice -----------
+            // ---------------- weight warps: thread = slot t, the 16 voxels of each of the step's x-slices -----
             // Over a tile the base-2 exponent of the weight is a quadratic in the local voxel (ks, ly, lz):
             //   k (d0 + h l)^T P (d0 + h l),  k = -log2(e) / 2,  d0 = tile-origin voxel centre - mean,
-            // so its 10 coefficients are formed once per tile (the first of its 4 x-slice steps) and each
-            // step only adds the ks terms.  The y / z box masks of the tile are 0 / -inf terms added per
+            // so its 10 coefficients are formed once per tile (its first step of the pass) and each x-slice
+            // only adds the ks terms.  The y / z box masks of the tile are 0 / -inf terms added per
             // (ly, lz), the x mask decides the whole slice.  Voxel centres are linear within a tile (a tile
             // never spans two stacked scenes).
             const int t = tid - 256;
@@ -354,9 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             for (int sk = 0; sk < nact && ok; ++sk, ++it) {
                 const int j = steps.next();
                 const int st = it % kStages;
-                const int ks = j & 3;
-                if ((j >> 2) != cur_tile && trow) {  // first step of the pass in this tile
-                    const int4 o = ms.org[j >> 2];
+                const int tj = j >> 1;  // tile of the step
+                if (tj != cur_tile && trow) {  // first step of the pass in this tile
+                    const int4 o = ms.org[tj];
                     const GParams& gp = ms.prm[t];
                     const float4 a = gp.w[0], b = gp.w[1], c = gp.w[2], d = gp.w[3], e4 = gp.w[4];
                     // P = [[b.x b.y b.z] [b.w c.x c.y] [c.z c.w d.x]]
@@ -393,9 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     Zq01 = make_float2(mz[0], mz[1]);
                     Zq23 = make_float2(mz[2], mz[3]);
                 }
-                cur_tile = j >> 2;
+                cur_tile = tj;
                 if (it >= kStages) ok = tc::mbar_wait(&ms.empty[st], ((it / kStages) + 1) & 1, err);
                 if (!ok) break;
+#pragma unroll 1
+                for (int kk = 0; kk < 2; ++kk) {
+                const int ks = (j & 1) * 2 + kk;
                 const bool act = slot && yz_in && ks >= xlo && ks <= xhi;
                 if (trow) {
                     // pairs of z-consecutive voxels (lz = 0,1 and 2,3) in packed f32x2 arithmetic:
@@ -407,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                         const float fk = (float)ks;
                         const float Ak = fmaf(fmaf(Qxx, fk, Bx), fk, A0);
                         const float Byk = fmaf(Qxy, fk, By), Bzk = fmaf(Qxz, fk, Bz);
-                        const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[(j >> 2) * kVoxPerTile + ks * 16]);
+                        const float4* L4 = reinterpret_cast<const float4*>(&ms.lrd[tj * kVoxPerTile + ks * 16]);
                         const float2 o2 = make_float2(opa, opa);
 #pragma unroll
                         for (int ly = 0; ly < 4; ++ly) {
@@ -435,17 +443,18 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     // K-major, 32-byte swizzle: row t = the slot's 16 voxels (32 bytes), chunk c at c ^ ((t / 4) % 2)
                     const int sw = (t >> 2) & 1;
                     const int off0 = (t >> 3) * 256 + (t & 7) * 32 + (sw << 4), off1 = off0 ^ 16;
-                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off0) = h0;
-                    *reinterpret_cast<uint4*>(b_stage(st, 0) + off1) = h1;
-                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off0) = l0;
-                    *reinterpret_cast<uint4*>(b_stage(st, 1) + off1) = l1;
+                    *reinterpret_cast<uint4*>(b_stage(st, 0) + kk * kBSub + off0) = h0;
+                    *reinterpret_cast<uint4*>(b_stage(st, 0) + kk * kBSub + off1) = h1;
+                    *reinterpret_cast<uint4*>(b_stage(st, 1) + kk * kBSub + off0) = l0;
+                    *reinterpret_cast<uint4*>(b_stage(st, 1) + kk * kBSub + off1) = l1;
+                }
                 }
                 tc::fence_async_smem();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&ms.full[st]);
             }
         } else if (kTma && warp == 17 && lane == 0) {
-            // ---------------- TMA thread: the step's gradient rows into the staging ring ----------------
+            // ---------------- TMA thread: the step's gradient rows (two x-slices) into the staging ring -----
             for (int sk = 0; sk < nact && ok; ++sk, ++it) {
                 const int j = steps.next();
                 const int gs = it % kGS;
@@ -461,9 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             // ---------------- MMA thread ----------------
             // Every stage's descriptors are formed once and kept in registers: the step loop is unrolled by
             // the stage count (a pass's step list comes in whole rounds of the ring, so stage s of a round
-            // is its step j0 + s), and each step is one wait and one block of six MMAs plus the commit that
-            // frees the stage.
-            static_assert(kStages == 4 && kMB == 2, "the MMA loop is unrolled for four stages of two M-blocks");
+            // is its step j0 + s), and each step is one wait and two blocks of six MMAs (one per x-slice)
+            // plus the commit that frees the stage.
+            static_assert(kStages == 2 && kMB == 2, "the MMA loop is unrolled for two stages of two M-blocks");
+            const uint64_t ao = (uint64_t)(kASub >> 4), bo = (uint64_t)(kBSub >> 4);  // the second x-slice
             const uint64_t adesc0 = tc::smem_desc(tc::smem_u32(a_stage(0, 0)), 1024, 4096, tc::kLayoutSw128);
             const uint64_t bdesc0 = tc::smem_desc(tc::smem_u32(b_stage(0, 0)), 16, 256, tc::kLayoutSw32);
             uint64_t dah[kStages][kMB], dal[kStages][kMB], dbh[kStages], dbl[kStages];
@@ -486,12 +496,25 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
                     ok = ok && tc::mbar_wait(&ms.full[st], par, err);
                     if (!ok) break;
                     tc::tc_fence_after();
-                    if (tr)
-                        tc::mma_step1x3_commit(tmem, dbh[st], dbl[st], dah[st][0], dal[st][0], idesc, (j0 + st) > 0,
+                    const bool acc = (j0 + st) > 0;
+                    if (tr) {
+                        tc::mma_f16_ss<tc::kColFill>(tmem, dbh[st], dah[st][0], idesc, acc);
+                        tc::mma_f16_ss<tc::kColLastUse>(tmem, dbh[st], dal[st][0], idesc, true);
+                        tc::mma_f16_ss(tmem, dbl[st], dah[st][0], idesc, true);
+                        tc::mma_step1x3_commit(tmem, dbh[st] + bo, dbl[st] + bo, dah[st][0] + ao, dal[st][0] + ao, idesc,
+                                               true, tc::smem_u32(&ms.empty[st]));
+                    } else {
+#pragma unroll
+                        for (int mb = 0; mb < kMB; ++mb) {
+                            const uint32_t d = tmem + (uint32_t)(mb * kSlots);
+                            tc::mma_f16_ss<tc::kColFill>(d, dah[st][mb], dbh[st], idesc, acc);
+                            tc::mma_f16_ss<tc::kColLastUse>(d, dah[st][mb], dbl[st], idesc, true);
+                            tc::mma_f16_ss(d, dal[st][mb], dbh[st], idesc, true);
+                        }
+                        tc::mma_step2x3_commit(tmem, tmem + kSlots, dah[st][0] + ao, dal[st][0] + ao, dah[st][1] + ao,
+                                               dal[st][1] + ao, dbh[st] + bo, dbl[st] + bo, idesc, true,
                                                tc::smem_u32(&ms.empty[st]));
-                    else
-                        tc::mma_step2x3_commit(tmem, tmem + kSlots, dah[st][0], dal[st][0], dah[st][1], dal[st][1],
-                                               dbh[st], dbl[st], idesc, (j0 + st) > 0, tc::smem_u32(&ms.empty[st]));
+                    }
                 }
             }
             it += nact;
@@ -598,7 +621,7 @@ int launch_fpass_tc(const float* grad_feats, int C, const float* density, const 
     CUtensorMap gmap;
     memset(&gmap, 0, sizeof(gmap));
     const int ldims[3] = {G.xlen, G.dims[1], G.dims[2]};
-    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, ldims, C, kCG, kTile, kTile, 1);
+    const bool tma = encode_grid_rows_f32(&gmap, grad_feats, ldims, C, kCG, kTile, kTile, 2);  // x-slice pairs
     auto kern = tma ? fpass_tc_kernel<true> : fpass_tc_kernel<false>;
     G2V_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int64_t grid = nblocks * ngroups;
