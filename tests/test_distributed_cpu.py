@@ -83,14 +83,30 @@ def _scene():
     return size, rng, m, o, cv, f, bx, dims, gD, gF, dref, fref
 
 
-def _rank_main(rank, world, port, out_path):
+def _pairs_per_column(bx, tiles_x):
+    """(Gaussian, tile) pairs per tile x column of the oracle's boxes (what tile_pairs_per_column reads
+    from the library's boxes on the GPU)."""
+    live = (bx.ub >= bx.lb).all(axis=1)
+    tlo, thi = bx.lb[live] // 4, bx.ub[live] // 4
+    per = (thi[:, 1] - tlo[:, 1] + 1) * (thi[:, 2] - tlo[:, 2] + 1)
+    cols = np.zeros(tiles_x + 1, np.int64)
+    np.add.at(cols, tlo[:, 0], per)
+    np.add.at(cols, thi[:, 0] + 1, -per)
+    return np.cumsum(cols)[:tiles_x].tolist()
+
+
+def _rank_main(rank, world, port, out_path, balanced=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
     try:
         size, rng, m, o, cv, f, bx, dims, gD, gF, dref, fref = _scene()
         tiles_x = (dims[0] + 3) // 4
-        tr = D.slab_tiles(tiles_x, rank, world)
+        if balanced:  # every rank derives the same bounds from the same boxes
+            b = D.balanced_slab_bounds(_pairs_per_column(bx, tiles_x), world)
+            tr = (b[rank], b[rank + 1])
+        else:
+            tr = D.slab_tiles(tiles_x, rank, world)
         xr = D.slab_voxel_rows(dims[0], tr)
         gm, gc, go, gf = oracle.backward(m, o, cv, f, bx.lb, bx.ub, size, rng, dims, gD, gF, dref, fref, x_range=xr)
         tm, tcv, to, tf = D.allreduce_grads(*(torch.from_numpy(np.ascontiguousarray(a)) for a in (gm, gc, go, gf)))
@@ -106,11 +122,17 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gloo_slab_gradients_sum_to_whole_grid(tmp_path, world):
+@pytest.mark.parametrize("world,balanced", [(2, False), (3, False), (3, True)])
+def test_gloo_slab_gradients_sum_to_whole_grid(tmp_path, world, balanced):
     out = str(tmp_path / "grads.npz")
-    mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, balanced), nprocs=world, start_method="spawn",
+                       join=True)
     size, rng, m, o, cv, f, bx, dims, gD, gF, dref, fref = _scene()
+    if balanced:  # the pairs per column sum to the scene's (Gaussian, tile) pairs
+        tiles_x = (dims[0] + 3) // 4
+        live = (bx.ub >= bx.lb).all(axis=1)
+        t = (bx.ub[live] // 4 - bx.lb[live] // 4 + 1).prod(axis=1).sum()
+        assert sum(_pairs_per_column(bx, tiles_x)) == t
     rm, rc, ro, rf = oracle.backward(m, o, cv, f, bx.lb, bx.ub, size, rng, dims, gD, gF, dref, fref)
     with np.load(out) as z:
         for key, ref in (("m", rm), ("c", rc), ("o", ro), ("f", rf)):
