@@ -52,6 +52,26 @@ def test_balanced_slab_bounds_uniform_and_degenerate():
         D.balanced_slab_bounds([1, 2], 3)
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_balanced_slabs_even_out_an_edge_thinned_scene(world):
+    """The purpose of the balanced split: on a scene whose Gaussians thin out towards its x edges (means
+    uniform over the range, so the edge columns see Gaussians from one side only; large variances as in
+    the single-scene config), the busiest balanced slab carries no more pairs than the busiest equal-width
+    slab, and at most one column more than the mean share."""
+    size, rng = [0.4] * 3, [-20.0, -20.0, -1.0, 20.0, 20.0, 5.4]  # 100 x 100 x 16 voxels, 25 tile columns
+    m, _, cv, _ = oracle.generate_inputs(3000, 1, rng, seed=9, var_max=8.0)
+    bx = oracle.boxes(m.numpy(), cv.numpy(), size, rng)
+    tiles_x = (bx.dims[0] + 3) // 4
+    cols = _pairs_per_column(bx, tiles_x)
+    total = sum(cols)
+    eq = [D.slab_tiles(tiles_x, r, world) for r in range(world)]
+    b = D.balanced_slab_bounds(cols, world)
+    eq_max = max(sum(cols[s:e]) for s, e in eq)
+    bal_max = max(sum(cols[s:e]) for s, e in zip(b, b[1:]))
+    assert bal_max <= eq_max
+    assert bal_max <= total / world + max(cols)
+
+
 def test_slab_voxel_rows_clip_the_last_tile():
     assert D.slab_voxel_rows(10, (0, 2)) == (0, 8)
     assert D.slab_voxel_rows(10, (2, 3)) == (8, 10)  # the last tile holds 2 voxel rows
