@@ -61,7 +61,7 @@ struct FMisc {
     uint64_t mma_done;
     uint32_t tmem_base;
     int fail;
-    uint32_t smask[kMaskPasses][4];  // per pass: the steps that meet a slot's box (bit j = step j)
+    uint32_t smask[kMaskPasses][2];  // per pass: the steps that meet a slot's box (bit j = step j)
     uint64_t gfull[kGS];   // TMA bytes of a staged step
     uint64_t gempty[kGS];  // 8 converter-warp arrivals
     alignas(16) GParams prm[kSlots];  // slot records of the pass (each weight thread stages its own)
@@ -69,20 +69,16 @@ struct FMisc {
     alignas(16) float lrd[kMaxBlockTiles * kVoxPerTile];  // log2(1 / max(D, eps)), -inf outside the grid
     int4 org[kMaxBlockTiles];  // voxel origin of each tile of the block, in step order
 };
-// Walks the set bits of a 128-bit step mask in ascending order.
+// Walks the set bits of a step mask (at most 64 steps: 32 tiles x 2 x-slice pairs) in ascending order.
 struct StepList {
-    uint64_t lo, hi;
+    uint64_t bits;
     __device__ __forceinline__ int next() {
-        if (lo) {
-            const int j = __ffsll((long long)lo) - 1;
-            lo &= lo - 1;
-            return j;
-        }
-        const int j = 64 + __ffsll((long long)hi) - 1;
-        hi &= hi - 1;
+        const int j = __ffsll((long long)bits) - 1;
+        bits &= bits - 1;
         return j;
     }
 };
+static_assert(kMaxBlockTiles * 2 <= 64, "a pass's steps fit one 64-bit mask");
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + (size_t)kGS * kGBytes + sizeof(FMisc);
 static_assert(kSmemBytes <= 227 * 1024, "fpass_tc_kernel shared memory");
 static_assert(offsetof(FMisc, lrd) % 16 == 0, "lrd is read as float4");
@@ -144,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             tc::mbar_init(&ms.empty[i], 1);
         }
         tc::mbar_init(&ms.mma_done, 1);
-        for (int i = 0; i < kMaskPasses * 4; ++i) ms.smask[i >> 2][i & 3] = 0u;
+        for (int i = 0; i < kMaskPasses * 2; ++i) ms.smask[i >> 1][i & 1] = 0u;
         for (int i = 0; i < kGS; ++i) {
             tc::mbar_init(&ms.gfull[i], 1);
             tc::mbar_init(&ms.gempty[i], 8);
@@ -167,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         const int nmask = min(Kb, kMaskPasses * kSlots);
         for (int sl0 = 0; sl0 < nmask; sl0 += kThreads) {
             const int sl = sl0 + tid;
-            uint64_t mlo = 0, mhi = 0;
+            uint64_t mlo = 0;  // 2 bits (x-slice pairs) per tile, at most 32 tiles
             if (sl < nmask) {
                 const GParams& gp = gparams[block_lists[s0 + sl]];
                 const float4 d = gp.w[3], e4 = gp.w[4];
@@ -183,14 +179,10 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
             }
             const uint32_t w0 = __reduce_or_sync(0xffffffffu, (uint32_t)mlo);
             const uint32_t w1 = __reduce_or_sync(0xffffffffu, (uint32_t)(mlo >> 32));
-            const uint32_t w2 = __reduce_or_sync(0xffffffffu, (uint32_t)mhi);
-            const uint32_t w3 = __reduce_or_sync(0xffffffffu, (uint32_t)(mhi >> 32));
             if (lane == 0 && sl < nmask) {
                 uint32_t* m = ms.smask[sl / kSlots];
                 if (w0) atomicOr(&m[0], w0);
                 if (w1) atomicOr(&m[1], w1);
-                if (w2) atomicOr(&m[2], w2);
-                if (w3) atomicOr(&m[3], w3);
             }
         }
     }
@@ -225,23 +217,17 @@ __global__ void __launch_bounds__(kThreads, 1) fpass_tc_kernel(
         // the pass's step list, padded to whole rounds of the operand ring with skipped steps (their
         // weights are zero) so that the MMA loop keeps one register set of descriptors per stage
         const int nsteps = ntiles * 2;
-        uint64_t step_lo = nsteps >= 64 ? ~0ull : (1ull << nsteps) - 1;
-        uint64_t step_hi = 0ull;
+        uint64_t step_bits = nsteps >= 64 ? ~0ull : (1ull << nsteps) - 1;
         if (pass < kMaskPasses) {
-            const uint64_t all_lo = step_lo, all_hi = step_hi;
-            step_lo = ((uint64_t)ms.smask[pass][1] << 32) | ms.smask[pass][0];
-            step_hi = ((uint64_t)ms.smask[pass][3] << 32) | ms.smask[pass][2];
-            for (int pad = (kStages - (__popcll(step_lo) + __popcll(step_hi))) & (kStages - 1); pad > 0; --pad) {
-                const uint64_t flo = all_lo & ~step_lo;  // lowest skipped step
-                if (flo) step_lo |= flo & (~flo + 1);
-                else {
-                    const uint64_t fhi = all_hi & ~step_hi;
-                    step_hi |= fhi & (~fhi + 1);
-                }
+            const uint64_t all = step_bits;
+            step_bits = ((uint64_t)ms.smask[pass][1] << 32) | ms.smask[pass][0];
+            if (__popcll(step_bits) & (kStages - 1)) {  // nsteps is even, so a skipped step exists
+                const uint64_t skipped = all & ~step_bits;
+                step_bits |= skipped & (~skipped + 1);  // the lowest one
             }
         }
-        const int nact = __popcll(step_lo) + __popcll(step_hi);
-        StepList steps{step_lo, step_hi};
+        const int nact = __popcll(step_bits);
+        StepList steps{step_bits};
         if (warp < 8) {
             // ---------------- converters: A = gF^T, thread = (8-channel chunk jc, 2 voxel rows) ----------
             const int jc = lane;                                     // channels c0 + 8 jc .. + 7
